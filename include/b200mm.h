@@ -1,0 +1,203 @@
+/*
+ * b200mm.h -- C ABI of the B200 (sm_100a) matmul hot path of the llms Qwen3 engine.
+ *
+ * Every entry point takes device pointers, sizes and row strides (in ELEMENTS),
+ * an opaque cudaStream_t (passed as void*), and returns an int status
+ * (B200MM_OK == 0).  Nothing here allocates or frees device memory: outputs and
+ * workspaces are owned by the caller (PyTorch's caching allocator in the Python
+ * shim).  No entry point synchronises the stream, so every call can be issued
+ * back to back and captured in a CUDA graph.
+ *
+ * Inner (column) strides are 1 for every matrix: the caller makes a tensor
+ * contiguous in its last dimension before the call.  Row strides may be larger
+ * than the row length.  Shapes and dtypes are validated on the host before any
+ * launch; an invalid call returns a status and launches nothing.
+ *
+ * Reference interfaces replaced (paths inside the aaholmes/llms project):
+ *   b200mm_gate_up_silu      <- kernels/fused_ffn.py:98-152  triton_fused_gate_up_silu
+ *                               (launch of _fused_gate_up_silu_kernel, fused_ffn.py:20-95)
+ *   b200mm_qkv               <- kernels/fused_qkv.py:88-149  triton_fused_qkv
+ *                               (launch of _qkv_matmul_kernel, fused_qkv.py:28-85)
+ *   b200mm_gate_up_silu_w8   <- no reference symbol: int8 weight-only variant of
+ *   b200mm_qkv_w8               the two calls above (dequantise W = q * s[row])
+ *   b200mm_mla_kv_scales     <- engine/mla.py:211-221 (the per-token RMS of the
+ *                               reconstructed K head, k_norm over the full head_dim)
+ *   b200mm_mla_decode        <- engine/mla.py:195-264, the T == 1 branch of
+ *                               MLAttention.forward (everything between the
+ *                               q/dkv/kr projections and the o projection)
+ */
+#ifndef B200MM_H_
+#define B200MM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200MM_ABI_VERSION 1
+
+/* status codes */
+enum {
+  B200MM_OK = 0,
+  B200MM_ERR_SHAPE = 1,        /* a size is <= 0, too large, or inconsistent */
+  B200MM_ERR_ALIGN = 2,        /* pointer / stride alignment the kernel needs */
+  B200MM_ERR_DTYPE = 3,        /* unsupported dtype code */
+  B200MM_ERR_LAUNCH = 4,       /* cudaGetLastError() after the launch */
+  B200MM_ERR_ARG = 5,          /* null pointer or bad scalar argument */
+  B200MM_ERR_WORKSPACE = 6,    /* workspace pointer null or too small */
+  B200MM_ERR_DEVICE = 7,       /* device is not sm_100 or a runtime query failed */
+  B200MM_ERR_TIMEOUT = 8       /* a bounded on-device wait gave up */
+};
+
+/* dtype codes for activations / dense weights / outputs */
+enum {
+  B200MM_F32 = 0,
+  B200MM_F16 = 1,
+  B200MM_BF16 = 2
+};
+
+/* Human-readable text for a status code (static storage, never NULL). */
+const char* b200mm_status_string(int status);
+
+/* B200MM_ABI_VERSION of the built library. */
+int b200mm_abi_version(void);
+
+/* Number of device kernels this library has launched since load (all
+ * entry points, all devices).  Host-side counter; used by the bench to
+ * report how many of its own kernels ran in a timed region. */
+uint64_t b200mm_launch_count(void);
+
+/*
+ * Kernel-family override for cross-checking in tests:
+ *   0 = automatic choice (default), 1 = always the generic kernels (the tiled
+ *   CUDA-core projection and the generic MLA split kernel).
+ * Process-wide; returns the previous value.  No reference counterpart.
+ */
+int b200mm_force_generic(int on);
+
+/*
+ * y[m, n] = silu(sum_k x[m,k] * wg[n,k]) * (sum_k x[m,k] * wu[n,k])
+ *
+ *   x  : [M, K]  dtype,  row stride ldx
+ *   wg : [N, K]  dtype,  row stride ldwg   (nn.Linear weight layout (out, in))
+ *   wu : [N, K]  dtype,  row stride ldwu
+ *   y  : [M, N]  dtype,  row stride ldy
+ * fp32 accumulation; silu(g) = g * sigmoid(g) on the fp32 accumulator; one
+ * rounding to dtype on store.  Replaces kernels/fused_ffn.py:98-152.
+ */
+int b200mm_gate_up_silu(const void* x, int64_t ldx,
+                        const void* wg, int64_t ldwg,
+                        const void* wu, int64_t ldwu,
+                        void* y, int64_t ldy,
+                        int64_t M, int64_t N, int64_t K,
+                        int dtype, void* stream);
+
+/*
+ * y[m, n] = sum_k x[m,k] * w[n,k]   with w = [Wq; Wk; Wv] row-stacked
+ *
+ *   x : [M, K], w : [N, K] (N = n_q + 2 n_k), y : [M, N]; all `dtype`.
+ * The caller splits y's columns into q / k / v views.  Replaces
+ * kernels/fused_qkv.py:88-149.
+ */
+int b200mm_qkv(const void* x, int64_t ldx,
+               const void* w, int64_t ldw,
+               void* y, int64_t ldy,
+               int64_t M, int64_t N, int64_t K,
+               int dtype, void* stream);
+
+/*
+ * Int8 weight-only variants (no reference counterpart; new in this build).
+ *   wq : int8 [N, K] row stride ldw, values in [-127, 127]
+ *   s  : fp32 [N]   per-output-channel scale, W[n,k] = wq[n,k] * s[n]
+ *   x, y : `dtype` (F16 or BF16)
+ * y = (x . wq^T) * s, accumulated in fp32; the gate/up variant applies
+ * silu(g * sg) * (u * su).
+ */
+int b200mm_gate_up_silu_w8(const void* x, int64_t ldx,
+                           const int8_t* wg, const float* sg,
+                           const int8_t* wu, const float* su,
+                           int64_t ldw,
+                           void* y, int64_t ldy,
+                           int64_t M, int64_t N, int64_t K,
+                           int dtype, void* stream);
+
+int b200mm_qkv_w8(const void* x, int64_t ldx,
+                  const int8_t* w, const float* s, int64_t ldw,
+                  void* y, int64_t ldy,
+                  int64_t M, int64_t N, int64_t K,
+                  int dtype, void* stream);
+
+/*
+ * MLA latent-cache shapes shared by the two MLA entry points.
+ *   B      batch rows served by this call (rows 0..B-1 of the cache)
+ *   H      query heads, KV key/value groups (H % KV == 0)
+ *   D      head_dim, DR = d_rope (last DR dims of a head carry RoPE),
+ *          DN = D - DR
+ *   R      latent rank
+ * Cache tensors (engine/mla.py:41-87, MLAKVCache):
+ *   c_kv       [*, S, R]       dtype, strides (c_sb, c_st) elements, unit inner
+ *   k_rope_pre [*, S, KV, DR]  dtype, strides (r_sb, r_st), inner [KV, DR] dense
+ *   kscale     [*, S, KV]      fp32,  strides (s_sb, s_st), inner dense
+ * Weights (the nn.Linear weights viewed per group):
+ *   w_uk : [KV, DN, R] dtype dense (uk_nope.weight.view(KV, DN, R))
+ *   w_uv : [KV, D, R]  dtype dense (uv.weight.view(KV, D, R))
+ *   k_norm_w : fp32 [D]  (k_norm.weight)
+ */
+typedef struct b200mm_mla_shape {
+  int32_t B, H, KV, D, DR, R;
+  int32_t dtype;          /* B200MM_BF16 / F16 / F32 for cache, q, weights, out */
+  float eps;              /* k_norm eps */
+} b200mm_mla_shape;
+
+/*
+ * kscale[b, t, g] = rsqrt(mean_d(k[b,t,g,d]^2) + eps) for t in [t0, t1), with
+ * k[b,t,g] = [w_uk[g] . c_kv[b,t] ; k_rope_pre[b,t,g]] (the reconstructed,
+ * un-normed K head of engine/mla.py:212-215).  This is the per-token factor the
+ * k_norm RMSNorm (engine/mla.py:221, engine/attention.py:28-33) multiplies by;
+ * it is written once per token when the token enters the cache, so a decode
+ * step never re-expands K.
+ */
+int b200mm_mla_kv_scales(const b200mm_mla_shape* shape,
+                         const void* c_kv, int64_t c_sb, int64_t c_st,
+                         const void* k_rope_pre, int64_t r_sb, int64_t r_st,
+                         const void* w_uk,
+                         float* kscale, int64_t s_sb, int64_t s_st,
+                         int64_t t0, int64_t t1, void* stream);
+
+/*
+ * Bytes of workspace b200mm_mla_decode needs for (shape, L).  0 on bad shape.
+ */
+size_t b200mm_mla_decode_workspace_size(const b200mm_mla_shape* shape, int64_t L);
+
+/*
+ * One decode step of MLA attention with absorbed up-projections.
+ *   q   : [B, H, D] dtype, batch stride q_sb (q after q_norm, before RoPE)
+ *   L   : context length including the new token; the query sits at
+ *         position L-1 and attends to cache positions 0..L-1
+ *   rope_inv_freq : fp32 [DR/2]; angle(t, i) = float(t) * inv_freq[i]
+ *   scale : softmax scale (head_dim ** -0.5 in the reference SDPA)
+ *   out : [B, H, D] dtype, batch stride o_sb -- equals the SDPA output of
+ *         engine/mla.py:262 transposed to (B, 1, H, D), i.e. the input of
+ *         the o projection.
+ *   workspace : >= b200mm_mla_decode_workspace_size(shape, L) bytes,
+ *         256-byte aligned; contents need not be initialised.
+ */
+int b200mm_mla_decode(const b200mm_mla_shape* shape,
+                      const void* q, int64_t q_sb,
+                      const void* c_kv, int64_t c_sb, int64_t c_st,
+                      const void* k_rope_pre, int64_t r_sb, int64_t r_st,
+                      const float* kscale, int64_t s_sb, int64_t s_st,
+                      const void* w_uk, const void* w_uv,
+                      const float* k_norm_w, const float* rope_inv_freq,
+                      float scale, int64_t L,
+                      void* out, int64_t o_sb,
+                      void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200MM_H_ */

@@ -1,0 +1,125 @@
+"""ctypes binding of ``libb200mm.so`` (declared in ``include/b200mm.h``).
+
+This module is the only place Python touches the C ABI.  It loads the
+in-tree library built by ``llms_b200/csrc/Makefile`` and raises at import
+time if it is missing: there is no Python or CPU fallback for the kernels.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libb200mm.so"
+
+B200MM_OK = 0
+DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+_c_i64 = ctypes.c_int64
+_c_p = ctypes.c_void_p
+
+
+class MlaShape(ctypes.Structure):
+    """Mirror of ``b200mm_mla_shape``."""
+
+    _fields_ = [
+        ("B", ctypes.c_int32),
+        ("H", ctypes.c_int32),
+        ("KV", ctypes.c_int32),
+        ("D", ctypes.c_int32),
+        ("DR", ctypes.c_int32),
+        ("R", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("eps", ctypes.c_float),
+    ]
+
+
+# name -> (restype, argtypes); kept in the order of include/b200mm.h
+SIGNATURES: dict[str, tuple] = {
+    "b200mm_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "b200mm_abi_version": (ctypes.c_int, []),
+    "b200mm_launch_count": (ctypes.c_uint64, []),
+    "b200mm_force_generic": (ctypes.c_int, [ctypes.c_int]),
+    "b200mm_gate_up_silu": (
+        ctypes.c_int,
+        [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int, _c_p],
+    ),
+    "b200mm_qkv": (
+        ctypes.c_int,
+        [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int, _c_p],
+    ),
+    "b200mm_gate_up_silu_w8": (
+        ctypes.c_int,
+        [_c_p, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int, _c_p],
+    ),
+    "b200mm_qkv_w8": (
+        ctypes.c_int,
+        [_c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int, _c_p],
+    ),
+    "b200mm_mla_kv_scales": (
+        ctypes.c_int,
+        [ctypes.POINTER(MlaShape), _c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_p,
+         _c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_p],
+    ),
+    "b200mm_mla_decode_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(MlaShape), _c_i64]),
+    "b200mm_mla_decode": (
+        ctypes.c_int,
+        [ctypes.POINTER(MlaShape), _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64,
+         _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, ctypes.c_float, _c_i64, _c_p, _c_i64,
+         _c_p, ctypes.c_size_t, _c_p],
+    ),
+}
+
+
+def _load() -> ctypes.CDLL:
+    if not LIB_PATH.exists():
+        raise ImportError(
+            f"{LIB_PATH} is not built; run `make -C llms_b200/csrc -j8` or "
+            "`python -c 'import __graft_entry__ as g; g.build()'`"
+        )
+    lib = ctypes.CDLL(os.fspath(LIB_PATH))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+
+
+class KernelError(RuntimeError):
+    """A b200mm entry point returned a non-zero status."""
+
+
+def check(status: int, what: str) -> None:
+    if status != B200MM_OK:
+        msg = lib.b200mm_status_string(status).decode()
+        raise KernelError(f"{what} failed with status {status}: {msg}")
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return DTYPE_CODES[dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {dtype}; expected float32, float16 or bfloat16") from None
+
+
+def stream_of(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def launch_count() -> int:
+    return int(lib.b200mm_launch_count())
+
+
+def require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if t.device.type != "cuda":
+            raise RuntimeError(
+                "b200mm kernels run on CUDA (sm_100a) tensors only; got a tensor on "
+                f"{t.device}. There is no CPU path."
+            )

@@ -1,0 +1,214 @@
+// extern "C" entry points of libb200mm.so: argument validation on the host,
+// then dispatch to the kernel families.  Declarations and the reference
+// interfaces they replace are in include/b200mm.h.
+#include <mutex>
+
+#include "dense.cuh"
+#include "mla.cuh"
+
+namespace b200mm {
+
+std::atomic<uint64_t> g_launches{0};
+std::atomic<int> g_force_generic{0};
+
+namespace {
+constexpr int kMaxDev = 64;
+int g_sms[kMaxDev] = {0};
+int g_cc_ok[kMaxDev] = {0};  // 0 unknown, 1 sm_100, -1 other
+}  // namespace
+
+int current_device() {
+  int d = -1;
+  if (cudaGetDevice(&d) != cudaSuccess) return -1;
+  return d;
+}
+
+int num_sms(int device) {
+  if (device < 0 || device >= kMaxDev) return 148;
+  if (g_sms[device] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || v <= 0) v = 148;
+    g_sms[device] = v;
+  }
+  return g_sms[device];
+}
+
+// The kernels are compiled for sm_100a only; refuse other devices up front
+// instead of failing with "no kernel image" at launch.
+int check_device() {
+  const int d = current_device();
+  if (d < 0 || d >= kMaxDev) return B200MM_ERR_DEVICE;
+  if (g_cc_ok[d] == 0) {
+    int major = 0, minor = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, d) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, d) != cudaSuccess)
+      return B200MM_ERR_DEVICE;
+    g_cc_ok[d] = (major == 10 && minor == 0) ? 1 : -1;
+  }
+  return g_cc_ok[d] == 1 ? B200MM_OK : B200MM_ERR_DEVICE;
+}
+
+int dense_dispatch(const DenseArgs& a) {
+  if (g_force_generic.load(std::memory_order_relaxed)) return tiled_launch(a);
+  if (tc_supported(a)) return tc_launch(a);
+  if (gemv_supported(a)) return gemv_launch(a);
+  return tiled_launch(a);
+}
+
+namespace {
+
+int validate_dense(const DenseArgs& a) {
+  if (!a.x || !a.w0 || !a.y || (a.gate && !a.w1)) return B200MM_ERR_ARG;
+  if (a.w8 && (!a.s0 || (a.gate && !a.s1))) return B200MM_ERR_ARG;
+  if (a.dtype != B200MM_F32 && a.dtype != B200MM_F16 && a.dtype != B200MM_BF16) return B200MM_ERR_DTYPE;
+  if (a.w8 && a.dtype == B200MM_F32) return B200MM_ERR_DTYPE;
+  if (a.M < 0 || a.N < 1 || a.K < 1) return B200MM_ERR_SHAPE;
+  if (a.ldx < a.K || a.ldw0 < a.K || (a.gate && a.ldw1 < a.K) || a.ldy < a.N) return B200MM_ERR_SHAPE;
+  return B200MM_OK;
+}
+
+bool fits_i32(int64_t v) { return v >= 0 && v < (int64_t(1) << 31); }
+
+int run_dense(DenseArgs& a, int64_t M, int64_t N, int64_t K) {
+  if (!fits_i32(M) || !fits_i32(N) || !fits_i32(K)) return B200MM_ERR_SHAPE;
+  a.M = (int)M; a.N = (int)N; a.K = (int)K;
+  int st = validate_dense(a);
+  if (st != B200MM_OK) return st;
+  if (a.M == 0) return B200MM_OK;
+  st = check_device();
+  if (st != B200MM_OK) return st;
+  st = dense_dispatch(a);
+  if (st != B200MM_OK) return st;
+  return launch_status();
+}
+
+}  // namespace
+}  // namespace b200mm
+
+using namespace b200mm;
+
+extern "C" {
+
+const char* b200mm_status_string(int s) {
+  switch (s) {
+    case B200MM_OK: return "ok";
+    case B200MM_ERR_SHAPE: return "invalid or unsupported shape";
+    case B200MM_ERR_ALIGN: return "pointer or stride alignment not supported";
+    case B200MM_ERR_DTYPE: return "unsupported dtype";
+    case B200MM_ERR_LAUNCH: return "kernel launch failed";
+    case B200MM_ERR_ARG: return "null pointer or invalid argument";
+    case B200MM_ERR_WORKSPACE: return "workspace missing or too small";
+    case B200MM_ERR_DEVICE: return "device is not an sm_100 GPU or a device query failed";
+    case B200MM_ERR_TIMEOUT: return "an on-device wait timed out";
+    default: return "unknown status";
+  }
+}
+
+int b200mm_abi_version(void) { return B200MM_ABI_VERSION; }
+
+uint64_t b200mm_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int b200mm_force_generic(int on) { return g_force_generic.exchange(on ? 1 : 0); }
+
+int b200mm_gate_up_silu(const void* x, int64_t ldx, const void* wg, int64_t ldwg, const void* wu,
+                        int64_t ldwu, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
+                        int dtype, void* stream) {
+  DenseArgs a{};
+  a.x = x; a.ldx = ldx; a.w0 = wg; a.ldw0 = ldwg; a.w1 = wu; a.ldw1 = ldwu;
+  a.y = y; a.ldy = ldy; a.dtype = dtype; a.w8 = false; a.gate = true;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return run_dense(a, M, N, K);
+}
+
+int b200mm_qkv(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy,
+               int64_t M, int64_t N, int64_t K, int dtype, void* stream) {
+  DenseArgs a{};
+  a.x = x; a.ldx = ldx; a.w0 = w; a.ldw0 = ldw; a.y = y; a.ldy = ldy;
+  a.dtype = dtype; a.w8 = false; a.gate = false;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return run_dense(a, M, N, K);
+}
+
+int b200mm_gate_up_silu_w8(const void* x, int64_t ldx, const int8_t* wg, const float* sg,
+                           const int8_t* wu, const float* su, int64_t ldw, void* y, int64_t ldy,
+                           int64_t M, int64_t N, int64_t K, int dtype, void* stream) {
+  DenseArgs a{};
+  a.x = x; a.ldx = ldx; a.w0 = wg; a.ldw0 = ldw; a.w1 = wu; a.ldw1 = ldw;
+  a.s0 = sg; a.s1 = su; a.y = y; a.ldy = ldy; a.dtype = dtype; a.w8 = true; a.gate = true;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return run_dense(a, M, N, K);
+}
+
+int b200mm_qkv_w8(const void* x, int64_t ldx, const int8_t* w, const float* s, int64_t ldw,
+                  void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int dtype, void* stream) {
+  DenseArgs a{};
+  a.x = x; a.ldx = ldx; a.w0 = w; a.ldw0 = ldw; a.s0 = s; a.y = y; a.ldy = ldy;
+  a.dtype = dtype; a.w8 = true; a.gate = false;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return run_dense(a, M, N, K);
+}
+
+int b200mm_mla_kv_scales(const b200mm_mla_shape* shape, const void* c_kv, int64_t c_sb, int64_t c_st,
+                         const void* k_rope_pre, int64_t r_sb, int64_t r_st, const void* w_uk,
+                         float* kscale, int64_t s_sb, int64_t s_st, int64_t t0, int64_t t1,
+                         void* stream) {
+  if (!shape) return B200MM_ERR_ARG;
+  MlaScalesArgs a{};
+  a.s = *shape;
+  a.c_kv = c_kv; a.c_sb = c_sb; a.c_st = c_st;
+  a.kr = k_rope_pre; a.r_sb = r_sb; a.r_st = r_st;
+  a.w_uk = w_uk; a.kscale = kscale; a.s_sb = s_sb; a.s_st = s_st;
+  a.t0 = t0; a.t1 = t1; a.stream = static_cast<cudaStream_t>(stream);
+  int st = mla_validate_shape(a.s);
+  if (st != B200MM_OK) return st;
+  if (!c_kv || !kscale || (a.s.DR > 0 && !k_rope_pre) || (a.s.D - a.s.DR > 0 && !w_uk)) return B200MM_ERR_ARG;
+  if (t0 < 0 || t1 < t0 || t1 >= (int64_t(1) << 31)) return B200MM_ERR_SHAPE;
+  if (t1 == t0 || a.s.B == 0) return B200MM_OK;
+  st = check_device();
+  if (st != B200MM_OK) return st;
+  st = mla_scales_launch(a);
+  if (st != B200MM_OK) return st;
+  return launch_status();
+}
+
+size_t b200mm_mla_decode_workspace_size(const b200mm_mla_shape* shape, int64_t L) {
+  if (!shape || mla_validate_shape(*shape) != B200MM_OK || L < 1) return 0;
+  return mla_workspace_bytes(*shape, L);
+}
+
+int b200mm_mla_decode(const b200mm_mla_shape* shape, const void* q, int64_t q_sb, const void* c_kv,
+                      int64_t c_sb, int64_t c_st, const void* k_rope_pre, int64_t r_sb, int64_t r_st,
+                      const float* kscale, int64_t s_sb, int64_t s_st, const void* w_uk,
+                      const void* w_uv, const float* k_norm_w, const float* rope_inv_freq,
+                      float scale, int64_t L, void* out, int64_t o_sb, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+  if (!shape) return B200MM_ERR_ARG;
+  MlaDecodeArgs a{};
+  a.s = *shape;
+  a.q = q; a.q_sb = q_sb;
+  a.c_kv = c_kv; a.c_sb = c_sb; a.c_st = c_st;
+  a.kr = k_rope_pre; a.r_sb = r_sb; a.r_st = r_st;
+  a.kscale = kscale; a.s_sb = s_sb; a.s_st = s_st;
+  a.w_uk = w_uk; a.w_uv = w_uv; a.k_norm_w = k_norm_w; a.inv_freq = rope_inv_freq;
+  a.scale = scale; a.L = L; a.out = out; a.o_sb = o_sb;
+  a.ws = workspace; a.ws_bytes = workspace_bytes;
+  a.stream = static_cast<cudaStream_t>(stream);
+  int st = mla_validate_shape(a.s);
+  if (st != B200MM_OK) return st;
+  if (L < 1 || L >= (int64_t(1) << 31)) return B200MM_ERR_SHAPE;
+  if (!q || !c_kv || !kscale || !w_uv || !k_norm_w || !out) return B200MM_ERR_ARG;
+  if (a.s.DR > 0 && (!k_rope_pre || !rope_inv_freq)) return B200MM_ERR_ARG;
+  if (a.s.D - a.s.DR > 0 && !w_uk) return B200MM_ERR_ARG;
+  if (!(scale > 0.f)) return B200MM_ERR_ARG;
+  if (a.s.B == 0) return B200MM_OK;
+  const size_t need = mla_workspace_bytes(a.s, L);
+  if (need > 0 && (!workspace || workspace_bytes < need || ((uintptr_t)workspace & 255u)))
+    return B200MM_ERR_WORKSPACE;
+  st = check_device();
+  if (st != B200MM_OK) return st;
+  st = mla_decode_launch(a);
+  if (st != B200MM_OK) return st;
+  return launch_status();
+}
+
+}  // extern "C"

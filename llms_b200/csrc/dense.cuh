@@ -1,0 +1,34 @@
+// Dense projection kernels (fused QKV, fused gate-up-SiLU, int8 weight-only):
+// parameter block and dispatch entry shared by the kernel files.
+#pragma once
+#include "common.cuh"
+
+namespace b200mm {
+
+// One call of the projection family.  y[m, n] = epilogue(x[m,:] . w[n,:]).
+//   gate == false : y = acc0 * s0[n]                 (QKV; s0 == nullptr -> 1)
+//   gate == true  : y = silu(acc_g * sg[n]) * acc_u * su[n]
+struct DenseArgs {
+  const void* x; int64_t ldx;       // [M, K] activation dtype
+  const void* w0; int64_t ldw0;     // [N, K] (gate or stacked qkv)
+  const void* w1; int64_t ldw1;     // [N, K] up weights (gate mode only)
+  const float* s0; const float* s1; // per-row scales (int8 weights only)
+  void* y; int64_t ldy;             // [M, N] activation dtype
+  int M, N, K;
+  int dtype;                        // B200MM_F32 / F16 / BF16 (x, y, dense w)
+  bool w8;                          // weights are int8
+  bool gate;                        // gate-up-SiLU epilogue
+  cudaStream_t stream;
+};
+
+int dense_dispatch(const DenseArgs& a);
+
+// Kernel families (each returns B200MM_OK, or a status if it declines / fails).
+// `*_supported` answers whether the family can serve the call, with no launch.
+bool gemv_supported(const DenseArgs& a);
+int gemv_launch(const DenseArgs& a);
+int tiled_launch(const DenseArgs& a);
+bool tc_supported(const DenseArgs& a);
+int tc_launch(const DenseArgs& a);
+
+}  // namespace b200mm

@@ -1,0 +1,247 @@
+// Small-M (decode) projection kernel: weight-streaming GEMV for M <= 8.
+//
+// The weight matrix is the only large operand (31.5 MB for the Qwen3-4B QKV
+// projection, 99.6 MB for gate+up), so the kernel is an HBM stream:
+//   * every warp owns a "unit" of two weight rows (gate row n + up row n for
+//     the gate-up epilogue, rows 2u and 2u+1 for QKV) and reads both rows end
+//     to end with 16-byte, L1-bypassing loads -- NCH loads per lane per row in
+//     flight before the first FMA;
+//   * the activation rows x[0..M) are staged once per CTA in shared memory in
+//     their own dtype, so one 16-byte shared load feeds both weight rows;
+//   * fp32 accumulation, warp-shuffle reduction, and the SiLU*up / int8 scale
+//     epilogue in registers: the [M, 2N] gate/up intermediate never exists;
+//   * launched with programmatic dependent launch: a warp issues the loads of
+//     its first unit's weights before `griddepcontrol.wait`, so weight
+//     streaming overlaps the tail of the kernel that produced x.
+// Grid: (SM count) x (resident CTAs per SM), grid-stride over units.
+#include "dense.cuh"
+
+namespace b200mm {
+
+namespace {
+
+constexpr int kThreads = 256;
+
+struct GemvParams {
+  const void* x; int64_t ldx;
+  const void* w0; int64_t ldw0;
+  const void* w1; int64_t ldw1;
+  const float* s0; const float* s1;
+  void* y; int64_t ldy;
+  int M, N, K;
+};
+
+template <typename TX, typename TW, int MR, bool GATE, int NCH>
+__global__ void __launch_bounds__(kThreads)
+gemv_kernel(const GemvParams p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  TX* xs = reinterpret_cast<TX*>(smem_raw);  // [MR][K] activation rows
+
+  constexpr int WV = Chunk<TW>::kElems;      // weights per 16-byte chunk
+  constexpr int XV = Chunk<TX>::kElems;      // activations per 16-byte chunk
+  static_assert(WV % XV == 0, "weight chunk must cover whole activation chunks");
+  constexpr int XPW = WV / XV;               // activation chunks per weight chunk
+
+  const int lane = threadIdx.x & 31;
+  const int warps_per_cta = blockDim.x >> 5;
+  const int gwarp = blockIdx.x * warps_per_cta + (threadIdx.x >> 5);
+  const int nwarps = gridDim.x * warps_per_cta;
+  const int N = p.N, K = p.K, M = p.M;
+  const int nunits = GATE ? N : (N + 1) >> 1;
+  const int nchunks = K / WV;
+  constexpr int kSeg = 32 * NCH;
+  const int nseg = (nchunks + kSeg - 1) / kSeg;
+
+  const TW* w0 = static_cast<const TW*>(p.w0);
+  const TW* w1 = static_cast<const TW*>(p.w1);
+
+  auto row_ptrs = [&](int u, const TW*& r0, const TW*& r1, bool& v1) {
+    if (GATE) {
+      r0 = w0 + (int64_t)u * p.ldw0;
+      r1 = w1 + (int64_t)u * p.ldw1;
+      v1 = true;
+    } else {
+      const int n0 = 2 * u;
+      r0 = w0 + (int64_t)n0 * p.ldw0;
+      v1 = (n0 + 1) < N;
+      r1 = w0 + (int64_t)(v1 ? n0 + 1 : n0) * p.ldw0;
+    }
+  };
+
+  uint4 wv[2][NCH];
+  auto load_seg = [&](int u, int seg) {
+    const TW* r0; const TW* r1; bool v1;
+    row_ptrs(u, r0, r1, v1);
+#pragma unroll
+    for (int i = 0; i < NCH; ++i) {
+      const int c = seg * kSeg + i * 32 + lane;
+      if (c < nchunks) {
+        wv[0][i] = ld_stream16(r0 + (int64_t)c * WV);
+        wv[1][i] = v1 ? ld_stream16(r1 + (int64_t)c * WV) : make_uint4(0, 0, 0, 0);
+      } else {
+        wv[0][i] = make_uint4(0, 0, 0, 0);
+        wv[1][i] = make_uint4(0, 0, 0, 0);
+      }
+    }
+  };
+
+  // Weights are never written by another kernel: start streaming them now.
+  int u = gwarp;
+  if (u < nunits) load_seg(u, 0);
+  pdl_trigger();
+  pdl_wait();
+
+  // Stage x[0..M) (zero rows M..MR) in shared memory, 16 bytes at a time.
+  {
+    const TX* x = static_cast<const TX*>(p.x);
+    const int kc = K / XV;  // 16-byte chunks per row
+    for (int i = threadIdx.x; i < MR * kc; i += blockDim.x) {
+      const int m = i / kc, c = i - m * kc;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (m < M) v = *reinterpret_cast<const uint4*>(x + (int64_t)m * p.ldx + (int64_t)c * XV);
+      *reinterpret_cast<uint4*>(xs + (int64_t)m * K + (int64_t)c * XV) = v;
+    }
+  }
+  __syncthreads();
+
+  bool preloaded = true;
+  for (; u < nunits; u += nwarps) {
+    float acc[2][MR];
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+      for (int m = 0; m < MR; ++m) acc[r][m] = 0.f;
+
+    for (int seg = 0; seg < nseg; ++seg) {
+      if (!preloaded) load_seg(u, seg);
+      preloaded = false;
+#pragma unroll
+      for (int i = 0; i < NCH; ++i) {
+        const int c = seg * kSeg + i * 32 + lane;
+        if (c < nchunks) {
+          float f0[WV], f1[WV];
+          Chunk<TW>::unpack(wv[0][i], f0);
+          Chunk<TW>::unpack(wv[1][i], f1);
+#pragma unroll
+          for (int m = 0; m < MR; ++m) {
+            const TX* xp = xs + (int64_t)m * K + (int64_t)c * WV;
+#pragma unroll
+            for (int h = 0; h < XPW; ++h) {
+              float xf[XV];
+              Chunk<TX>::unpack(*reinterpret_cast<const uint4*>(xp + h * XV), xf);
+#pragma unroll
+              for (int e = 0; e < XV; ++e) {
+                acc[0][m] = fmaf(f0[h * XV + e], xf[e], acc[0][m]);
+                acc[1][m] = fmaf(f1[h * XV + e], xf[e], acc[1][m]);
+              }
+            }
+          }
+        }
+      }
+    }
+
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+      for (int m = 0; m < MR; ++m) acc[r][m] = warp_sum(acc[r][m]);
+
+    // lanes 0..MR-1 store row m = lane (values are uniform across the warp)
+    if (lane < MR && lane < M) {
+      float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+      for (int m = 0; m < MR; ++m)
+        if (m == lane) { a0 = acc[0][m]; a1 = acc[1][m]; }
+      TX* y = static_cast<TX*>(p.y) + (int64_t)lane * p.ldy;
+      if (GATE) {
+        if (p.s0) { a0 *= p.s0[u]; a1 *= p.s1[u]; }
+        y[u] = from_f<TX>(silu_mul(a0, a1));
+      } else {
+        const int n0 = 2 * u;
+        if (p.s0) a0 *= p.s0[n0];
+        y[n0] = from_f<TX>(a0);
+        if (n0 + 1 < N) {
+          if (p.s0) a1 *= p.s0[n0 + 1];
+          y[n0 + 1] = from_f<TX>(a1);
+        }
+      }
+    }
+  }
+}
+
+template <typename TX, typename TW, int MR, bool GATE>
+int launch_one(const DenseArgs& a) {
+  constexpr int NCH = (sizeof(TW) == 2) ? 10 : 8;
+  auto kern = gemv_kernel<TX, TW, MR, GATE, NCH>;
+  const size_t smem = (size_t)MR * a.K * sizeof(TX);
+  static int configured_smem[64] = {0};  // per device: largest opt-in set so far
+  static int blocks_per_sm[64][8] = {{0}};
+  int dev = current_device();
+  if (dev < 0 || dev >= 64) return B200MM_ERR_DEVICE;
+  if (smem > 48 * 1024 && (int)smem > configured_smem[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return B200MM_ERR_LAUNCH;
+    configured_smem[dev] = (int)smem;
+  }
+  // occupancy depends on smem; cache per (device, smem bucket of 32 KB)
+  const int bucket = (int)(smem >> 15) < 8 ? (int)(smem >> 15) : 7;
+  int& bps = blocks_per_sm[dev][bucket];
+  if (bps == 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, kern, kThreads, smem) != cudaSuccess || bps < 1)
+      bps = 1;
+  }
+  const int nunits = a.gate ? a.N : (a.N + 1) / 2;
+  const int warps_per_cta = kThreads / 32;
+  int grid = num_sms(dev) * bps;
+  const int need = (nunits + warps_per_cta - 1) / warps_per_cta;
+  if (grid > need) grid = need;
+  if (grid < 1) grid = 1;
+  GemvParams p{a.x, a.ldx, a.w0, a.ldw0, a.w1, a.ldw1, a.s0, a.s1, a.y, a.ldy, a.M, a.N, a.K};
+  cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, a.stream, p);
+  return e == cudaSuccess ? B200MM_OK : B200MM_ERR_LAUNCH;
+}
+
+template <typename TX, typename TW, bool GATE>
+int launch_mr(const DenseArgs& a) {
+  if (a.M <= 1) return launch_one<TX, TW, 1, GATE>(a);
+  if (a.M <= 2) return launch_one<TX, TW, 2, GATE>(a);
+  if (a.M <= 4) return launch_one<TX, TW, 4, GATE>(a);
+  return launch_one<TX, TW, 8, GATE>(a);
+}
+
+template <typename TX, typename TW>
+int launch_gate(const DenseArgs& a) {
+  return a.gate ? launch_mr<TX, TW, true>(a) : launch_mr<TX, TW, false>(a);
+}
+
+inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+}  // namespace
+
+bool gemv_supported(const DenseArgs& a) {
+  if (a.M < 1 || a.M > 8) return false;
+  const int xsz = a.dtype == B200MM_F32 ? 4 : 2;
+  const int wsz = a.w8 ? 1 : xsz;
+  const int wv = 16 / wsz;
+  if (a.K % wv != 0) return false;
+  if ((a.K * xsz) % 16 != 0) return false;
+  if (!aligned16(a.x) || (a.ldx * xsz) % 16 != 0) return false;
+  if (!aligned16(a.w0) || (a.ldw0 * wsz) % 16 != 0) return false;
+  if (a.gate && (!aligned16(a.w1) || (a.ldw1 * wsz) % 16 != 0)) return false;
+  const int mr = a.M <= 1 ? 1 : a.M <= 2 ? 2 : a.M <= 4 ? 4 : 8;
+  if ((size_t)mr * a.K * xsz > 200 * 1024) return false;
+  return true;
+}
+
+int gemv_launch(const DenseArgs& a) {
+  if (a.w8) {
+    if (a.dtype == B200MM_BF16) return launch_gate<__nv_bfloat16, int8_t>(a);
+    if (a.dtype == B200MM_F16) return launch_gate<__half, int8_t>(a);
+    return B200MM_ERR_DTYPE;
+  }
+  if (a.dtype == B200MM_BF16) return launch_gate<__nv_bfloat16, __nv_bfloat16>(a);
+  if (a.dtype == B200MM_F16) return launch_gate<__half, __half>(a);
+  if (a.dtype == B200MM_F32) return launch_gate<float, float>(a);
+  return B200MM_ERR_DTYPE;
+}
+
+}  // namespace b200mm

@@ -1,0 +1,367 @@
+// MLA latent-KV decode with absorbed up-projections (any shape).
+//
+// The reference decode step (engine/mla.py:195-264) rebuilds K and V for all
+// L cached tokens every step: V = W_uv c_t, K = k_norm([W_uk c_t ; kr_t]),
+// partial RoPE on the last DR dims, GQA expansion, SDPA.  Here the step reads
+// each cached token once, in latent form:
+//
+//   s_t,g     = rsqrt(mean_d k_t,g[d]^2 + eps)        (side-band, written at append)
+//   qt_h      = W_uk,g^T (w_k[:DN] * q_h[:DN])         (absorbed query, per step)
+//   qr_h      = rope_{L-1}(q_h[DN:])
+//   score_t,h = scale * s_t,g * (qt_h . c_t + qr_h . rope_t(w_k[DN:] * kr_t,g))
+//   out_h     = W_uv,g (sum_t softmax(score)_t,h c_t)
+//
+// which equals the reference because k_norm multiplies the raw head by the
+// scalar s_t,g and then by w_k elementwise, and RoPE is linear.  The context
+// is split into S chunks per batch row (flash-decoding); each split writes a
+// partial (max, sum, sum p c) and a combine kernel merges the splits and
+// applies W_uv once per head.
+#include "mla.cuh"
+
+namespace b200mm {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kTileT = 16;  // tokens per tile in the generic split kernel
+
+inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+template <typename T>
+__device__ __forceinline__ float ldf(const T* p, int64_t i) { return to_f<T>(p[i]); }
+
+// --- per-token k RMS side-band --------------------------------------------
+// grid: (ceil((t1-t0)/8), B); block 256.  Each CTA handles 8 tokens of one
+// batch row; warps walk the KV*DN rows of W_uk, lanes split the rank.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) mla_scales_kernel(const MlaScalesArgs a) {
+  extern __shared__ float sm[];
+  const int R = a.s.R, KV = a.s.KV, D = a.s.D, DR = a.s.DR, DN = D - DR;
+  constexpr int TT = 8;
+  float* cs = sm;                 // [TT][R]
+  float* ssq = sm + TT * R;       // [TT][KV]
+  const int b = blockIdx.y;
+  const int64_t tb = a.t0 + (int64_t)blockIdx.x * TT;
+  const int nt = (int)imin64(TT, a.t1 - tb);
+  const T* c = static_cast<const T*>(a.c_kv) + (int64_t)b * a.c_sb;
+  const T* kr = static_cast<const T*>(a.kr);
+  const T* wuk = static_cast<const T*>(a.w_uk);
+
+  pdl_trigger();
+  pdl_wait();
+  for (int i = threadIdx.x; i < TT * R; i += blockDim.x) {
+    const int t = i / R, r = i % R;
+    cs[i] = t < nt ? ldf(c, (tb + t) * a.c_st + r) : 0.f;
+  }
+  // rope-half contribution: sum of squares of kr
+  for (int i = threadIdx.x; i < TT * KV; i += blockDim.x) {
+    const int t = i / KV, g = i % KV;
+    float acc = 0.f;
+    if (t < nt && DR > 0) {
+      const T* p = kr + (int64_t)b * a.r_sb + (tb + t) * a.r_st + (int64_t)g * DR;
+      for (int d = 0; d < DR; ++d) { const float v = ldf(p, d); acc = fmaf(v, v, acc); }
+    }
+    ssq[i] = acc;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int row = warp; row < KV * DN; row += nw) {
+    const int g = row / DN;
+    const T* wr = wuk + (int64_t)row * R;
+    float acc[TT];
+#pragma unroll
+    for (int t = 0; t < TT; ++t) acc[t] = 0.f;
+    for (int r = lane; r < R; r += 32) {
+      const float w = ldf(wr, r);
+#pragma unroll
+      for (int t = 0; t < TT; ++t) acc[t] = fmaf(w, cs[t * R + r], acc[t]);
+    }
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+      const float v = warp_sum(acc[t]);
+      if (lane == 0) atomicAdd(&ssq[t * KV + g], v * v);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < nt * KV; i += blockDim.x) {
+    const int t = i / KV, g = i % KV;
+    a.kscale[(int64_t)b * a.s_sb + (tb + t) * a.s_st + g] = rsqrtf(ssq[i] / (float)D + a.s.eps);
+  }
+}
+
+// --- absorbed query --------------------------------------------------------
+// grid: (H, B); block 256.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) mla_absorb_kernel(const MlaDecodeArgs a, MlaWorkspace w) {
+  extern __shared__ float sm[];
+  const int H = a.s.H, KV = a.s.KV, D = a.s.D, DR = a.s.DR, DN = D - DR, R = a.s.R;
+  const int h = blockIdx.x, b = blockIdx.y, g = h / (H / KV);
+  float* qn = sm;  // [D]
+  const T* q = static_cast<const T*>(a.q) + (int64_t)b * a.q_sb + (int64_t)h * D;
+  float* ws = static_cast<float*>(a.ws);
+  float* qt = ws + w.off_qt / 4 + ((int64_t)b * H + h) * R;
+  float* qr = ws + w.off_qr / 4 + ((int64_t)b * H + h) * DR;
+
+  pdl_trigger();
+  pdl_wait();
+  for (int d = threadIdx.x; d < D; d += blockDim.x) qn[d] = ldf(q, d);
+  __syncthreads();
+  // qt[r] = sum_i W_uk[g, i, r] * w_k[i] * q[i]
+  const T* wuk = static_cast<const T*>(a.w_uk) + (int64_t)g * DN * R;
+  for (int r = threadIdx.x; r < R; r += blockDim.x) {
+    float acc = 0.f;
+    for (int i = 0; i < DN; ++i) acc = fmaf(ldf(wuk, (int64_t)i * R + r), a.k_norm_w[i] * qn[i], acc);
+    qt[r] = acc;
+  }
+  // qr = rope at position L-1 (rotate-half convention, angle = pos * inv_freq)
+  const int half = DR / 2;
+  const float pos = (float)(a.L - 1);
+  for (int j = threadIdx.x; j < DR; j += blockDim.x) {
+    const int i = j < half ? j : j - half;
+    float sn, cs;
+    sincosf(pos * a.inv_freq[i], &sn, &cs);
+    const float x = qn[DN + j];
+    const float rot = j < half ? -qn[DN + j + half] : qn[DN + j - half];
+    qr[j] = x * cs + rot * sn;
+  }
+}
+
+// --- generic split kernel ---------------------------------------------------
+// grid: (S, B); block 256.  Shared: qt[H][R], qr[H][DR], acc[H][R], c[TT][R],
+// z[TT][KV][DR], sc[H][TT], st[TT][KV], m[H], l[H], alpha[H].
+template <typename T>
+__global__ void __launch_bounds__(kThreads) mla_split_kernel(const MlaDecodeArgs a, MlaWorkspace w) {
+  extern __shared__ float sm[];
+  const int H = a.s.H, KV = a.s.KV, D = a.s.D, DR = a.s.DR, DN = D - DR, R = a.s.R;
+  const int hpg = H / KV, half = DR / 2;
+  const int sidx = blockIdx.x, b = blockIdx.y;
+  float* qt = sm;
+  float* qr = qt + H * R;
+  float* acc = qr + H * DR;
+  float* cs = acc + H * R;
+  float* z = cs + kTileT * R;
+  float* sc = z + kTileT * KV * DR;
+  float* st = sc + H * kTileT;
+  float* mrun = st + kTileT * KV;
+  float* lrun = mrun + H;
+  float* alpha = lrun + H;
+
+  const float* ws = static_cast<const float*>(a.ws);
+  const int64_t t_begin = (int64_t)sidx * w.chunk;
+  const int64_t t_end = imin64(a.L, t_begin + w.chunk);
+  const T* c = static_cast<const T*>(a.c_kv) + (int64_t)b * a.c_sb;
+  const T* kr = static_cast<const T*>(a.kr) + (int64_t)b * a.r_sb;
+  const float* ks = a.kscale + (int64_t)b * a.s_sb;
+
+  pdl_trigger();
+  pdl_wait();
+  for (int i = threadIdx.x; i < H * R; i += blockDim.x) {
+    qt[i] = ws[w.off_qt / 4 + (int64_t)b * H * R + i];
+    acc[i] = 0.f;
+  }
+  for (int i = threadIdx.x; i < H * DR; i += blockDim.x) qr[i] = ws[w.off_qr / 4 + (int64_t)b * H * DR + i];
+  for (int i = threadIdx.x; i < H; i += blockDim.x) { mrun[i] = -INFINITY; lrun[i] = 0.f; }
+  __syncthreads();
+
+  for (int64_t t0 = t_begin; t0 < t_end; t0 += kTileT) {
+    const int nt = (int)imin64(kTileT, t_end - t0);
+    for (int i = threadIdx.x; i < kTileT * R; i += blockDim.x) {
+      const int t = i / R, r = i % R;
+      cs[i] = t < nt ? ldf(c, (t0 + t) * a.c_st + r) : 0.f;
+    }
+    for (int i = threadIdx.x; i < kTileT * KV * DR; i += blockDim.x) {
+      const int t = i / (KV * DR), rem = i % (KV * DR), g = rem / DR, j = rem % DR;
+      float v = 0.f;
+      if (t < nt) {
+        const T* p = kr + (t0 + t) * a.r_st + (int64_t)g * DR;
+        const int ii = j < half ? j : j - half;
+        float sn, cn;
+        sincosf((float)(t0 + t) * a.inv_freq[ii], &sn, &cn);
+        const float x = a.k_norm_w[DN + j] * ldf(p, j);
+        const float rot = j < half ? -a.k_norm_w[DN + j + half] * ldf(p, j + half)
+                                   : a.k_norm_w[DN + j - half] * ldf(p, j - half);
+        v = x * cn + rot * sn;
+      }
+      z[i] = v;
+    }
+    for (int i = threadIdx.x; i < kTileT * KV; i += blockDim.x) {
+      const int t = i / KV, g = i % KV;
+      st[i] = t < nt ? ks[(t0 + t) * a.s_st + g] : 0.f;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < H * kTileT; i += blockDim.x) {
+      const int h = i / kTileT, t = i % kTileT, g = h / hpg;
+      float v = -INFINITY;
+      if (t < nt) {
+        float d0 = 0.f;
+        for (int r = 0; r < R; ++r) d0 = fmaf(qt[h * R + r], cs[t * R + r], d0);
+        for (int j = 0; j < DR; ++j) d0 = fmaf(qr[h * DR + j], z[(t * KV + g) * DR + j], d0);
+        v = d0 * st[t * KV + g] * a.scale;
+      }
+      sc[i] = v;
+    }
+    __syncthreads();
+    for (int h = threadIdx.x; h < H; h += blockDim.x) {
+      float mx = mrun[h];
+      for (int t = 0; t < nt; ++t) mx = fmaxf(mx, sc[h * kTileT + t]);
+      const float al = expf(mrun[h] - mx);
+      float sum = 0.f;
+      for (int t = 0; t < kTileT; ++t) {
+        const float p = t < nt ? expf(sc[h * kTileT + t] - mx) : 0.f;
+        sc[h * kTileT + t] = p;
+        sum += p;
+      }
+      lrun[h] = lrun[h] * al + sum;
+      mrun[h] = mx;
+      alpha[h] = al;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < H * R; i += blockDim.x) {
+      const int h = i / R, r = i % R;
+      float v = acc[i] * alpha[h];
+      for (int t = 0; t < nt; ++t) v = fmaf(sc[h * kTileT + t], cs[t * R + r], v);
+      acc[i] = v;
+    }
+    __syncthreads();
+  }
+  float* pacc = const_cast<float*>(ws) + w.off_pacc / 4 + (((int64_t)b * w.S + sidx) * H) * R;
+  float* pml = const_cast<float*>(ws) + w.off_pml / 4 + (((int64_t)b * w.S + sidx) * H) * 2;
+  for (int i = threadIdx.x; i < H * R; i += blockDim.x) pacc[i] = acc[i];
+  for (int h = threadIdx.x; h < H; h += blockDim.x) { pml[2 * h] = mrun[h]; pml[2 * h + 1] = lrun[h]; }
+}
+
+// --- combine: merge splits, apply W_uv -------------------------------------
+// grid: (H, B); block 256.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) mla_combine_kernel(const MlaDecodeArgs a, MlaWorkspace w) {
+  extern __shared__ float sm[];
+  const int H = a.s.H, KV = a.s.KV, D = a.s.D, R = a.s.R;
+  const int h = blockIdx.x, b = blockIdx.y, g = h / (H / KV);
+  const int S = w.S;
+  float* av = sm;          // [R]
+  float* wgt = sm + R;     // [S]
+  const float* ws = static_cast<const float*>(a.ws);
+  const float* pml = ws + w.off_pml / 4 + ((int64_t)b * S * H) * 2;
+  const float* pacc = ws + w.off_pacc / 4 + ((int64_t)b * S * H) * R;
+
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float s_inv_l;
+  if (threadIdx.x == 0) {
+    float mx = -INFINITY;
+    for (int s = 0; s < S; ++s) mx = fmaxf(mx, pml[((int64_t)s * H + h) * 2]);
+    float l = 0.f;
+    for (int s = 0; s < S; ++s) {
+      const float e = expf(pml[((int64_t)s * H + h) * 2] - mx);
+      wgt[s] = e;
+      l += e * pml[((int64_t)s * H + h) * 2 + 1];
+    }
+    s_inv_l = 1.f / l;
+  }
+  __syncthreads();
+  for (int r = threadIdx.x; r < R; r += blockDim.x) {
+    float v = 0.f;
+    for (int s = 0; s < S; ++s) v = fmaf(wgt[s], pacc[((int64_t)s * H + h) * R + r], v);
+    av[r] = v * s_inv_l;
+  }
+  __syncthreads();
+  const T* wuv = static_cast<const T*>(a.w_uv) + (int64_t)g * D * R;
+  T* out = static_cast<T*>(a.out) + (int64_t)b * a.o_sb + (int64_t)h * D;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int d = warp; d < D; d += nw) {
+    float v = 0.f;
+    for (int r = lane; r < R; r += 32) v = fmaf(ldf(wuv, (int64_t)d * R + r), av[r], v);
+    v = warp_sum(v);
+    if (lane == 0) out[d] = from_f<T>(v);
+  }
+}
+
+size_t split_smem_bytes(const b200mm_mla_shape& s) {
+  const int H = s.H, R = s.R, DR = s.DR, KV = s.KV;
+  return sizeof(float) * ((size_t)H * R * 2 + (size_t)H * DR + (size_t)kTileT * R +
+                          (size_t)kTileT * KV * DR + (size_t)H * kTileT + (size_t)kTileT * KV + 3 * H);
+}
+
+template <typename K, typename... Args>
+int launch_smem(K kern, dim3 grid, size_t smem, cudaStream_t st, Args... args) {
+  if (smem > 48 * 1024) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return B200MM_ERR_LAUNCH;
+  }
+  return launch_pdl(kern, grid, dim3(kThreads), smem, st, args...) == cudaSuccess ? B200MM_OK
+                                                                                  : B200MM_ERR_LAUNCH;
+}
+
+template <typename T>
+int decode_t(const MlaDecodeArgs& a) {
+  const MlaWorkspace w = mla_plan(a.s, a.L);
+  const int B = a.s.B, H = a.s.H;
+  int st = launch_smem(mla_absorb_kernel<T>, dim3(H, B), sizeof(float) * a.s.D, a.stream, a, w);
+  if (st) return st;
+  if (!g_force_generic.load(std::memory_order_relaxed) && mla_fast_supported(a)) {
+    st = mla_fast_split_launch(a, w);
+  } else {
+    st = launch_smem(mla_split_kernel<T>, dim3(w.S, B), split_smem_bytes(a.s), a.stream, a, w);
+  }
+  if (st) return st;
+  return launch_smem(mla_combine_kernel<T>, dim3(H, B), sizeof(float) * (a.s.R + w.S), a.stream, a, w);
+}
+
+template <typename T>
+int scales_t(const MlaScalesArgs& a) {
+  const int64_t n = a.t1 - a.t0;
+  dim3 grid((unsigned)((n + 7) / 8), (unsigned)a.s.B);
+  const size_t smem = sizeof(float) * (8 * (size_t)a.s.R + 8 * (size_t)a.s.KV);
+  return launch_smem(mla_scales_kernel<T>, grid, smem, a.stream, a);
+}
+
+}  // namespace
+
+int mla_validate_shape(const b200mm_mla_shape& s) {
+  if (s.dtype != B200MM_F32 && s.dtype != B200MM_F16 && s.dtype != B200MM_BF16) return B200MM_ERR_DTYPE;
+  if (s.B < 0 || s.B > 65535 || s.H < 1 || s.KV < 1 || s.H % s.KV || s.H > 65535) return B200MM_ERR_SHAPE;
+  if (s.D < 1 || s.D > 1024 || s.DR < 0 || s.DR > s.D || (s.DR & 1)) return B200MM_ERR_SHAPE;
+  if (s.R < 1 || s.R > 4096) return B200MM_ERR_SHAPE;
+  if (!(s.eps >= 0.f)) return B200MM_ERR_ARG;
+  if (split_smem_bytes(s) > 200 * 1024) return B200MM_ERR_SHAPE;
+  return B200MM_OK;
+}
+
+MlaWorkspace mla_plan(const b200mm_mla_shape& s, int64_t L) {
+  MlaWorkspace w{};
+  const int B = s.B > 0 ? s.B : 1;
+  // Enough splits for ~2 CTAs per SM in total, chunks of >= 64 tokens.
+  const int target = 2 * num_sms(current_device());
+  int64_t S = (target + B - 1) / B;
+  const int64_t max_s = (L + 63) / 64;
+  if (S > max_s) S = max_s;
+  if (S < 1) S = 1;
+  int64_t chunk = (L + S - 1) / S;
+  chunk = (chunk + 63) / 64 * 64;
+  S = (L + chunk - 1) / chunk;
+  w.S = (int)S;
+  w.chunk = chunk;
+  const size_t BH = (size_t)B * s.H;
+  w.off_qt = 0;
+  w.off_qr = align256(w.off_qt + sizeof(float) * BH * s.R);
+  w.off_pacc = align256(w.off_qr + sizeof(float) * BH * (s.DR > 0 ? s.DR : 1));
+  w.off_pml = align256(w.off_pacc + sizeof(float) * BH * S * s.R);
+  w.total = align256(w.off_pml + sizeof(float) * BH * S * 2);
+  return w;
+}
+
+size_t mla_workspace_bytes(const b200mm_mla_shape& s, int64_t L) { return mla_plan(s, L).total; }
+
+int mla_scales_launch(const MlaScalesArgs& a) {
+  if (a.s.dtype == B200MM_BF16) return scales_t<__nv_bfloat16>(a);
+  if (a.s.dtype == B200MM_F16) return scales_t<__half>(a);
+  return scales_t<float>(a);
+}
+
+int mla_decode_launch(const MlaDecodeArgs& a) {
+  if (a.s.dtype == B200MM_BF16) return decode_t<__nv_bfloat16>(a);
+  if (a.s.dtype == B200MM_F16) return decode_t<__half>(a);
+  return decode_t<float>(a);
+}
+
+}  // namespace b200mm

@@ -1,0 +1,323 @@
+"""Absorbed latent-KV MLA decode backend for the engine's ``MLAttention``.
+
+The reference decode step (engine/mla.py:173-265, T == 1) re-expands K and V
+for every cached token on every step.  This backend keeps the reference's
+cache (``MLAKVCache``: ``c_kv`` and ``k_rope_pre``, engine/mla.py:41-87) and
+its module parameters, and runs the attention core in one pass over the
+latent cache through ``b200mm_mla_decode``:
+
+* per-token k-RMS factors (the scalar the ``k_norm`` RMSNorm multiplies each
+  reconstructed K head by) are kept in a float32 side-band ``[B, S, KV]``
+  attached to the cache object and filled once per token by
+  ``b200mm_mla_kv_scales`` -- lazily for tokens a prefill wrote, and for the
+  new token of each decode step;
+* the query is absorbed through ``W_uk`` and the context is split across CTAs
+  with an online-softmax merge; ``W_uv`` is applied once per head.
+
+Public pieces:
+  mla_decode(...)       functional core (q already q_norm'ed)
+  mla_kv_scales(...)    side-band fill for a token range
+  B200MLAttention       drop-in module (same constructor / forward signature
+                        as the reference ``MLAttention``)
+  apply_b200_mla(model) in-place swap walker, mirroring ``apply_mla``
+                        (mla/swap.py:21-69)
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from . import _capi
+from .kernels._eager import rotate_half
+
+
+def rope_inv_freq(head_dim: int, d_rope: int, theta: float, device=None) -> torch.Tensor:
+    """The reference's partial-RoPE frequencies (engine/mla.py:158-163): the
+    first d_rope/2 entries of the head_dim-sized vector, in float32."""
+    full = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim))
+    return full[: d_rope // 2].contiguous().to(device)
+
+
+def _shape(B, H, KV, D, DR, R, dtype, eps) -> _capi.MlaShape:
+    return _capi.MlaShape(B=B, H=H, KV=KV, D=D, DR=DR, R=R, dtype=_capi.dtype_code(dtype), eps=eps)
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def workspace_bytes(B: int, H: int, KV: int, D: int, DR: int, R: int, L: int, dtype, eps: float = 1e-6) -> int:
+    shp = _shape(B, H, KV, D, DR, R, dtype, eps)
+    return int(_capi.lib.b200mm_mla_decode_workspace_size(ctypes.byref(shp), L))
+
+
+def mla_kv_scales(c_kv: torch.Tensor, k_rope_pre: torch.Tensor | None, w_uk: torch.Tensor | None,
+                  kscale: torch.Tensor, *, B: int, t0: int, t1: int, num_kv_heads: int, head_dim: int,
+                  eps: float) -> None:
+    """Fill ``kscale[:B, t0:t1, :]`` from the cached latent / rope keys.
+
+    c_kv [*, S, R]; k_rope_pre [*, S, KV, DR] or None (DR == 0);
+    w_uk [KV, DN, R] or None (DN == 0); kscale float32 [*, S, KV].
+    """
+    _capi.require_cuda(c_kv, kscale)
+    R = c_kv.shape[-1]
+    DR = 0 if k_rope_pre is None else k_rope_pre.shape[-1]
+    shp = _shape(B, 1 * num_kv_heads, num_kv_heads, head_dim, DR, R, c_kv.dtype, eps)
+    if kscale.dtype != torch.float32 or kscale.stride(-1) != 1:
+        raise ValueError("kscale must be float32 with a dense last dim")
+    with torch.cuda.device(c_kv.device):
+        st = _capi.lib.b200mm_mla_kv_scales(
+            ctypes.byref(shp), c_kv.data_ptr(), c_kv.stride(0), c_kv.stride(1),
+            _ptr(k_rope_pre), 0 if k_rope_pre is None else k_rope_pre.stride(0),
+            0 if k_rope_pre is None else k_rope_pre.stride(1),
+            _ptr(w_uk), kscale.data_ptr(), kscale.stride(0), kscale.stride(1), t0, t1,
+            _capi.stream_of(c_kv),
+        )
+    _capi.check(st, "b200mm_mla_kv_scales")
+
+
+def mla_decode(q: torch.Tensor, c_kv: torch.Tensor, k_rope_pre: torch.Tensor | None, kscale: torch.Tensor,
+               w_uk: torch.Tensor | None, w_uv: torch.Tensor, k_norm_w: torch.Tensor,
+               inv_freq: torch.Tensor | None, *, L: int, scale: float, eps: float,
+               out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """One MLA decode step over cache positions ``0..L-1``.
+
+    Args:
+        q: ``(B, H, D)`` query after ``q_norm``, before RoPE.
+        c_kv: ``(*, S, R)`` latent cache (rows ``0..B-1`` used), S >= L.
+        k_rope_pre: ``(*, S, KV, DR)`` un-normed rope keys, or None if DR == 0.
+        kscale: ``(*, S, KV)`` float32 side-band, valid for positions < L.
+        w_uk: ``(KV, DN, R)``, or None if DN == 0.  w_uv: ``(KV, D, R)``.
+        k_norm_w: ``(D,)`` float32.  inv_freq: ``(DR/2,)`` float32.
+    Returns:
+        ``(B, H, D)`` attention output in q's dtype (the input of ``o``).
+    """
+    B, H, D = q.shape
+    R = c_kv.shape[-1]
+    KV = w_uv.shape[0]
+    DR = 0 if k_rope_pre is None else k_rope_pre.shape[-1]
+    _capi.require_cuda(q, c_kv, kscale, w_uv)
+    if q.stride(-1) != 1 or q.stride(1) != D:
+        q = q.contiguous()
+    shp = _shape(B, H, KV, D, DR, R, q.dtype, eps)
+    ws_bytes = int(_capi.lib.b200mm_mla_decode_workspace_size(ctypes.byref(shp), L))
+    if workspace is None or workspace.numel() < ws_bytes:
+        workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
+    if out is None:
+        out = torch.empty((B, H, D), dtype=q.dtype, device=q.device)
+    with torch.cuda.device(q.device):
+        st = _capi.lib.b200mm_mla_decode(
+            ctypes.byref(shp), q.data_ptr(), q.stride(0),
+            c_kv.data_ptr(), c_kv.stride(0), c_kv.stride(1),
+            _ptr(k_rope_pre), 0 if k_rope_pre is None else k_rope_pre.stride(0),
+            0 if k_rope_pre is None else k_rope_pre.stride(1),
+            kscale.data_ptr(), kscale.stride(0), kscale.stride(1),
+            _ptr(w_uk), w_uv.data_ptr(), k_norm_w.data_ptr(), _ptr(inv_freq),
+            float(scale), L, out.data_ptr(), out.stride(0),
+            workspace.data_ptr(), workspace.numel(), _capi.stream_of(q),
+        )
+    _capi.check(st, "b200mm_mla_decode")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# drop-in module
+# ---------------------------------------------------------------------------
+class _RMSNorm(nn.Module):
+    def __init__(self, dim: int, eps: float) -> None:
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(dim))
+        self.eps = eps
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        xf = x.float()
+        xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
+        return self.weight * xf.to(x.dtype)
+
+
+def _sideband(kv_cache, layer_idx: int, KV: int, like: torch.Tensor):
+    """The float32 k-RMS side-band for ``layer_idx`` (allocated on first use)
+    and the number of leading positions it currently covers."""
+    bands = getattr(kv_cache, "_b200_kscale", None)
+    if bands is None:
+        bands = {}
+        kv_cache._b200_kscale = bands
+        kv_cache._b200_kscale_len = {}
+    if layer_idx not in bands:
+        c = kv_cache.c_kv[layer_idx]
+        bands[layer_idx] = torch.empty((c.shape[0], c.shape[1], KV), dtype=torch.float32, device=c.device)
+        kv_cache._b200_kscale_len[layer_idx] = 0
+    return bands[layer_idx], kv_cache._b200_kscale_len
+
+
+class B200MLAttention(nn.Module):
+    """Partial-RoPE GQA over the compressed latent cache, with the T == 1
+    (decode) step on the absorbed B200 kernel.
+
+    Constructor, parameters (``q, dkv, uk_nope, uv, kr, o, q_norm, k_norm``,
+    ``rope_cos/rope_sin`` buffers) and ``forward`` signature follow the
+    reference ``MLAttention`` (engine/mla.py:105-181).  Prefill (T > 1)
+    follows the reference's reconstruct-then-SDPA math (engine/mla.py:189-265).
+    """
+
+    def __init__(self, *, hidden_size: int, num_heads: int, num_kv_heads: int, head_dim: int, rms_eps: float,
+                 rank: int, d_rope: int, max_position_embeddings: int, rope_theta: float = 10000.0,
+                 qk_norm_mode: str = "single") -> None:
+        super().__init__()
+        if d_rope < 0 or d_rope > head_dim:
+            raise ValueError(f"d_rope={d_rope} not in [0, head_dim={head_dim}]")
+        if qk_norm_mode != "single":
+            raise NotImplementedError(f"qk_norm_mode={qk_norm_mode!r}: only 'single' is implemented")
+        self.num_heads, self.num_kv_heads, self.head_dim = num_heads, num_kv_heads, head_dim
+        self.rank, self.d_rope, self.d_nope = rank, d_rope, head_dim - d_rope
+        self.qk_norm_mode = qk_norm_mode
+        self.rope_theta = rope_theta
+        self.q = nn.Linear(hidden_size, num_heads * head_dim, bias=False)
+        self.dkv = nn.Linear(hidden_size, rank, bias=False)
+        self.uk_nope = nn.Linear(rank, num_kv_heads * self.d_nope, bias=False) if self.d_nope > 0 else None
+        self.uv = nn.Linear(rank, num_kv_heads * head_dim, bias=False)
+        self.kr = nn.Linear(hidden_size, num_kv_heads * d_rope, bias=False) if d_rope > 0 else None
+        self.o = nn.Linear(num_heads * head_dim, hidden_size, bias=False)
+        self.q_norm = _RMSNorm(head_dim, rms_eps)
+        self.k_norm = _RMSNorm(head_dim, rms_eps)
+        if d_rope > 0:
+            inv = rope_inv_freq(head_dim, d_rope, rope_theta)
+            ang = torch.outer(torch.arange(max_position_embeddings, dtype=torch.float32), inv)
+            emb = torch.cat([ang, ang], dim=-1)
+            self.register_buffer("rope_cos", emb.cos(), persistent=False)
+            self.register_buffer("rope_sin", emb.sin(), persistent=False)
+        else:
+            self.rope_cos = None
+            self.rope_sin = None
+
+    @classmethod
+    def from_eager(cls, eager: nn.Module, *, rope_theta: float | None = None) -> "B200MLAttention":
+        """Wrap a reference ``MLAttention``, sharing all parameters and buffers.
+
+        The reference module does not store its RoPE base; pass ``rope_theta``
+        (the artifact's ``meta["rope_theta"]``) unless ``eager`` carries one.
+        """
+        theta = rope_theta if rope_theta is not None else getattr(eager, "rope_theta", None)
+        if eager.d_rope > 0 and theta is None:
+            raise ValueError("rope_theta is required to wrap an MLAttention with d_rope > 0")
+        out = cls.__new__(cls)
+        nn.Module.__init__(out)
+        for name in ("num_heads", "num_kv_heads", "head_dim", "rank", "d_rope", "d_nope", "qk_norm_mode"):
+            setattr(out, name, getattr(eager, name))
+        out.rope_theta = theta
+        for name in ("q", "dkv", "uk_nope", "uv", "kr", "o", "q_norm", "k_norm"):
+            setattr(out, name, getattr(eager, name))
+        out.rope_cos = eager.rope_cos
+        out.rope_sin = eager.rope_sin
+        return out
+
+    # -- helpers ------------------------------------------------------------
+    def _consts(self, device):
+        """float32 k_norm weight and RoPE frequencies, cached per device."""
+        key = (device, self.k_norm.weight._version, self.k_norm.weight.data_ptr())
+        cache = getattr(self, "_b200_consts", None)
+        if cache is None or cache[0] != key:
+            kw = self.k_norm.weight.detach().float().contiguous().to(device)
+            inv = rope_inv_freq(self.head_dim, self.d_rope, self.rope_theta, device) if self.d_rope > 0 else None
+            cache = (key, kw, inv)
+            self._b200_consts = cache
+        return cache[1], cache[2]
+
+    def supports_fast_decode(self, x: torch.Tensor) -> bool:
+        return x.is_cuda and x.shape[1] == 1 and x.dtype in _capi.DTYPE_CODES
+
+    def forward(self, x: torch.Tensor, *, kv_cache, layer_idx: int, start_pos: int,
+                cos: torch.Tensor | None = None, sin: torch.Tensor | None = None) -> torch.Tensor:
+        del cos, sin  # accepted for signature compatibility, as in the reference
+        if self.supports_fast_decode(x):
+            return self._decode(x, kv_cache=kv_cache, layer_idx=layer_idx, start_pos=start_pos)
+        return self._eager(x, kv_cache=kv_cache, layer_idx=layer_idx, start_pos=start_pos)
+
+    def _write_cache(self, x, kv_cache, layer_idx, start_pos, end):
+        B, T, _ = x.shape
+        kv_cache.c_kv[layer_idx][:B, start_pos:end, :] = self.dkv(x)
+        if self.d_rope > 0:
+            kv_cache.k_rope_pre[layer_idx][:B, start_pos:end] = self.kr(x).view(B, T, self.num_kv_heads, self.d_rope)
+
+    def _decode(self, x, *, kv_cache, layer_idx, start_pos):
+        B = x.shape[0]
+        H, KV, D, DR, DN = self.num_heads, self.num_kv_heads, self.head_dim, self.d_rope, self.d_nope
+        end = start_pos + 1
+        q = self.q_norm(self.q(x).view(B, 1, H, D))
+        self._write_cache(x, kv_cache, layer_idx, start_pos, end)
+        c = kv_cache.c_kv[layer_idx]
+        kr = kv_cache.k_rope_pre[layer_idx] if DR > 0 else None
+        w_uk = self.uk_nope.weight.view(KV, DN, self.rank) if DN > 0 else None
+        w_uv = self.uv.weight.view(KV, D, self.rank)
+        kscale, lens = _sideband(kv_cache, layer_idx, KV, c)
+        valid = min(lens[layer_idx], start_pos)
+        mla_kv_scales(c, kr, w_uk, kscale, B=B, t0=valid, t1=end, num_kv_heads=KV, head_dim=D,
+                      eps=self.k_norm.eps)
+        lens[layer_idx] = end
+        kw, inv = self._consts(x.device)
+        attn = mla_decode(q.view(B, H, D), c, kr, kscale, w_uk, w_uv, kw, inv, L=end, scale=D ** -0.5,
+                          eps=self.k_norm.eps)
+        return self.o(attn.view(B, 1, H * D))
+
+    def _eager(self, x, *, kv_cache, layer_idx, start_pos):
+        """Reconstruct-then-SDPA path of the reference (engine/mla.py:189-265)."""
+        B, T, _ = x.shape
+        H, KV, D, DN, DR = self.num_heads, self.num_kv_heads, self.head_dim, self.d_nope, self.d_rope
+        end = start_pos + T
+        q = self.q_norm(self.q(x).view(B, T, H, D)).transpose(1, 2)
+        self._write_cache(x, kv_cache, layer_idx, start_pos, end)
+        # tokens rewritten here invalidate their side-band entries
+        lens = getattr(kv_cache, "_b200_kscale_len", None)
+        if lens is not None and layer_idx in lens:
+            lens[layer_idx] = min(lens[layer_idx], start_pos)
+        c = kv_cache.c_kv[layer_idx][:B, :end]
+        v = self.uv(c).view(B, end, KV, D)
+        parts = []
+        if DN > 0:
+            parts.append(self.uk_nope(c).view(B, end, KV, DN))
+        if DR > 0:
+            parts.append(kv_cache.k_rope_pre[layer_idx][:B, :end])
+        k = self.k_norm(torch.cat(parts, dim=-1) if len(parts) > 1 else parts[0])
+        if DR > 0:
+            qn, qr = q.split([DN, DR], dim=-1)
+            kn, kr = k.split([DN, DR], dim=-1)
+            cq, sq = self.rope_cos[start_pos:end].to(q.dtype), self.rope_sin[start_pos:end].to(q.dtype)
+            ck, sk = self.rope_cos[:end].to(k.dtype), self.rope_sin[:end].to(k.dtype)
+            qr = qr * cq + rotate_half(qr) * sq
+            kr = kr.transpose(1, 2)
+            kr = (kr * ck + rotate_half(kr) * sk).transpose(1, 2)
+            q = torch.cat([qn, qr], dim=-1) if DN > 0 else qr
+            k = torch.cat([kn, kr], dim=-1) if DN > 0 else kr
+        k = k.transpose(1, 2)
+        v = v.transpose(1, 2)
+        if H // KV > 1:
+            k = k.repeat_interleave(H // KV, dim=1)
+            v = v.repeat_interleave(H // KV, dim=1)
+        qp = torch.arange(start_pos, end, device=x.device).unsqueeze(1)
+        kp = torch.arange(0, end, device=x.device).unsqueeze(0)
+        attn = F.scaled_dot_product_attention(q, k, v, attn_mask=qp >= kp)
+        return self.o(attn.transpose(1, 2).reshape(B, T, H * D))
+
+
+def apply_b200_mla(model: nn.Module, *, rope_theta: float | None = None) -> nn.Module:
+    """Swap every latent-attention ``block.attn`` (anything with ``dkv``,
+    ``uv`` and ``rank``) for :class:`B200MLAttention`, sharing parameters.
+    Idempotent; returns ``model``."""
+    if rope_theta is None:
+        cfg = getattr(model, "cfg", None)
+        rp = getattr(cfg, "rope_parameters", None)
+        if isinstance(rp, dict) and "rope_theta" in rp:
+            rope_theta = float(rp["rope_theta"])
+        elif cfg is not None and hasattr(cfg, "rope_theta"):
+            rope_theta = float(cfg.rope_theta)
+    for block in model.layers:
+        a = block.attn
+        if isinstance(a, B200MLAttention):
+            continue
+        if all(hasattr(a, n) for n in ("dkv", "uv", "rank")):
+            block.attn = B200MLAttention.from_eager(a, rope_theta=rope_theta)
+    return model

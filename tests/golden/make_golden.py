@@ -1,0 +1,180 @@
+"""Generate golden outputs by running the REFERENCE engine's own modules.
+
+Run in a container where the reference checkout exists:
+
+    LLMS_REF=/path/to/aaholmes-llms python tests/golden/make_golden.py
+
+Inputs come from ``oracle/inputs.py`` (seeded numpy), so the fixtures hold
+only the reference's OUTPUTS (plus the few values the reference module itself
+produced inside its forward, e.g. the normalised q of an MLA step).  Every
+forward runs in float32 on CPU on bf16-representable inputs, i.e. the
+"fp32-accumulated reference on identical inputs" the parity tests compare
+against.  Values are captured with forward hooks on the reference modules:
+  * gate-up-SiLU: the input of ``FFN.down`` inside ``FFN.forward``
+    (engine/model.py:36-37);
+  * QKV: the outputs of ``Attention.q/k/v`` inside ``Attention.forward``
+    (engine/attention.py:119-121);
+  * MLA decode: the output of ``q_norm`` and the input of ``o`` inside
+    ``MLAttention.forward`` (engine/mla.py:195-265), T == 1.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+sys.path.insert(0, str(REPO))
+REF = Path(os.environ.get("LLMS_REF", "/root/reference"))
+sys.path.insert(0, str(REF / "src"))
+
+from engine.attention import Attention, RMSNorm  # noqa: E402
+from engine.kv_cache import KVCache  # noqa: E402
+from engine.mla import MLAKVCache, MLAttention  # noqa: E402
+from engine.model import FFN  # noqa: E402
+
+from oracle import inputs as I  # noqa: E402
+
+
+def capture_input(module):
+    box = {}
+    h = module.register_forward_hook(lambda m, args, out: box.__setitem__("v", args[0].detach().clone()))
+    return box, h
+
+
+def capture_output(module):
+    box = {}
+    h = module.register_forward_hook(lambda m, args, out: box.__setitem__("v", out.detach().clone()))
+    return box, h
+
+
+def ref_gate_up(x, wg, wu):
+    N, K = wg.shape
+    ffn = FFN(K, N)
+    with torch.no_grad():
+        ffn.gate.weight.copy_(torch.from_numpy(wg))
+        ffn.up.weight.copy_(torch.from_numpy(wu))
+    box, h = capture_input(ffn.down)
+    with torch.no_grad():
+        ffn(torch.from_numpy(x))
+    h.remove()
+    return box["v"].numpy()
+
+
+def ref_qkv(x, w, n_q, n_k, head_dim=128):
+    K = w.shape[1]
+    attn = Attention(hidden_size=K, num_heads=n_q // head_dim, num_kv_heads=n_k // head_dim,
+                     head_dim=head_dim, rms_eps=1e-6)
+    with torch.no_grad():
+        attn.q.weight.copy_(torch.from_numpy(w[:n_q]))
+        attn.k.weight.copy_(torch.from_numpy(w[n_q:n_q + n_k]))
+        attn.v.weight.copy_(torch.from_numpy(w[n_q + n_k:]))
+    bq, h1 = capture_output(attn.q)
+    bk, h2 = capture_output(attn.k)
+    bv, h3 = capture_output(attn.v)
+    M = x.shape[0]
+    cache = KVCache.alloc(num_layers=1, max_batch=1, num_kv_heads=n_k // head_dim, max_seq_len=M,
+                          head_dim=head_dim, dtype=torch.float32, device="cpu")
+    cos = torch.ones(M, head_dim)
+    sin = torch.zeros(M, head_dim)
+    with torch.no_grad():
+        attn(torch.from_numpy(x)[None], kv_cache=cache, layer_idx=0, cos=cos, sin=sin, start_pos=0)
+    for h in (h1, h2, h3):
+        h.remove()
+    return bq["v"][0].numpy(), bk["v"][0].numpy(), bv["v"][0].numpy()
+
+
+def ref_mla_decode(d, L, *, H, KV, D, DR, R, theta, eps, seed, knorm_noise):
+    """Run MLAttention.forward for one token at position L-1 on a cache whose
+    rows 0..L-2 are the seeded inputs.  Returns (q_normed, new c row, new kr
+    row, attention output before o, rope tables for positions 0..L-1)."""
+    B = d["q"].shape[0]
+    hidden = 64
+    torch.manual_seed(seed)
+    mla = MLAttention(hidden_size=hidden, num_heads=H, num_kv_heads=KV, head_dim=D, rms_eps=eps, rank=R,
+                      d_rope=DR, max_position_embeddings=L + 1, rope_theta=theta, qk_norm_mode="single")
+    with torch.no_grad():
+        for lin in (mla.q, mla.dkv, mla.kr, mla.o):
+            if lin is not None:
+                lin.weight.copy_(torch.randn_like(lin.weight) * 0.1)
+        if mla.uk_nope is not None:
+            mla.uk_nope.weight.copy_(torch.from_numpy(d["w_uk"].reshape(KV * (D - DR), R)))
+        mla.uv.weight.copy_(torch.from_numpy(d["w_uv"].reshape(KV * D, R)))
+        kw = torch.from_numpy(d["k_norm_w"]).clone()
+        if knorm_noise:
+            kw = kw + knorm_noise * torch.randn(D)
+        mla.k_norm.weight.copy_(kw)
+    cache = MLAKVCache.alloc(num_layers=1, max_batch=B, num_kv_heads=KV, max_seq_len=L + 1, rank=R,
+                             d_rope=DR, dtype=torch.float32, device="cpu")
+    cache.c_kv[0][:, : L - 1] = torch.from_numpy(d["c_kv"][:, : L - 1])
+    if DR > 0:
+        cache.k_rope_pre[0][:, : L - 1] = torch.from_numpy(d["k_rope_pre"][:, : L - 1])
+    bq, h1 = capture_output(mla.q_norm)
+    bo, h2 = capture_input(mla.o)
+    x = torch.randn(B, 1, hidden)
+    with torch.no_grad():
+        mla(x, kv_cache=cache, layer_idx=0, start_pos=L - 1)
+    h1.remove()
+    h2.remove()
+    out = dict(
+        q=bq["v"][:, 0].numpy(),
+        c_new=cache.c_kv[0][:, L - 1].numpy().copy(),
+        attn=bo["v"][:, 0].reshape(B, H, D).numpy(),
+        k_norm_w=mla.k_norm.weight.detach().numpy().copy(),
+    )
+    if DR > 0:
+        out["kr_new"] = cache.k_rope_pre[0][:, L - 1].numpy().copy()
+        out["rope_cos"] = mla.rope_cos[:L].numpy().copy()
+        out["rope_sin"] = mla.rope_sin[:L].numpy().copy()
+    return out
+
+
+def main() -> None:
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    out = {}
+
+    x, wg, wu = I.cfg1()
+    out["cfg1_gate_up"] = ref_gate_up(x, wg, wu)
+
+    for M in (1, 4):
+        x, w = I.cfg2(M)
+        q, k, v = ref_qkv(x, w, 4096, 1024)
+        out[f"cfg2_m{M}_q"], out[f"cfg2_m{M}_k"], out[f"cfg2_m{M}_v"] = q, k, v
+        x, wg, wu = I.cfg3(M)
+        out[f"cfg3_m{M}_gate_up"] = ref_gate_up(x, wg, wu)
+
+    # int8 weight-only: dequantise, then the reference modules
+    for M in (1, 4):
+        lay = I.cfg5_layer(M=M)
+        wq = lay["qkv_q"].astype(np.float32) * lay["qkv_s"][:, None]
+        q, k, v = ref_qkv(lay["x"], wq, 4096, 1024)
+        out[f"cfg5_m{M}_qkv"] = np.concatenate([q, k, v], axis=-1)
+        wg = lay["gate_q"].astype(np.float32) * lay["gate_s"][:, None]
+        wu = lay["up_q"].astype(np.float32) * lay["up_s"][:, None]
+        out[f"cfg5_m{M}_gate_up"] = ref_gate_up(lay["x"], wg, wu)
+
+    mla_cases = {
+        # name: (B, L, dims, knorm noise)
+        "mla_4b_b2_l37": (2, 37, dict(H=32, KV=8, D=128, DR=32, R=256), 0.0),
+        "mla_4b_b1_l300_knorm": (1, 300, dict(H=32, KV=8, D=128, DR=32, R=256), 0.1),
+        "mla_tiny_dr8": (3, 9, dict(H=4, KV=2, D=16, DR=8, R=12), 0.1),
+        "mla_tiny_dr0": (2, 5, dict(H=4, KV=2, D=16, DR=0, R=12), 0.1),
+        "mla_tiny_drfull": (2, 6, dict(H=4, KV=2, D=16, DR=16, R=12), 0.1),
+    }
+    for name, (B, L, dims, noise) in mla_cases.items():
+        d = I.cfg4(B, L, **dims)
+        r = ref_mla_decode(d, L, theta=1e6, eps=1e-6, seed=5, knorm_noise=noise, **dims)
+        for k_, v_ in r.items():
+            out[f"{name}__{k_}"] = v_
+
+    np.savez_compressed(HERE / "golden.npz", **{k: np.asarray(v, np.float32) for k, v in out.items()})
+    print(f"wrote {HERE / 'golden.npz'} with {len(out)} arrays")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,93 @@
+"""C ABI checks that need no GPU: the library loads, exports every symbol
+the header declares, and rejects invalid calls before touching a device."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def header_symbols():
+    text = (ROOT / "include" / "b200mm.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(b200mm_\w+)\s*\(", text)))
+
+
+def test_library_exports_header_symbols():
+    from llms_b200 import _capi
+    syms = header_symbols()
+    assert len(syms) >= 10
+    for s in syms:
+        assert hasattr(_capi.lib, s), f"{s} declared in include/b200mm.h but not exported"
+        assert s in _capi.SIGNATURES, f"{s} has no ctypes signature"
+
+
+def test_status_strings_and_version():
+    from llms_b200 import _capi
+    assert _capi.lib.b200mm_abi_version() == 1
+    assert _capi.lib.b200mm_status_string(0) == b"ok"
+    for code in range(1, 9):
+        assert _capi.lib.b200mm_status_string(code) not in (b"ok", b"unknown status")
+    assert _capi.lib.b200mm_status_string(99) == b"unknown status"
+
+
+def test_null_pointers_and_bad_shapes_rejected_before_launch():
+    from llms_b200 import _capi
+    L = _capi.lib
+    before = L.b200mm_launch_count()
+    assert L.b200mm_gate_up_silu(None, 64, None, 64, None, 64, None, 64, 1, 64, 64, 2, None) == 5
+    fake = ctypes.c_void_p(16)
+    # K < 1, N < 1, ld < K, bad dtype
+    assert L.b200mm_qkv(fake, 64, fake, 64, fake, 96, 1, 96, 0, 2, None) == 1
+    assert L.b200mm_qkv(fake, 64, fake, 64, fake, 96, 1, 0, 64, 2, None) == 1
+    assert L.b200mm_qkv(fake, 32, fake, 64, fake, 96, 1, 96, 64, 2, None) == 1
+    assert L.b200mm_qkv(fake, 64, fake, 64, fake, 96, 1, 96, 64, 7, None) == 3
+    # int8 with fp32 activations is not a supported combination
+    assert L.b200mm_qkv_w8(fake, 64, fake, fake, 64, fake, 96, 1, 96, 64, 0, None) == 3
+    # M == 0 is a successful no-op
+    assert L.b200mm_qkv(fake, 64, fake, 64, fake, 96, 0, 96, 64, 2, None) == 0
+    shp = _capi.MlaShape(B=1, H=32, KV=8, D=128, DR=33, R=256, dtype=2, eps=1e-6)  # odd d_rope
+    assert L.b200mm_mla_decode_workspace_size(ctypes.byref(shp), 10) == 0
+    shp.DR = 32
+    assert L.b200mm_mla_decode_workspace_size(ctypes.byref(shp), 10) > 0
+    assert L.b200mm_launch_count() == before
+
+
+def test_shim_rejects_with_reference_messages():
+    """Same ValueError messages as reference tests/test_kernels_fused_ffn.py:209-229
+    and tests/test_kernels_fused_qkv.py:253-277 (host-side validation, CPU tensors)."""
+    from llms_b200.kernels import triton_fused_gate_up_silu, triton_fused_qkv
+    x = torch.randn(2, 64)
+    Wg = torch.randn(128, 64)
+    with pytest.raises(ValueError, match="Wg shape.*Wu shape"):
+        triton_fused_gate_up_silu(x, Wg, torch.randn(127, 64))
+    with pytest.raises(ValueError, match="Wg shape.*Wu shape"):
+        triton_fused_gate_up_silu(x, Wg, torch.randn(128, 63))
+    W3 = torch.randn(2, 128, 64)
+    with pytest.raises(ValueError, match="Wg must be 2D"):
+        triton_fused_gate_up_silu(x, W3, W3)
+    with pytest.raises(ValueError, match="x last dim.*Wg.shape"):
+        triton_fused_gate_up_silu(torch.randn(2, 63), Wg, Wg)
+
+    W_qkv = torch.randn(96, 64)
+    with pytest.raises(ValueError, match="n_q .* 2.n_k"):
+        triton_fused_qkv(x, W_qkv, n_q=64, n_k=15)
+    with pytest.raises(ValueError, match="x last dim .* W_qkv"):
+        triton_fused_qkv(torch.randn(2, 63), W_qkv, n_q=64, n_k=16)
+    with pytest.raises(ValueError, match="W_qkv must be 2D"):
+        triton_fused_qkv(x, torch.randn(2, 96, 64), n_q=64, n_k=16)
+
+
+def test_cpu_tensors_fail_loudly():
+    """No CPU fallback: a valid call on CPU tensors raises instead of computing."""
+    from llms_b200.kernels import triton_fused_gate_up_silu, triton_fused_qkv
+    x = torch.randn(2, 64)
+    W = torch.randn(96, 64)
+    with pytest.raises(RuntimeError, match="no CPU path"):
+        triton_fused_gate_up_silu(x, W, W)
+    with pytest.raises(RuntimeError, match="no CPU path"):
+        triton_fused_qkv(x, W, n_q=64, n_k=16)

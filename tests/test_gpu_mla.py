@@ -1,0 +1,159 @@
+"""GPU parity of the absorbed MLA latent decode vs the oracle and the
+reference's golden outputs.  Calls go through llms_b200.mla -> the C ABI."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import inputs as I
+from oracle import reference_math as O
+from tests.conftest import bf16_check
+from tests.gpu_util import dev, force_generic, host
+from tests.test_oracle_golden import MLA_CASES, mla_case
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import llms_b200.mla  # noqa: F401
+
+
+def run_kernel(d, L, dims, dtype, *, S=None, theta=1e6, eps=1e-6):
+    """Side-band fill + decode through the C ABI. Cache allocated with S >= L rows."""
+    from llms_b200 import mla
+    B, H, D = d["q"].shape
+    KV, DR, R = dims["KV"], dims["DR"], dims["R"]
+    S = S or L + 3
+    c = torch.zeros((B, S, R), dtype=dtype, device="cuda")
+    c[:, :L] = dev(d["c_kv"][:, :L], dtype)
+    kr = None
+    if DR:
+        kr = torch.zeros((B, S, KV, DR), dtype=dtype, device="cuda")
+        kr[:, :L] = dev(d["k_rope_pre"][:, :L], dtype)
+    w_uk = dev(d["w_uk"], dtype) if D - DR else None
+    w_uv = dev(d["w_uv"], dtype)
+    ks = torch.full((B, S, KV), float("nan"), dtype=torch.float32, device="cuda")
+    mla.mla_kv_scales(c, kr, w_uk, ks, B=B, t0=0, t1=L, num_kv_heads=KV, head_dim=D, eps=eps)
+    kw = dev(d["k_norm_w"], torch.float32)
+    inv = mla.rope_inv_freq(D, DR, theta, "cuda") if DR else None
+    out = mla.mla_decode(dev(d["q"], dtype), c, kr, ks, w_uk, w_uv, kw, inv, L=L, scale=D ** -0.5, eps=eps)
+    torch.cuda.synchronize()
+    return out, ks
+
+
+def oracle_out(d, L, dims, dtype_round=True):
+    q = d["q"]
+    if dtype_round:
+        q = I.round_bf16(q)
+    inv = O.mla_inv_freq(dims["D"], dims["DR"], 1e6)
+    return O.mla_decode(q, d["c_kv"], d["k_rope_pre"], d["w_uk"], d["w_uv"], d["k_norm_w"], 1e-6, inv, L)
+
+
+@pytest.mark.parametrize("name", list(MLA_CASES))
+def test_golden_fp32(golden, name):
+    """fp32 storage: the kernel matches the reference module's output."""
+    B, L, dims, d = mla_case(golden, name)
+    out, _ = run_kernel(d, L, dims, torch.float32)
+    np.testing.assert_allclose(host(out), golden[f"{name}__attn"], rtol=1e-3, atol=1e-4)
+
+
+@pytest.mark.parametrize("name", list(MLA_CASES))
+def test_golden_bf16(golden, name):
+    """bf16 storage (q rounded to bf16): within the bf16 bar of the golden output."""
+    B, L, dims, d = mla_case(golden, name)
+    out, _ = run_kernel(d, L, dims, torch.bfloat16)
+    bf16_check(host(out), oracle_out(d, L, dims))
+    bf16_check(host(out), golden[f"{name}__attn"], max_abs=3e-2, rel_l2=1e-2)
+
+
+def test_kv_scales_vs_oracle():
+    dims = dict(H=32, KV=8, D=128, DR=32, R=256)
+    d = I.cfg4(2, 100, **dims)
+    _, ks = run_kernel(d, 100, dims, torch.bfloat16)
+    e = O.mla_kv_scales(d["c_kv"], d["k_rope_pre"], d["w_uk"], 1e-6, 128)
+    np.testing.assert_allclose(host(ks[:, :100]), e, rtol=2e-5, atol=0)
+
+
+@pytest.mark.parametrize("B,L", [(1, 1), (1, 63), (1, 64), (1, 65), (1, 512), (8, 512), (2, 4096), (8, 4096),
+                                 (32, 512)])
+def test_cfg4_shapes(B, L):
+    dims = dict(H=32, KV=8, D=128, DR=32, R=256)
+    d = I.cfg4(B, L, **dims)
+    out, _ = run_kernel(d, L, dims, torch.bfloat16)
+    bf16_check(host(out), oracle_out(d, L, dims))
+
+
+@pytest.mark.parametrize("B,L", [(1, 32768), (4, 32768)])
+def test_cfg4_long_context(B, L):
+    """Full BASELINE context length: oracle on the full input (float64 BLAS)."""
+    dims = dict(H=32, KV=8, D=128, DR=32, R=256)
+    d = I.cfg4(B, L, **dims)
+    out, _ = run_kernel(d, L, dims, torch.bfloat16)
+    bf16_check(host(out), oracle_out(d, L, dims))
+
+
+def test_constant_cache_property():
+    """If every cached token is the same, attention returns W_uv c for any L
+    (softmax weights sum to 1) -- checked at L = 32768, B = 32."""
+    from llms_b200 import mla
+    B, L, H, KV, D, DR, R = 32, 32768, 32, 8, 128, 32, 256
+    rng = np.random.default_rng(7)
+    c1 = rng.standard_normal(R).astype(np.float32)
+    c = torch.from_numpy(I.round_bf16(c1)).cuda().to(torch.bfloat16).expand(B, L, R).contiguous()
+    kr = torch.randn(B, L, KV, DR, device="cuda", dtype=torch.bfloat16)
+    w_uk = torch.randn(KV, D - DR, R, device="cuda", dtype=torch.bfloat16) * 0.25
+    w_uv = torch.randn(KV, D, R, device="cuda", dtype=torch.bfloat16) * 0.25
+    q = torch.randn(B, H, D, device="cuda", dtype=torch.bfloat16)
+    kr[:] = kr[:, :1]  # identical rope keys too -> identical scores up to RoPE phase
+    ks = torch.empty(B, L, KV, device="cuda")
+    mla.mla_kv_scales(c, kr, w_uk, ks, B=B, t0=0, t1=L, num_kv_heads=KV, head_dim=D, eps=1e-6)
+    out = mla.mla_decode(q, c, kr, ks, w_uk, w_uv, torch.ones(D, device="cuda"),
+                         mla.rope_inv_freq(D, DR, 1e6, "cuda"), L=L, scale=D ** -0.5, eps=1e-6)
+    g_of = np.arange(H) // (H // KV)
+    e = np.einsum("hdr,r->hd", host(w_uv)[g_of].astype(np.float64), host(c[0, 0]).astype(np.float64))
+    bf16_check(host(out), np.broadcast_to(e, (B, H, D)))
+
+
+@pytest.mark.parametrize("B,L", [(1, 700), (3, 2000)])
+def test_generic_matches_fast(B, L):
+    dims = dict(H=32, KV=8, D=128, DR=32, R=256)
+    d = I.cfg4(B, L, **dims)
+    fast, _ = run_kernel(d, L, dims, torch.bfloat16)
+    with force_generic():
+        slow, _ = run_kernel(d, L, dims, torch.bfloat16)
+    bf16_check(host(fast), host(slow).astype(np.float64))
+
+
+def test_module_decode_matches_eager():
+    """B200MLAttention: prefill (eager math) then decode steps on the kernel
+    agree with the eager reconstruct path at every step."""
+    from llms_b200.mla import B200MLAttention
+
+    class Cache:
+        def __init__(s, B, S, R, KV, DR, dtype):
+            s.c_kv = [torch.zeros(B, S, R, dtype=dtype, device="cuda")]
+            s.k_rope_pre = [torch.zeros(B, S, KV, DR, dtype=dtype, device="cuda")]
+            s.cur_len = 0
+
+    torch.manual_seed(0)
+    m = B200MLAttention(hidden_size=256, num_heads=32, num_kv_heads=8, head_dim=128, rms_eps=1e-6, rank=256,
+                        d_rope=32, max_position_embeddings=128, rope_theta=1e6).cuda().float()
+    with torch.no_grad():
+        for p in m.parameters():
+            p.copy_(torch.randn_like(p) * 0.1)
+        m.k_norm.weight.add_(1.0)
+    B, T0 = 2, 9
+    x0 = torch.randn(B, T0, 256, device="cuda")
+    ca, cb = Cache(B, 64, 256, 8, 32, torch.float32), Cache(B, 64, 256, 8, 32, torch.float32)
+    with torch.no_grad():
+        ya = m(x0, kv_cache=ca, layer_idx=0, start_pos=0)
+        yb = m._eager(x0, kv_cache=cb, layer_idx=0, start_pos=0)
+        torch.testing.assert_close(ya, yb)
+        for step in range(4):
+            xs = torch.randn(B, 1, 256, device="cuda")
+            ya = m(xs, kv_cache=ca, layer_idx=0, start_pos=T0 + step)
+            yb = m._eager(xs, kv_cache=cb, layer_idx=0, start_pos=T0 + step)
+            torch.testing.assert_close(ya, yb, rtol=1e-3, atol=1e-4)

@@ -1,0 +1,80 @@
+"""Pin the CPU oracle against golden outputs of the reference engine's own
+modules (tests/golden/make_golden.py).  CPU only."""
+
+import numpy as np
+import pytest
+
+from oracle import inputs as I
+from oracle import reference_math as O
+
+
+def _close(a, e, rtol, atol):
+    np.testing.assert_allclose(np.asarray(a, np.float64), np.asarray(e, np.float64), rtol=rtol, atol=atol)
+
+
+def test_cfg1_gate_up(golden):
+    x, wg, wu = I.cfg1()
+    _close(O.gate_up_silu(x, wg, wu), golden["cfg1_gate_up"], 1e-4, 1e-6)
+
+
+@pytest.mark.parametrize("M", [1, 4])
+def test_cfg2_qkv(golden, M):
+    x, w = I.cfg2(M)
+    q, k, v = O.qkv(x, w, 4096, 1024)
+    for name, got in (("q", q), ("k", k), ("v", v)):
+        _close(got, golden[f"cfg2_m{M}_{name}"], 1e-4, 1e-5)
+
+
+@pytest.mark.parametrize("M", [1, 4])
+def test_cfg3_gate_up(golden, M):
+    x, wg, wu = I.cfg3(M)
+    _close(O.gate_up_silu(x, wg, wu), golden[f"cfg3_m{M}_gate_up"], 1e-4, 1e-5)
+
+
+@pytest.mark.parametrize("M", [1, 4])
+def test_cfg5_int8(golden, M):
+    lay = I.cfg5_layer(M=M)
+    q, k, v = O.qkv(lay["x"], O.dequant(lay["qkv_q"], lay["qkv_s"]), 4096, 1024)
+    _close(np.concatenate([q, k, v], -1), golden[f"cfg5_m{M}_qkv"], 1e-4, 1e-5)
+    g = O.gate_up_silu(lay["x"], O.dequant(lay["gate_q"], lay["gate_s"]), O.dequant(lay["up_q"], lay["up_s"]))
+    _close(g, golden[f"cfg5_m{M}_gate_up"], 1e-4, 5e-5)
+
+
+MLA_CASES = {
+    "mla_4b_b2_l37": (2, 37, dict(H=32, KV=8, D=128, DR=32, R=256)),
+    "mla_4b_b1_l300_knorm": (1, 300, dict(H=32, KV=8, D=128, DR=32, R=256)),
+    "mla_tiny_dr8": (3, 9, dict(H=4, KV=2, D=16, DR=8, R=12)),
+    "mla_tiny_dr0": (2, 5, dict(H=4, KV=2, D=16, DR=0, R=12)),
+    "mla_tiny_drfull": (2, 6, dict(H=4, KV=2, D=16, DR=16, R=12)),
+}
+
+
+def mla_case(golden, name):
+    """Inputs of a golden MLA case: seeded cache rows 0..L-2 plus the new
+    token's row L-1 and the normalised q captured from the reference module."""
+    B, L, dims = MLA_CASES[name]
+    d = I.cfg4(B, L, **dims)
+    d["c_kv"][:, L - 1] = golden[f"{name}__c_new"]
+    if dims["DR"] > 0:
+        d["k_rope_pre"][:, L - 1] = golden[f"{name}__kr_new"]
+    d["q"] = golden[f"{name}__q"]
+    d["k_norm_w"] = golden[f"{name}__k_norm_w"]
+    return B, L, dims, d
+
+
+@pytest.mark.parametrize("name", list(MLA_CASES))
+def test_mla_decode(golden, name):
+    B, L, dims, d = mla_case(golden, name)
+    inv = O.mla_inv_freq(dims["D"], dims["DR"], 1e6)
+    out = O.mla_decode(d["q"], d["c_kv"], d["k_rope_pre"], d["w_uk"], d["w_uv"], d["k_norm_w"], 1e-6, inv, L)
+    _close(out, golden[f"{name}__attn"], 2e-4, 2e-5)
+
+
+@pytest.mark.parametrize("name", ["mla_4b_b2_l37", "mla_tiny_dr8"])
+def test_mla_rope_tables(golden, name):
+    """The reference's partial-RoPE table (engine/mla.py:151-171, theta=1e6,
+    head_dim 128, d_rope 32 for the 4B case) matches the oracle's."""
+    B, L, dims = MLA_CASES[name]
+    cos, sin = O.rope_cos_sin(np.arange(L), O.mla_inv_freq(dims["D"], dims["DR"], 1e6))
+    _close(cos, golden[f"{name}__rope_cos"], 0, 2e-6)
+    _close(sin, golden[f"{name}__rope_sin"], 0, 2e-6)
