@@ -127,14 +127,16 @@ __global__ void __launch_bounds__(kThreads) mla_absorb_kernel(const MlaDecodeArg
 }
 
 // --- generic split kernel ---------------------------------------------------
-// grid: (S, B); block 256.  Shared: qt[H][R], qr[H][DR], acc[H][R], c[TT][R],
-// z[TT][KV][DR], sc[H][TT], st[TT][KV], m[H], l[H], alpha[H].
+// grid: (G); block 256.  CTA i walks its range of 64-token units, 16 tokens at
+// a time, and writes one partial per batch row it touches.
+// Shared: qt[H][R], qr[H][DR], acc[H][R], c[TT][R], z[TT][KV][DR], sc[H][TT],
+// st[TT][KV], m[H], l[H], alpha[H].
 template <typename T>
 __global__ void __launch_bounds__(kThreads) mla_split_kernel(const MlaDecodeArgs a, MlaWorkspace w) {
   extern __shared__ float sm[];
   const int H = a.s.H, KV = a.s.KV, D = a.s.D, DR = a.s.DR, DN = D - DR, R = a.s.R;
   const int hpg = H / KV, half = DR / 2;
-  const int sidx = blockIdx.x, b = blockIdx.y;
+  const int cta = blockIdx.x;
   float* qt = sm;
   float* qr = qt + H * R;
   float* acc = qr + H * DR;
@@ -146,122 +148,141 @@ __global__ void __launch_bounds__(kThreads) mla_split_kernel(const MlaDecodeArgs
   float* lrun = mrun + H;
   float* alpha = lrun + H;
 
-  const float* ws = static_cast<const float*>(a.ws);
-  const int64_t t_begin = (int64_t)sidx * w.chunk;
-  const int64_t t_end = imin64(a.L, t_begin + w.chunk);
-  const T* c = static_cast<const T*>(a.c_kv) + (int64_t)b * a.c_sb;
-  const T* kr = static_cast<const T*>(a.kr) + (int64_t)b * a.r_sb;
-  const float* ks = a.kscale + (int64_t)b * a.s_sb;
+  float* ws = static_cast<float*>(a.ws);
+  const int64_t u_begin = mla_range_begin(w, cta), u_end = mla_range_begin(w, cta + 1);
 
   pdl_trigger();
   pdl_wait();
-  for (int i = threadIdx.x; i < H * R; i += blockDim.x) {
-    qt[i] = ws[w.off_qt / 4 + (int64_t)b * H * R + i];
-    acc[i] = 0.f;
-  }
-  for (int i = threadIdx.x; i < H * DR; i += blockDim.x) qr[i] = ws[w.off_qr / 4 + (int64_t)b * H * DR + i];
-  for (int i = threadIdx.x; i < H; i += blockDim.x) { mrun[i] = -INFINITY; lrun[i] = 0.f; }
-  __syncthreads();
-
-  for (int64_t t0 = t_begin; t0 < t_end; t0 += kTileT) {
-    const int nt = (int)imin64(kTileT, t_end - t0);
-    for (int i = threadIdx.x; i < kTileT * R; i += blockDim.x) {
-      const int t = i / R, r = i % R;
-      cs[i] = t < nt ? ldf(c, (t0 + t) * a.c_st + r) : 0.f;
-    }
-    for (int i = threadIdx.x; i < kTileT * KV * DR; i += blockDim.x) {
-      const int t = i / (KV * DR), rem = i % (KV * DR), g = rem / DR, j = rem % DR;
-      float v = 0.f;
-      if (t < nt) {
-        const T* p = kr + (t0 + t) * a.r_st + (int64_t)g * DR;
-        const int ii = j < half ? j : j - half;
-        float sn, cn;
-        sincosf((float)(t0 + t) * a.inv_freq[ii], &sn, &cn);
-        const float x = a.k_norm_w[DN + j] * ldf(p, j);
-        const float rot = j < half ? -a.k_norm_w[DN + j + half] * ldf(p, j + half)
-                                   : a.k_norm_w[DN + j - half] * ldf(p, j - half);
-        v = x * cn + rot * sn;
-      }
-      z[i] = v;
-    }
-    for (int i = threadIdx.x; i < kTileT * KV; i += blockDim.x) {
-      const int t = i / KV, g = i % KV;
-      st[i] = t < nt ? ks[(t0 + t) * a.s_st + g] : 0.f;
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < H * kTileT; i += blockDim.x) {
-      const int h = i / kTileT, t = i % kTileT, g = h / hpg;
-      float v = -INFINITY;
-      if (t < nt) {
-        float d0 = 0.f;
-        for (int r = 0; r < R; ++r) d0 = fmaf(qt[h * R + r], cs[t * R + r], d0);
-        for (int j = 0; j < DR; ++j) d0 = fmaf(qr[h * DR + j], z[(t * KV + g) * DR + j], d0);
-        v = d0 * st[t * KV + g] * a.scale;
-      }
-      sc[i] = v;
-    }
-    __syncthreads();
-    for (int h = threadIdx.x; h < H; h += blockDim.x) {
-      float mx = mrun[h];
-      for (int t = 0; t < nt; ++t) mx = fmaxf(mx, sc[h * kTileT + t]);
-      const float al = expf(mrun[h] - mx);
-      float sum = 0.f;
-      for (int t = 0; t < kTileT; ++t) {
-        const float p = t < nt ? expf(sc[h * kTileT + t] - mx) : 0.f;
-        sc[h * kTileT + t] = p;
-        sum += p;
-      }
-      lrun[h] = lrun[h] * al + sum;
-      mrun[h] = mx;
-      alpha[h] = al;
-    }
-    __syncthreads();
+  int64_t u = u_begin;
+  while (u < u_end) {
+    const int b = (int)(u / w.ntiles);
+    const int64_t u_stop = imin64(u_end, (int64_t)(b + 1) * w.ntiles);  // units of row b in this range
+    const T* c = static_cast<const T*>(a.c_kv) + (int64_t)b * a.c_sb;
+    const T* kr = static_cast<const T*>(a.kr) + (int64_t)b * a.r_sb;
+    const float* ks = a.kscale + (int64_t)b * a.s_sb;
     for (int i = threadIdx.x; i < H * R; i += blockDim.x) {
-      const int h = i / R, r = i % R;
-      float v = acc[i] * alpha[h];
-      for (int t = 0; t < nt; ++t) v = fmaf(sc[h * kTileT + t], cs[t * R + r], v);
-      acc[i] = v;
+      qt[i] = ws[w.off_qt / 4 + (int64_t)b * H * R + i];
+      acc[i] = 0.f;
     }
+    for (int i = threadIdx.x; i < H * DR; i += blockDim.x) qr[i] = ws[w.off_qr / 4 + (int64_t)b * H * DR + i];
+    for (int i = threadIdx.x; i < H; i += blockDim.x) { mrun[i] = -INFINITY; lrun[i] = 0.f; }
     __syncthreads();
+    const int64_t t_begin = (u - (int64_t)b * w.ntiles) * kMlaUnit;
+    const int64_t t_end = imin64(a.L, (u_stop - (int64_t)b * w.ntiles) * kMlaUnit);
+    for (int64_t t0 = t_begin; t0 < t_end; t0 += kTileT) {
+      const int nt = (int)imin64(kTileT, t_end - t0);
+      for (int i = threadIdx.x; i < kTileT * R; i += blockDim.x) {
+        const int t = i / R, r = i % R;
+        cs[i] = t < nt ? ldf(c, (t0 + t) * a.c_st + r) : 0.f;
+      }
+      for (int i = threadIdx.x; i < kTileT * KV * DR; i += blockDim.x) {
+        const int t = i / (KV * DR), rem = i % (KV * DR), g = rem / DR, j = rem % DR;
+        float v = 0.f;
+        if (t < nt) {
+          const T* p = kr + (t0 + t) * a.r_st + (int64_t)g * DR;
+          const int ii = j < half ? j : j - half;
+          float sn, cn;
+          sincosf((float)(t0 + t) * a.inv_freq[ii], &sn, &cn);
+          const float x = a.k_norm_w[DN + j] * ldf(p, j);
+          const float rot = j < half ? -a.k_norm_w[DN + j + half] * ldf(p, j + half)
+                                     : a.k_norm_w[DN + j - half] * ldf(p, j - half);
+          v = x * cn + rot * sn;
+        }
+        z[i] = v;
+      }
+      for (int i = threadIdx.x; i < kTileT * KV; i += blockDim.x) {
+        const int t = i / KV, g = i % KV;
+        st[i] = t < nt ? ks[(t0 + t) * a.s_st + g] : 0.f;
+      }
+      __syncthreads();
+      for (int i = threadIdx.x; i < H * kTileT; i += blockDim.x) {
+        const int h = i / kTileT, t = i % kTileT, g = h / hpg;
+        float v = -INFINITY;
+        if (t < nt) {
+          float d0 = 0.f;
+          for (int r = 0; r < R; ++r) d0 = fmaf(qt[h * R + r], cs[t * R + r], d0);
+          for (int j = 0; j < DR; ++j) d0 = fmaf(qr[h * DR + j], z[(t * KV + g) * DR + j], d0);
+          v = d0 * st[t * KV + g] * a.scale;
+        }
+        sc[i] = v;
+      }
+      __syncthreads();
+      for (int h = threadIdx.x; h < H; h += blockDim.x) {
+        float mx = mrun[h];
+        for (int t = 0; t < nt; ++t) mx = fmaxf(mx, sc[h * kTileT + t]);
+        const float al = expf(mrun[h] - mx);
+        float sum = 0.f;
+        for (int t = 0; t < kTileT; ++t) {
+          const float p = t < nt ? expf(sc[h * kTileT + t] - mx) : 0.f;
+          sc[h * kTileT + t] = p;
+          sum += p;
+        }
+        lrun[h] = lrun[h] * al + sum;
+        mrun[h] = mx;
+        alpha[h] = al;
+      }
+      __syncthreads();
+      for (int i = threadIdx.x; i < H * R; i += blockDim.x) {
+        const int h = i / R, r = i % R;
+        float v = acc[i] * alpha[h];
+        for (int t = 0; t < nt; ++t) v = fmaf(sc[h * kTileT + t], cs[t * R + r], v);
+        acc[i] = v;
+      }
+      __syncthreads();
+    }
+    const int64_t slot = (int64_t)cta + b;
+    float* pacc = ws + w.off_pacc / 4 + slot * H * R;
+    float* pml = ws + w.off_pml / 4 + slot * H * 2;
+    for (int i = threadIdx.x; i < H * R; i += blockDim.x) pacc[i] = acc[i];
+    for (int h = threadIdx.x; h < H; h += blockDim.x) { pml[2 * h] = mrun[h]; pml[2 * h + 1] = lrun[h]; }
+    __syncthreads();
+    u = u_stop;
   }
-  float* pacc = const_cast<float*>(ws) + w.off_pacc / 4 + (((int64_t)b * w.S + sidx) * H) * R;
-  float* pml = const_cast<float*>(ws) + w.off_pml / 4 + (((int64_t)b * w.S + sidx) * H) * 2;
-  for (int i = threadIdx.x; i < H * R; i += blockDim.x) pacc[i] = acc[i];
-  for (int h = threadIdx.x; h < H; h += blockDim.x) { pml[2 * h] = mrun[h]; pml[2 * h + 1] = lrun[h]; }
 }
 
-// --- combine: merge splits, apply W_uv -------------------------------------
-// grid: (H, B); block 256.
+// --- combine: merge partials, apply W_uv ----------------------------------
+// grid: (H, B); block 256.  Partials of row b: slot i + b for every range i
+// overlapping [b*ntiles, (b+1)*ntiles).
 template <typename T>
 __global__ void __launch_bounds__(kThreads) mla_combine_kernel(const MlaDecodeArgs a, MlaWorkspace w) {
   extern __shared__ float sm[];
   const int H = a.s.H, KV = a.s.KV, D = a.s.D, R = a.s.R;
   const int h = blockIdx.x, b = blockIdx.y, g = h / (H / KV);
-  const int S = w.S;
   float* av = sm;          // [R]
-  float* wgt = sm + R;     // [S]
+  float* wgt = sm + R;     // [G + 1] merge weight per range (0 if not overlapping)
   const float* ws = static_cast<const float*>(a.ws);
-  const float* pml = ws + w.off_pml / 4 + ((int64_t)b * S * H) * 2;
-  const float* pacc = ws + w.off_pacc / 4 + ((int64_t)b * S * H) * R;
+  const float* pml = ws + w.off_pml / 4;
+  const float* pacc = ws + w.off_pacc / 4;
+  const int64_t lo = (int64_t)b * w.ntiles, hi = lo + w.ntiles;
 
   pdl_trigger();
   pdl_wait();
   __shared__ float s_inv_l;
+  __shared__ int s_i0, s_i1;
   if (threadIdx.x == 0) {
+    int i0 = -1, i1 = -1;
+    for (int i = 0; i < w.G; ++i) {
+      const int64_t r0 = mla_range_begin(w, i), r1 = mla_range_begin(w, i + 1);
+      if (r0 < hi && r1 > lo) { if (i0 < 0) i0 = i; i1 = i; }
+    }
     float mx = -INFINITY;
-    for (int s = 0; s < S; ++s) mx = fmaxf(mx, pml[((int64_t)s * H + h) * 2]);
+    for (int i = i0; i <= i1; ++i) mx = fmaxf(mx, pml[(((int64_t)i + b) * H + h) * 2]);
     float l = 0.f;
-    for (int s = 0; s < S; ++s) {
-      const float e = expf(pml[((int64_t)s * H + h) * 2] - mx);
-      wgt[s] = e;
-      l += e * pml[((int64_t)s * H + h) * 2 + 1];
+    for (int i = i0; i <= i1; ++i) {
+      const float* p = pml + (((int64_t)i + b) * H + h) * 2;
+      const float e = expf(p[0] - mx);
+      wgt[i - i0] = e;
+      l += e * p[1];
     }
     s_inv_l = 1.f / l;
+    s_i0 = i0;
+    s_i1 = i1;
   }
   __syncthreads();
+  const int i0 = s_i0, n = s_i1 - s_i0 + 1;
   for (int r = threadIdx.x; r < R; r += blockDim.x) {
     float v = 0.f;
-    for (int s = 0; s < S; ++s) v = fmaf(wgt[s], pacc[((int64_t)s * H + h) * R + r], v);
+    for (int k = 0; k < n; ++k) v = fmaf(wgt[k], pacc[(((int64_t)i0 + k + b) * H + h) * R + r], v);
     av[r] = v * s_inv_l;
   }
   __syncthreads();
@@ -294,17 +315,18 @@ int launch_smem(K kern, dim3 grid, size_t smem, cudaStream_t st, Args... args) {
 
 template <typename T>
 int decode_t(const MlaDecodeArgs& a) {
-  const MlaWorkspace w = mla_plan(a.s, a.L);
+  const bool fast = !g_force_generic.load(std::memory_order_relaxed) && mla_fast_supported(a);
+  const MlaWorkspace w = mla_plan(a.s, a.L, fast);
   const int B = a.s.B, H = a.s.H;
   int st = launch_smem(mla_absorb_kernel<T>, dim3(H, B), sizeof(float) * a.s.D, a.stream, a, w);
   if (st) return st;
-  if (!g_force_generic.load(std::memory_order_relaxed) && mla_fast_supported(a)) {
+  if (fast) {
     st = mla_fast_split_launch(a, w);
   } else {
-    st = launch_smem(mla_split_kernel<T>, dim3(w.S, B), split_smem_bytes(a.s), a.stream, a, w);
+    st = launch_smem(mla_split_kernel<T>, dim3(w.G), split_smem_bytes(a.s), a.stream, a, w);
   }
   if (st) return st;
-  return launch_smem(mla_combine_kernel<T>, dim3(H, B), sizeof(float) * (a.s.R + w.S), a.stream, a, w);
+  return launch_smem(mla_combine_kernel<T>, dim3(H, B), sizeof(float) * (a.s.R + w.G + 1), a.stream, a, w);
 }
 
 template <typename T>
@@ -327,30 +349,28 @@ int mla_validate_shape(const b200mm_mla_shape& s) {
   return B200MM_OK;
 }
 
-MlaWorkspace mla_plan(const b200mm_mla_shape& s, int64_t L) {
+MlaWorkspace mla_plan(const b200mm_mla_shape& s, int64_t L, bool fast) {
   MlaWorkspace w{};
   const int B = s.B > 0 ? s.B : 1;
-  // Enough splits for ~2 CTAs per SM in total, chunks of >= 64 tokens.
-  const int target = 2 * num_sms(current_device());
-  int64_t S = (target + B - 1) / B;
-  const int64_t max_s = (L + 63) / 64;
-  if (S > max_s) S = max_s;
-  if (S < 1) S = 1;
-  int64_t chunk = (L + S - 1) / S;
-  chunk = (chunk + 63) / 64 * 64;
-  S = (L + chunk - 1) / chunk;
-  w.S = (int)S;
-  w.chunk = chunk;
+  w.ntiles = (L + kMlaUnit - 1) / kMlaUnit;
+  w.T = (int64_t)B * w.ntiles;
+  const int64_t want = fast ? mla_fast_ctas() : 2 * num_sms(current_device());
+  w.G = (int)(want < w.T ? want : w.T);
   const size_t BH = (size_t)B * s.H;
+  const size_t slots = (size_t)w.G + B;
   w.off_qt = 0;
   w.off_qr = align256(w.off_qt + sizeof(float) * BH * s.R);
   w.off_pacc = align256(w.off_qr + sizeof(float) * BH * (s.DR > 0 ? s.DR : 1));
-  w.off_pml = align256(w.off_pacc + sizeof(float) * BH * S * s.R);
-  w.total = align256(w.off_pml + sizeof(float) * BH * S * 2);
+  w.off_pml = align256(w.off_pacc + sizeof(float) * slots * s.H * s.R);
+  w.off_err = align256(w.off_pml + sizeof(float) * slots * s.H * 2);
+  w.total = align256(w.off_err + 16);
   return w;
 }
 
-size_t mla_workspace_bytes(const b200mm_mla_shape& s, int64_t L) { return mla_plan(s, L).total; }
+size_t mla_workspace_bytes(const b200mm_mla_shape& s, int64_t L) {
+  const size_t a = mla_plan(s, L, true).total, b = mla_plan(s, L, false).total;
+  return a > b ? a : b;
+}
 
 int mla_scales_launch(const MlaScalesArgs& a) {
   if (a.s.dtype == B200MM_BF16) return scales_t<__nv_bfloat16>(a);

@@ -29,25 +29,41 @@ struct MlaDecodeArgs {
   cudaStream_t stream;
 };
 
-// Workspace (fp32, every region 256-byte aligned):
-//   qt   [B, H, R]        absorbed no-RoPE query  W_uk^T (w_k[:DN] * q[:DN])
-//   qr   [B, H, DR]       RoPE'd query rope half at position L-1
-//   pacc [B, S, H, R]     per-split sum_t p_t c_t (p relative to the split max)
-//   pml  [B, S, H, 2]     per-split (max score, sum p)
+// Work plan shared by the split kernels and the combine kernel.
+// The flattened (batch row, 64-token tile) sequence of T = B * ntiles units
+// is cut into G contiguous ranges, range i = [floor(i*T/G), floor((i+1)*T/G)),
+// one per CTA of the split kernel.  A CTA writes one partial per batch row
+// its range touches, into slot (i + b); batch row b's partials are the slots
+// i + b of every range i that overlaps it (so at most G + B slots exist).
+//
+// Workspace (every region 256-byte aligned):
+//   qt   fp32 [B, H, R]        absorbed no-RoPE query  W_uk^T (w_k[:DN] * q[:DN])
+//   qr   fp32 [B, H, DR]       RoPE'd query rope half at position L-1
+//   pacc fp32 [G+B, H, R]      per-partial sum_t p_t c_t (p relative to the partial max)
+//   pml  fp32 [G+B, H, 2]      per-partial (max score, sum p)
+//   err  int32[4]              error flag of bounded waits (0 = ok)
+constexpr int kMlaUnit = 64;  // tokens per work unit
+
 struct MlaWorkspace {
-  int S;                  // context splits per batch row
-  int64_t chunk;          // tokens per split (the last split may be shorter)
-  size_t off_qt, off_qr, off_pacc, off_pml, total;
+  int G;                  // split CTAs (work ranges)
+  int64_t ntiles;         // 64-token units per batch row
+  int64_t T;              // B * ntiles
+  size_t off_qt, off_qr, off_pacc, off_pml, off_err, total;
 };
 
+__host__ __device__ inline int64_t mla_range_begin(const MlaWorkspace& w, int i) {
+  return (int64_t)i * w.T / w.G;
+}
+
 int mla_validate_shape(const b200mm_mla_shape& s);
-MlaWorkspace mla_plan(const b200mm_mla_shape& s, int64_t L);
+MlaWorkspace mla_plan(const b200mm_mla_shape& s, int64_t L, bool fast);
 size_t mla_workspace_bytes(const b200mm_mla_shape& s, int64_t L);
 int mla_scales_launch(const MlaScalesArgs& a);
 int mla_decode_launch(const MlaDecodeArgs& a);
 
 // production-shape split kernel (R=256, D=128, DR=32, H=32, KV=8, 16-bit dtype)
 bool mla_fast_supported(const MlaDecodeArgs& a);
+int mla_fast_ctas();                   // G for the production-shape kernel
 int mla_fast_split_launch(const MlaDecodeArgs& a, const MlaWorkspace& w);
 
 }  // namespace b200mm
