@@ -13,7 +13,7 @@ from pathlib import Path
 
 import torch
 
-LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libb200mm.so"
+LIB_PATH = Path(os.environ.get("B200MM_LIB", Path(__file__).resolve().parent / "_lib" / "libb200mm.so"))
 
 B200MM_OK = 0
 DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}

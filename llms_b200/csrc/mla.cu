@@ -104,12 +104,15 @@ __global__ void __launch_bounds__(kThreads) mla_absorb_kernel(const MlaDecodeArg
 
   pdl_trigger();
   pdl_wait();
+  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0)
+    *reinterpret_cast<int*>(static_cast<unsigned char*>(a.ws) + w.off_err) = 0;
   for (int d = threadIdx.x; d < D; d += blockDim.x) qn[d] = ldf(q, d);
   __syncthreads();
   // qt[r] = sum_i W_uk[g, i, r] * w_k[i] * q[i]
   const T* wuk = static_cast<const T*>(a.w_uk) + (int64_t)g * DN * R;
   for (int r = threadIdx.x; r < R; r += blockDim.x) {
     float acc = 0.f;
+#pragma unroll 8
     for (int i = 0; i < DN; ++i) acc = fmaf(ldf(wuk, (int64_t)i * R + r), a.k_norm_w[i] * qn[i], acc);
     qt[r] = acc;
   }
@@ -258,42 +261,54 @@ __global__ void __launch_bounds__(kThreads) mla_combine_kernel(const MlaDecodeAr
   pdl_trigger();
   pdl_wait();
   __shared__ float s_inv_l;
-  __shared__ int s_i0, s_i1;
-  if (threadIdx.x == 0) {
-    int i0 = -1, i1 = -1;
-    for (int i = 0; i < w.G; ++i) {
-      const int64_t r0 = mla_range_begin(w, i), r1 = mla_range_begin(w, i + 1);
-      if (r0 < hi && r1 > lo) { if (i0 < 0) i0 = i; i1 = i; }
-    }
+  // ranges overlapping [lo, hi): range i holds units [floor(i*T/G), floor((i+1)*T/G))
+  const int i0 = (int)(((lo + 1) * w.G - 1) / w.T);
+  const int i1 = (int)((hi * w.G - 1) / w.T);
+  const int n = i1 - i0 + 1;
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
     float mx = -INFINITY;
-    for (int i = i0; i <= i1; ++i) mx = fmaxf(mx, pml[(((int64_t)i + b) * H + h) * 2]);
+    for (int k = lane; k < n; k += 32) mx = fmaxf(mx, pml[(((int64_t)i0 + k + b) * H + h) * 2]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float l = 0.f;
-    for (int i = i0; i <= i1; ++i) {
-      const float* p = pml + (((int64_t)i + b) * H + h) * 2;
+    for (int k = lane; k < n; k += 32) {
+      const float* p = pml + (((int64_t)i0 + k + b) * H + h) * 2;
       const float e = expf(p[0] - mx);
-      wgt[i - i0] = e;
+      wgt[k] = e;
       l += e * p[1];
     }
-    s_inv_l = 1.f / l;
-    s_i0 = i0;
-    s_i1 = i1;
+    l = warp_sum(l);
+    if (lane == 0) s_inv_l = 1.f / l;
   }
   __syncthreads();
-  const int i0 = s_i0, n = s_i1 - s_i0 + 1;
   for (int r = threadIdx.x; r < R; r += blockDim.x) {
-    float v = 0.f;
-    for (int k = 0; k < n; ++k) v = fmaf(wgt[k], pacc[(((int64_t)i0 + k + b) * H + h) * R + r], v);
-    av[r] = v * s_inv_l;
+    float v0 = 0.f, v1 = 0.f, v2 = 0.f, v3 = 0.f;
+    const float* pc = pacc + (((int64_t)i0 + b) * H + h) * R + r;
+    const int64_t step = (int64_t)H * R;
+    int k = 0;
+    for (; k + 4 <= n; k += 4) {
+      const float p0 = pc[(k + 0) * step], p1 = pc[(k + 1) * step];
+      const float p2 = pc[(k + 2) * step], p3 = pc[(k + 3) * step];
+      v0 = fmaf(wgt[k], p0, v0);
+      v1 = fmaf(wgt[k + 1], p1, v1);
+      v2 = fmaf(wgt[k + 2], p2, v2);
+      v3 = fmaf(wgt[k + 3], p3, v3);
+    }
+    for (; k < n; ++k) v0 = fmaf(wgt[k], pc[k * step], v0);
+    av[r] = ((v0 + v1) + (v2 + v3)) * s_inv_l;
   }
   __syncthreads();
   const T* wuv = static_cast<const T*>(a.w_uv) + (int64_t)g * D * R;
   T* out = static_cast<T*>(a.out) + (int64_t)b * a.o_sb + (int64_t)h * D;
+  // a split kernel that gave up on a bounded wait leaves NaN, never a silent result
+  const bool failed = *reinterpret_cast<const int*>(static_cast<const unsigned char*>(a.ws) + w.off_err) != 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   for (int d = warp; d < D; d += nw) {
     float v = 0.f;
     for (int r = lane; r < R; r += 32) v = fmaf(ldf(wuv, (int64_t)d * R + r), av[r], v);
     v = warp_sum(v);
-    if (lane == 0) out[d] = from_f<T>(v);
+    if (lane == 0) out[d] = from_f<T>(failed ? __int_as_float(0x7fc00000) : v);
   }
 }
 
@@ -315,13 +330,15 @@ int launch_smem(K kern, dim3 grid, size_t smem, cudaStream_t st, Args... args) {
 
 template <typename T>
 int decode_t(const MlaDecodeArgs& a) {
-  const bool fast = !g_force_generic.load(std::memory_order_relaxed) && mla_fast_supported(a);
+  MlaMaps maps;
+  const bool fast =
+      !g_force_generic.load(std::memory_order_relaxed) && mla_fast_supported(a) && mla_fast_maps(a, &maps);
   const MlaWorkspace w = mla_plan(a.s, a.L, fast);
   const int B = a.s.B, H = a.s.H;
   int st = launch_smem(mla_absorb_kernel<T>, dim3(H, B), sizeof(float) * a.s.D, a.stream, a, w);
   if (st) return st;
   if (fast) {
-    st = mla_fast_split_launch(a, w);
+    st = mla_fast_split_launch(a, w, maps);
   } else {
     st = launch_smem(mla_split_kernel<T>, dim3(w.G), split_smem_bytes(a.s), a.stream, a, w);
   }

@@ -1,7 +1,7 @@
 // MLA latent-KV decode: argument blocks, workspace layout and kernel entry
 // points shared between the generic and the production-shape kernels.
 #pragma once
-#include "common.cuh"
+#include "tma.cuh"
 
 namespace b200mm {
 
@@ -62,8 +62,12 @@ int mla_scales_launch(const MlaScalesArgs& a);
 int mla_decode_launch(const MlaDecodeArgs& a);
 
 // production-shape split kernel (R=256, D=128, DR=32, H=32, KV=8, 16-bit dtype)
+struct MlaMaps {
+  CUtensorMap c, kr, ks;  // TMA maps of c_kv, k_rope_pre and the k-RMS side-band (token extent = L)
+};
 bool mla_fast_supported(const MlaDecodeArgs& a);
+bool mla_fast_maps(const MlaDecodeArgs& a, MlaMaps* maps);  // false if the driver rejects a map
 int mla_fast_ctas();                   // G for the production-shape kernel
-int mla_fast_split_launch(const MlaDecodeArgs& a, const MlaWorkspace& w);
+int mla_fast_split_launch(const MlaDecodeArgs& a, const MlaWorkspace& w, const MlaMaps& maps);
 
 }  // namespace b200mm

@@ -1,8 +1,334 @@
-// Large-M projection kernel on tcgen05 tensor cores (placeholder: declines
-// every call until the tensor-core path lands).
+// Large-M projection kernel on 5th-generation tensor cores (tcgen05).
+//
+//   Y[M, N] = X[M, K] . W[N, K]^T            (fused QKV: W = [Wq; Wk; Wv])
+//   Y[M, N] = silu(X Wg^T) * (X Wu^T)        (fused gate-up-SiLU)
+//
+// One CTA per 128 x BN output tile (BN x 2 for gate-up), 6 warps:
+//   warp 0      TMA producer: X box [64 k x 128 rows], W box(es) [64 k x BN
+//               rows], 128-byte swizzle, into a STAGES-deep ring guarded by
+//               full/empty mbarriers;
+//   warp 1      allocates TMEM, one thread issues tcgen05.mma (kind::f16,
+//               M = 128, N = BN, K = 16 per instruction, fp32 accumulator in
+//               TMEM) and frees each stage with tcgen05.commit;
+//   warps 2-5   epilogue: tcgen05.ld of the accumulator (each warp reads its
+//               32-lane quadrant), SiLU * up in registers for gate-up, one
+//               rounding to the output dtype, 16-byte stores.
+// Every mbarrier wait is bounded; a CTA whose wait expires stops issuing,
+// drains its own copies in flight, frees TMEM and writes NaN over its tile.
 #include "dense.cuh"
+#include "tma.cuh"
 
 namespace b200mm {
-bool tc_supported(const DenseArgs&) { return false; }
-int tc_launch(const DenseArgs&) { return B200MM_ERR_SHAPE; }
+
+namespace {
+
+constexpr int BM = 128;  // tile rows (X rows) = MMA M = TMEM lanes
+constexpr int BK = 64;   // K per stage: 128 bytes of 16-bit elements (one swizzle span)
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 256;
+
+template <bool GATE, int BN>
+struct Cfg {
+  static constexpr int NB = GATE ? 2 : 1;                // W tiles per stage
+  static constexpr uint32_t A_BYTES = BM * BK * 2;       // 16 KB
+  static constexpr uint32_t B_BYTES = BN * BK * 2;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + NB * B_BYTES;
+  static constexpr int STAGES = (200 * 1024 / STAGE_BYTES) > 8 ? 8 : (200 * 1024 / STAGE_BYTES);
+  static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static_assert(NB * BN <= (int)kTmemCols, "accumulators exceed the TMEM allocation");
+  static_assert(BN % 32 == 0 && BN >= 32 && NB * BN <= 256, "MMA N = NB * BN must be a multiple of 32 in [32, 256]");
+  static_assert(B_BYTES % 1024 == 0, "W boxes must keep the 1024-byte swizzle-atom alignment");
+};
+
+struct TcParams {
+  int M, N, K;
+  void* y;
+  int64_t ldy;
+};
+
+// UMMA shared-memory descriptor: K-major operand in the 128-byte swizzle,
+// 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);  // start address
+  d |= (uint64_t)1 << 16;                          // leading byte offset (unused when swizzled)
+  d |= (uint64_t)(1024 >> 4) << 32;                // stride byte offset: 8 rows x 128 B
+  d |= (uint64_t)1 << 46;                          // descriptor version for sm_100
+  d |= (uint64_t)2 << 61;                          // layout: SWIZZLE_128B
+  return d;
+}
+
+template <typename T> constexpr uint32_t ab_format();
+template <> constexpr uint32_t ab_format<__nv_bfloat16>() { return 1; }
+template <> constexpr uint32_t ab_format<__half>() { return 0; }
+
+// kind::f16 instruction descriptor: fp32 accumulate, A/B K-major, M x N.
+template <typename T, int N>
+constexpr uint32_t idesc() {
+  return (1u << 4) | (ab_format<T>() << 7) | (ab_format<T>() << 10) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+          tmem_d),
+      "l"(a), "l"(b), "r"(id), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(void* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <typename T> __device__ __forceinline__ uint32_t pack_out(float a, float b);
+template <> __device__ __forceinline__ uint32_t pack_out<__nv_bfloat16>(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <> __device__ __forceinline__ uint32_t pack_out<__half>(float a, float b) {
+  __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <typename T, bool GATE, int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap mx, const __grid_constant__ CUtensorMap mw0,
+                   const __grid_constant__ CUtensorMap mw1, const TcParams p) {
+  using C = Cfg<GATE, BN>;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                       ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* accum = empty + C::STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  volatile int* failed = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* issued = const_cast<int*>(failed) + 1;
+  int* consumed = issued + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // m-tiles vary fastest: a wave covers all of X against a narrow band of W,
+  // so each weight row leaves HBM once and X stays in L2
+  const int tile_m = blockIdx.x, tile_n = blockIdx.y;
+  const int nk = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    *failed = 0;
+    *issued = 0;
+    *consumed = 0;
+    mbar_init_fence();
+    prefetch_map(&mx);
+    prefetch_map(&mw0);
+    if (GATE) prefetch_map(&mw1);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  pdl_trigger();
+  pdl_wait();  // X may be the output of the previous kernel
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int kb = 0;
+      for (; kb < nk; ++kb) {
+        const int s = kb % C::STAGES, it = kb / C::STAGES;
+        if (kb >= C::STAGES && !mbar_wait(&empty[s], (uint32_t)((it - 1) & 1))) {
+          *failed = 1;
+          break;
+        }
+        if (*failed) break;
+        unsigned char* st = sm + s * C::STAGE_BYTES;
+        mbar_expect_tx(&full[s], C::STAGE_BYTES);
+        tma_load_2d(st, &mx, kb * BK, tile_m * BM, &full[s]);
+        tma_load_2d(st + C::A_BYTES, &mw0, kb * BK, tile_n * BN, &full[s]);
+        if (GATE) tma_load_2d(st + C::A_BYTES + C::B_BYTES, &mw1, kb * BK, tile_n * BN, &full[s]);
+      }
+      *issued = kb;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // gate-up: the Wg and Wu boxes are adjacent in shared memory, so one
+      // N = 2*BN instruction reads A once and fills [gate | up] accumulators
+      constexpr uint32_t ID = idesc<T, GATE ? 2 * BN : BN>();
+      int kb = 0;
+      for (; kb < nk; ++kb) {
+        const int s = kb % C::STAGES, it = kb / C::STAGES;
+        if (!mbar_wait(&full[s], (uint32_t)(it & 1))) {
+          *failed = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t st = smem_u32(sm + s * C::STAGE_BYTES);
+        const uint64_t a = sdesc(st), b = sdesc(st + C::A_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          // +32 bytes of K per instruction inside the 128-byte swizzle span
+          mma_f16(tmem, a + 2 * kk, b + 2 * kk, ID, (kb | kk) != 0);
+        }
+        mma_commit(&empty[s]);
+      }
+      *consumed = kb;
+      mma_commit(accum);  // fires once every MMA issued above has completed
+    }
+  } else {
+    // epilogue: warps 2..5 -> TMEM lane quadrant warp % 4
+    const bool ok = mbar_wait(accum, 0);
+    tc_fence_after();
+    const bool bad = !ok || *failed;
+    const int q = warp & 3;
+    const int row = tile_m * BM + 32 * q + lane;
+    const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16);
+    T* yrow = static_cast<T*>(p.y) + (int64_t)row * p.ldy;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      float v[32];
+      tmem_ld32(tq + c, v);
+      if (GATE) {
+        float u[32];
+        tmem_ld32(tq + BN + c, u);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = silu_mul(v[i], u[i]);
+      }
+      if (bad) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __int_as_float(0x7fc00000);
+      }
+      if (row < p.M) {
+        const int n0 = tile_n * BN + c;
+        if (n0 + 32 <= p.N) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint4 o;
+            o.x = pack_out<T>(v[8 * j + 0], v[8 * j + 1]);
+            o.y = pack_out<T>(v[8 * j + 2], v[8 * j + 3]);
+            o.z = pack_out<T>(v[8 * j + 4], v[8 * j + 5]);
+            o.w = pack_out<T>(v[8 * j + 6], v[8 * j + 7]);
+            *reinterpret_cast<uint4*>(yrow + n0 + 8 * j) = o;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (n0 + i < p.N) yrow[n0 + i] = from_f<T>(v[i]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && *failed) {
+    // copies issued but never consumed still target this CTA's shared memory
+    for (int kb = *consumed; kb < *issued; ++kb)
+      mbar_wait(&full[kb % C::STAGES], (uint32_t)((kb / C::STAGES) & 1));
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+inline bool al16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+template <typename T>
+constexpr CUtensorMapDataType map_dtype() {
+  return sizeof(T) == 2 && ab_format<T>() == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+template <typename T, bool GATE, int BN>
+int launch_bn(const DenseArgs& a) {
+  using C = Cfg<GATE, BN>;
+  CUtensorMap mx, mw0, mw1;
+  const CUtensorMapDataType dt = map_dtype<T>();
+  if (!make_map_2d(&mx, dt, a.x, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.ldx * 2, BK, BM,
+                   CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map_2d(&mw0, dt, a.w0, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)a.ldw0 * 2, BK, BN,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+    return B200MM_ERR_ALIGN;
+  if (GATE) {
+    if (!make_map_2d(&mw1, dt, a.w1, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)a.ldw1 * 2, BK, BN,
+                     CU_TENSOR_MAP_SWIZZLE_128B))
+      return B200MM_ERR_ALIGN;
+  } else {
+    mw1 = mw0;
+  }
+  auto kern = tc_gemm_kernel<T, GATE, BN>;
+  static bool configured[64] = {false};
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) return B200MM_ERR_DEVICE;
+  if (!configured[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM) != cudaSuccess)
+      return B200MM_ERR_LAUNCH;
+    configured[dev] = true;
+  }
+  TcParams p{a.M, a.N, a.K, a.y, a.ldy};
+  dim3 grid((a.M + BM - 1) / BM, (a.N + BN - 1) / BN);
+  if (grid.x > 2147483647u || grid.y > 65535u) return B200MM_ERR_SHAPE;
+  return launch_pdl(kern, grid, dim3(kThreads), C::SMEM, a.stream, mx, mw0, mw1, p) == cudaSuccess
+             ? B200MM_OK
+             : B200MM_ERR_LAUNCH;
+}
+
+// N tile: the widest whose grid still gives every SM a tile.
+template <typename T>
+int launch_t(const DenseArgs& a) {
+  const int sms = num_sms(current_device());
+  const long mt = (a.M + BM - 1) / BM;
+  auto tiles = [&](int bn) { return mt * ((a.N + bn - 1) / bn); };
+  if (a.gate) {
+    if (tiles(128) >= sms) return launch_bn<T, true, 128>(a);
+    return launch_bn<T, true, 64>(a);
+  }
+  if (tiles(256) >= sms) return launch_bn<T, false, 256>(a);
+  if (tiles(128) >= sms) return launch_bn<T, false, 128>(a);
+  return launch_bn<T, false, 64>(a);
+}
+
+}  // namespace
+
+bool tc_supported(const DenseArgs& a) {
+  if (a.w8 || (a.dtype != B200MM_BF16 && a.dtype != B200MM_F16)) return false;
+  if (a.M < 128) return false;
+  if (!al16(a.x) || !al16(a.w0) || !al16(a.y) || (a.gate && !al16(a.w1))) return false;
+  if ((a.ldx * 2) % 16 || (a.ldw0 * 2) % 16 || (a.ldy * 2) % 16 || (a.gate && (a.ldw1 * 2) % 16)) return false;
+  if ((a.K * 2) % 16) return false;
+  return true;
+}
+
+int tc_launch(const DenseArgs& a) {
+  if (a.dtype == B200MM_BF16) return launch_t<__nv_bfloat16>(a);
+  return launch_t<__half>(a);
+}
+
 }  // namespace b200mm
