@@ -196,6 +196,40 @@ int b200mm_mla_decode(const b200mm_mla_shape* shape,
                       void* workspace, size_t workspace_bytes,
                       void* stream);
 
+/*
+ * b200mm_mla_decode_noalloc -- no counterpart in the reference.
+ *
+ * b200mm_mla_decode for callers that cannot allocate device memory at decode
+ * time (a server drawing on a fixed arena reserved at start-up, a replayed
+ * CUDA graph whose allocations must not change, a plugin whose host framework
+ * owns every allocation): same arguments minus the workspace, same kernels,
+ * same results.  The workspace comes from one array compiled into the library
+ * (8 MiB, 256-byte aligned; B = 32, L = 32768 at the Qwen3-4B MLA shape needs
+ * about 7.1 MiB).  Every GPU that loads the library holds that array until the
+ * process exits.
+ *   - A call whose workspace would exceed 8 MiB returns B200MM_ERR_WORKSPACE
+ *     and launches nothing (b200mm_mla_decode_workspace_size gives the need).
+ *   - The first call on a device looks up the array's device address on that
+ *     device (cudaGetSymbolAddress, the device current at the call); make that
+ *     first call before any stream capture.
+ *   - The array is shared by every call and keeps the last call's contents:
+ *     two calls that can overlap on the GPU (different streams, or different
+ *     host threads without ordering) race on it.  Calls on one stream are
+ *     ordered and safe.  Nothing in it needs to start zeroed: the kernels write
+ *     each byte they later read.
+ *   - Calls no cudaMalloc / cudaFree or any allocating routine.
+ */
+int b200mm_mla_decode_noalloc(const b200mm_mla_shape* shape,
+                              const void* q, int64_t q_sb,
+                              const void* c_kv, int64_t c_sb, int64_t c_st,
+                              const void* k_rope_pre, int64_t r_sb, int64_t r_st,
+                              const float* kscale, int64_t s_sb, int64_t s_st,
+                              const void* w_uk, const void* w_uv,
+                              const float* k_norm_w, const float* rope_inv_freq,
+                              float scale, int64_t L,
+                              void* out, int64_t o_sb,
+                              void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -71,6 +71,11 @@ SIGNATURES: dict[str, tuple] = {
          _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, ctypes.c_float, _c_i64, _c_p, _c_i64,
          _c_p, ctypes.c_size_t, _c_p],
     ),
+    "b200mm_mla_decode_noalloc": (
+        ctypes.c_int,
+        [ctypes.POINTER(MlaShape), _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64,
+         _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, ctypes.c_float, _c_i64, _c_p, _c_i64, _c_p],
+    ),
 }
 
 
