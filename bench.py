@@ -54,7 +54,62 @@ def parse_args():
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--no-suite", action="store_true", help="skip the per-op sub-metrics")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
+    p.add_argument("--profile-op", choices=["qkv", "gate_up", "qkv_w8", "gate_up_w8", "mla"],
+                   help="run one op 3 times and exit (a small driver for ncu captures)")
+    p.add_argument("--M", type=int, default=1, help="--profile-op: rows of x")
+    p.add_argument("--B", type=int, default=32, help="--profile-op mla: batch")
+    p.add_argument("--L", type=int, default=4096, help="--profile-op mla: context")
     return p.parse_args()
+
+
+def profile_op(args):
+    """Three calls of one hot-path op at a BASELINE shape, for ncu: the first
+    two warm, the third is the one to capture (-s 2 -c 1)."""
+    from llms_b200 import mla
+    from llms_b200.kernels import int8_fused_gate_up_silu, int8_fused_qkv, triton_fused_gate_up_silu, triton_fused_qkv
+
+    torch.cuda.set_device(0)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    bf = dict(device="cuda", dtype=torch.bfloat16, generator=g)
+    if args.profile_op == "mla":
+        B, L, H, KV, D, DR, R = args.B, args.L, 32, 8, 128, 32, 256
+        c = torch.randn(B, L, R, **bf)
+        kr = torch.randn(B, L, KV, DR, **bf)
+        wuk = torch.randn(KV, D - DR, R, **bf) * 0.25
+        wuv = torch.randn(KV, D, R, **bf) * 0.25
+        q = torch.randn(B, H, D, **bf)
+        ks = torch.empty(B, L, KV, device="cuda")
+        mla.mla_kv_scales(c, kr, wuk, ks, B=B, t0=0, t1=L, num_kv_heads=KV, head_dim=D, eps=1e-6)
+        kw, inv = torch.ones(D, device="cuda"), mla.rope_inv_freq(D, DR, 1e6, "cuda")
+        fn = lambda: mla.mla_decode(q, c, kr, ks, wuk, wuv, kw, inv, L=L, scale=D ** -0.5, eps=1e-6)
+    else:
+        M = args.M
+        w8 = args.profile_op.endswith("_w8")
+        K = 4096 if w8 else HIDDEN
+        x = torch.randn(M, K, **bf)
+        if args.profile_op.startswith("gate_up"):
+            N = 12288 if w8 else INTER
+            if w8:
+                qg = torch.randint(-127, 128, (N, K), device="cuda", dtype=torch.int8, generator=g)
+                qu = torch.randint(-127, 128, (N, K), device="cuda", dtype=torch.int8, generator=g)
+                sg = torch.rand(N, device="cuda", generator=g) * 9e-4 + 1e-4
+                su = torch.rand(N, device="cuda", generator=g) * 9e-4 + 1e-4
+                fn = lambda: int8_fused_gate_up_silu(x, qg, sg, qu, su)
+            else:
+                wg, wu = torch.randn(N, K, **bf) * 0.02, torch.randn(N, K, **bf) * 0.02
+                fn = lambda: triton_fused_gate_up_silu(x, wg, wu)
+        else:
+            if w8:
+                wq = torch.randint(-127, 128, (NQ + 2 * NK, K), device="cuda", dtype=torch.int8, generator=g)
+                sq = torch.rand(NQ + 2 * NK, device="cuda", generator=g) * 9e-4 + 1e-4
+                fn = lambda: int8_fused_qkv(x, wq, sq, n_q=NQ, n_k=NK)
+            else:
+                w = torch.randn(NQ + 2 * NK, K, **bf) * 0.02
+                fn = lambda: triton_fused_qkv(x, w, n_q=NQ, n_k=NK)
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_op": args.profile_op, "ok": True}))
 
 
 # ---------------------------------------------------------------------------
@@ -259,12 +314,14 @@ def time_graph(graph, steps, warmup, world, post=None):
     barrier(world)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")  # lets ncu --nvtx-include timed/ select the timed region
     e0.record()
     for _ in range(steps):
         graph.replay()
         if post:
             post()
     e1.record()
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
@@ -300,31 +357,71 @@ def suite(job):
         per = sec / (20 * job.layers)
         out[name] = {"us_per_launch": per * 1e6, "GB/s": b / per / 1e9}
         del g
-    # M = 2048 TFLOP/s (one layer's weights; inputs 10+ MB, weights rotate over 4 layers)
-    for name, n_rows, gate in (("qkv_m2048", NQ + 2 * NK, False), ("gate_up_m2048", INTER, True)):
-        M = 2048
-        x = torch.randn(M, HIDDEN, device="cuda", dtype=torch.bfloat16)
-        y = torch.empty(M, n_rows, device="cuda", dtype=torch.bfloat16)
-        layers = range(4)
+    # other M: GB/s (HBM-bound, M <= 128) or TFLOP/s (M = 2048); weights rotate over 4 layers
+    for M in (4, 16, 128, 2048):
+        for name, n_rows, gate in (("qkv", NQ + 2 * NK, False), ("gate_up", INTER, True)):
+            x = torch.randn(M, HIDDEN, device="cuda", dtype=torch.bfloat16)
+            y = torch.empty(M, n_rows, device="cuda", dtype=torch.bfloat16)
+            layers = range(4)
 
-        def run():
-            s = torch.cuda.current_stream().cuda_stream
-            for i in layers:
-                if gate:
-                    st = _capi.lib.b200mm_gate_up_silu(x.data_ptr(), HIDDEN, job.wg[i].data_ptr(), HIDDEN,
-                                                       job.wu[i].data_ptr(), HIDDEN, y.data_ptr(), n_rows,
-                                                       M, n_rows, HIDDEN, 2, s)
-                else:
-                    st = _capi.lib.b200mm_qkv(x.data_ptr(), HIDDEN, job.wqkv[i].data_ptr(), HIDDEN,
-                                              y.data_ptr(), n_rows, M, n_rows, HIDDEN, 2, s)
-                _capi.check(st, name)
+            def run(x=x, y=y, n_rows=n_rows, gate=gate, M=M):
+                s = torch.cuda.current_stream().cuda_stream
+                for i in layers:
+                    if gate:
+                        st = _capi.lib.b200mm_gate_up_silu(x.data_ptr(), HIDDEN, job.wg[i].data_ptr(), HIDDEN,
+                                                           job.wu[i].data_ptr(), HIDDEN, y.data_ptr(), n_rows,
+                                                           M, n_rows, HIDDEN, 2, s)
+                    else:
+                        st = _capi.lib.b200mm_qkv(x.data_ptr(), HIDDEN, job.wqkv[i].data_ptr(), HIDDEN,
+                                                  y.data_ptr(), n_rows, M, n_rows, HIDDEN, 2, s)
+                    _capi.check(st, name)
 
-        g, _ = job.capture(run)
-        sec = time_graph(g, 5, 2, 1)
-        per = sec / (5 * len(layers))
-        flops = 2 * M * HIDDEN * (2 * n_rows if gate else n_rows)
-        out[name] = {"us_per_launch": per * 1e6, "TFLOP/s": flops / per / 1e12}
-        del g, x, y
+            g, _ = job.capture(run)
+            reps = 5 if M == 2048 else 20
+            sec = time_graph(g, reps, 2, 1)
+            per = sec / (reps * len(layers))
+            if M == 2048:
+                flops = 2 * M * HIDDEN * (2 * n_rows if gate else n_rows)
+                out[f"{name}_m{M}"] = {"us_per_launch": per * 1e6, "TFLOP/s": flops / per / 1e12}
+            else:
+                b = op_bytes(2 * n_rows if gate else n_rows, HIDDEN, M, n_rows)
+                out[f"{name}_m{M}"] = {"us_per_launch": per * 1e6, "GB/s": b / per / 1e9}
+            del g, x, y
+    # int8 weight-only at the Qwen3-8B shape (K = 4096): GB/s of int8 weights + activations
+    gq = torch.Generator(device="cuda").manual_seed(4)
+    K8, NQKV8, N8 = 4096, NQ + 2 * NK, 12288
+    w8 = [(torch.randint(-127, 128, (NQKV8, K8), device="cuda", dtype=torch.int8, generator=gq),
+           torch.rand(NQKV8, device="cuda", generator=gq) * 9e-4 + 1e-4,
+           torch.randint(-127, 128, (N8, K8), device="cuda", dtype=torch.int8, generator=gq),
+           torch.rand(N8, device="cuda", generator=gq) * 9e-4 + 1e-4,
+           torch.randint(-127, 128, (N8, K8), device="cuda", dtype=torch.int8, generator=gq),
+           torch.rand(N8, device="cuda", generator=gq) * 9e-4 + 1e-4) for _ in range(2)]
+    for M in (1, 16, 64):
+        for name, gate in (("qkv_w8", False), ("gate_up_w8", True)):
+            x = torch.randn(M, K8, device="cuda", dtype=torch.bfloat16)
+            n_rows = N8 if gate else NQKV8
+            y = torch.empty(M, n_rows, device="cuda", dtype=torch.bfloat16)
+
+            def run8(x=x, y=y, n_rows=n_rows, gate=gate, M=M):
+                s = torch.cuda.current_stream().cuda_stream
+                for (wq, sq, wg8, sg8, wu8, su8) in w8:
+                    if gate:
+                        st = _capi.lib.b200mm_gate_up_silu_w8(x.data_ptr(), K8, wg8.data_ptr(), sg8.data_ptr(),
+                                                              wu8.data_ptr(), su8.data_ptr(), K8, y.data_ptr(),
+                                                              n_rows, M, n_rows, K8, 2, s)
+                    else:
+                        st = _capi.lib.b200mm_qkv_w8(x.data_ptr(), K8, wq.data_ptr(), sq.data_ptr(), K8,
+                                                     y.data_ptr(), n_rows, M, n_rows, K8, 2, s)
+                    _capi.check(st, name)
+
+            g, _ = job.capture(run8)
+            sec = time_graph(g, 20, 2, 1)
+            per = sec / (20 * len(w8))
+            wrows = 2 * n_rows if gate else n_rows
+            b = wrows * K8 + 4 * wrows + 2 * M * (K8 + n_rows)
+            out[f"{name}_m{M}"] = {"us_per_launch": per * 1e6, "GB/s": b / per / 1e9}
+            del g, x, y
+    del w8
     # MLA decode GB/s at L = 32k
     H, KV, D, DR, R = 32, 8, 128, 32, 256
     for B, L in ((32, 32768), (1, 32768)):
@@ -406,6 +503,9 @@ def run_reference(args, rank, world):
 
 def main():
     args = parse_args()
+    if args.profile_op:
+        profile_op(args)
+        return
     rank, world, local = dist_setup()
     if args.impl == "reference":
         run_reference(args, rank, world)
