@@ -20,8 +20,9 @@
  *                               (launch of _qkv_matmul_kernel, fused_qkv.py:28-85)
  *   b200mm_gate_up_silu_w8   <- no reference symbol: int8 weight-only variant of
  *   b200mm_qkv_w8               the two calls above (dequantise W = q * s[row])
- *   b200mm_mla_kv_scales     <- engine/mla.py:211-221 (the per-token RMS of the
- *                               reconstructed K head, k_norm over the full head_dim)
+ *   b200mm_mla_append        <- engine/mla.py:211-242 for one token at a time: the
+ *                               per-token k_norm factor of the reconstructed K head
+ *                               and the RoPE'd rope half of K, kept as side-bands
  *   b200mm_mla_decode        <- engine/mla.py:195-264, the T == 1 branch of
  *                               MLAttention.forward (everything between the
  *                               q/dkv/kr projections and the o projection)
@@ -139,6 +140,7 @@ int b200mm_qkv_w8(const void* x, int64_t ldx,
  * Cache tensors (engine/mla.py:41-87, MLAKVCache):
  *   c_kv       [*, S, R]       dtype, strides (c_sb, c_st) elements, unit inner
  *   k_rope_pre [*, S, KV, DR]  dtype, strides (r_sb, r_st), inner [KV, DR] dense
+ *   (b200mm_mla_append reads k_rope_pre; the decode step reads its side-band kz)
  *   kscale     [*, S, KV]      fp32,  strides (s_sb, s_st), inner dense
  * Weights (the nn.Linear weights viewed per group):
  *   w_uk : [KV, DN, R] dtype dense (uk_nope.weight.view(KV, DN, R))
@@ -152,19 +154,27 @@ typedef struct b200mm_mla_shape {
 } b200mm_mla_shape;
 
 /*
- * kscale[b, t, g] = rsqrt(mean_d(k[b,t,g,d]^2) + eps) for t in [t0, t1), with
- * k[b,t,g] = [w_uk[g] . c_kv[b,t] ; k_rope_pre[b,t,g]] (the reconstructed,
- * un-normed K head of engine/mla.py:212-215).  This is the per-token factor the
- * k_norm RMSNorm (engine/mla.py:221, engine/attention.py:28-33) multiplies by;
- * it is written once per token when the token enters the cache, so a decode
- * step never re-expands K.
+ * Per-token side-bands of the MLA cache, written once when tokens enter the
+ * cache (positions [t0, t1) of batch rows 0..B-1), so a decode step never
+ * re-expands or re-rotates K:
+ *   kscale[b,t,g] fp32  = rsqrt(mean_d k[b,t,g,d]^2 + eps), where
+ *                         k[b,t,g] = [w_uk[g] . c_kv[b,t] ; k_rope_pre[b,t,g]]
+ *                         is the reconstructed, un-normed K head of
+ *                         engine/mla.py:212-215; k_norm (engine/mla.py:221,
+ *                         engine/attention.py:28-33) multiplies by it;
+ *   kz[b,t,g,:]  dtype  = rope_t(k_norm_w[DN:] * k_rope_pre[b,t,g,:]), the RoPE
+ *                         half of the normed K head divided by kscale
+ *                         (engine/mla.py:226-242; angle float(t) * inv_freq[i],
+ *                         rotate-half convention).
+ *   kz : [*, S, KV, DR] dtype, strides (z_sb, z_st), inner [KV, DR] dense.
  */
-int b200mm_mla_kv_scales(const b200mm_mla_shape* shape,
-                         const void* c_kv, int64_t c_sb, int64_t c_st,
-                         const void* k_rope_pre, int64_t r_sb, int64_t r_st,
-                         const void* w_uk,
-                         float* kscale, int64_t s_sb, int64_t s_st,
-                         int64_t t0, int64_t t1, void* stream);
+int b200mm_mla_append(const b200mm_mla_shape* shape,
+                      const void* c_kv, int64_t c_sb, int64_t c_st,
+                      const void* k_rope_pre, int64_t r_sb, int64_t r_st,
+                      const void* w_uk, const float* k_norm_w, const float* rope_inv_freq,
+                      float* kscale, int64_t s_sb, int64_t s_st,
+                      void* kz, int64_t z_sb, int64_t z_st,
+                      int64_t t0, int64_t t1, void* stream);
 
 /*
  * Bytes of workspace b200mm_mla_decode needs for (shape, L).  0 on bad shape.
@@ -174,6 +184,7 @@ size_t b200mm_mla_decode_workspace_size(const b200mm_mla_shape* shape, int64_t L
 /*
  * One decode step of MLA attention with absorbed up-projections.
  *   q   : [B, H, D] dtype, batch stride q_sb (q after q_norm, before RoPE)
+ *   kz, kscale : the side-bands of b200mm_mla_append, valid for positions < L
  *   L   : context length including the new token; the query sits at
  *         position L-1 and attends to cache positions 0..L-1
  *   rope_inv_freq : fp32 [DR/2]; angle(t, i) = float(t) * inv_freq[i]
@@ -187,7 +198,7 @@ size_t b200mm_mla_decode_workspace_size(const b200mm_mla_shape* shape, int64_t L
 int b200mm_mla_decode(const b200mm_mla_shape* shape,
                       const void* q, int64_t q_sb,
                       const void* c_kv, int64_t c_sb, int64_t c_st,
-                      const void* k_rope_pre, int64_t r_sb, int64_t r_st,
+                      const void* kz, int64_t z_sb, int64_t z_st,
                       const float* kscale, int64_t s_sb, int64_t s_st,
                       const void* w_uk, const void* w_uv,
                       const float* k_norm_w, const float* rope_inv_freq,
@@ -222,7 +233,7 @@ int b200mm_mla_decode(const b200mm_mla_shape* shape,
 int b200mm_mla_decode_noalloc(const b200mm_mla_shape* shape,
                               const void* q, int64_t q_sb,
                               const void* c_kv, int64_t c_sb, int64_t c_st,
-                              const void* k_rope_pre, int64_t r_sb, int64_t r_st,
+                              const void* kz, int64_t z_sb, int64_t z_st,
                               const float* kscale, int64_t s_sb, int64_t s_st,
                               const void* w_uk, const void* w_uv,
                               const float* k_norm_w, const float* rope_inv_freq,

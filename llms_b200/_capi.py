@@ -59,10 +59,10 @@ SIGNATURES: dict[str, tuple] = {
         ctypes.c_int,
         [_c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int, _c_p],
     ),
-    "b200mm_mla_kv_scales": (
+    "b200mm_mla_append": (
         ctypes.c_int,
-        [ctypes.POINTER(MlaShape), _c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_p,
-         _c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_p],
+        [ctypes.POINTER(MlaShape), _c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_p,
+         _c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_p],
     ),
     "b200mm_mla_decode_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(MlaShape), _c_i64]),
     "b200mm_mla_decode": (

@@ -50,7 +50,10 @@ int check_device() {
 
 int dense_dispatch(const DenseArgs& a) {
   if (g_force_generic.load(std::memory_order_relaxed)) return tiled_launch(a);
+  // M >= 65: tcgen05 GEMM; M <= 4: CUDA-core GEMV; 5..64: tensor-core GEMV
   if (tc_supported(a)) return tc_launch(a);
+  if (a.M <= 4 && gemv_supported(a)) return gemv_launch(a);
+  if (mmv_supported(a)) return mmv_launch(a);
   if (gemv_supported(a)) return gemv_launch(a);
   return tiled_launch(a);
 }
@@ -148,25 +151,28 @@ int b200mm_qkv_w8(const void* x, int64_t ldx, const int8_t* w, const float* s, i
   return run_dense(a, M, N, K);
 }
 
-int b200mm_mla_kv_scales(const b200mm_mla_shape* shape, const void* c_kv, int64_t c_sb, int64_t c_st,
-                         const void* k_rope_pre, int64_t r_sb, int64_t r_st, const void* w_uk,
-                         float* kscale, int64_t s_sb, int64_t s_st, int64_t t0, int64_t t1,
-                         void* stream) {
+int b200mm_mla_append(const b200mm_mla_shape* shape, const void* c_kv, int64_t c_sb, int64_t c_st,
+                      const void* k_rope_pre, int64_t r_sb, int64_t r_st, const void* w_uk, const float* k_norm_w,
+                      const float* rope_inv_freq, float* kscale, int64_t s_sb, int64_t s_st, void* kz,
+                      int64_t z_sb, int64_t z_st, int64_t t0, int64_t t1, void* stream) {
   if (!shape) return B200MM_ERR_ARG;
-  MlaScalesArgs a{};
+  MlaAppendArgs a{};
   a.s = *shape;
   a.c_kv = c_kv; a.c_sb = c_sb; a.c_st = c_st;
   a.kr = k_rope_pre; a.r_sb = r_sb; a.r_st = r_st;
-  a.w_uk = w_uk; a.kscale = kscale; a.s_sb = s_sb; a.s_st = s_st;
+  a.w_uk = w_uk; a.k_norm_w = k_norm_w; a.inv_freq = rope_inv_freq;
+  a.kscale = kscale; a.s_sb = s_sb; a.s_st = s_st;
+  a.kz = kz; a.z_sb = z_sb; a.z_st = z_st;
   a.t0 = t0; a.t1 = t1; a.stream = static_cast<cudaStream_t>(stream);
   int st = mla_validate_shape(a.s);
   if (st != B200MM_OK) return st;
-  if (!c_kv || !kscale || (a.s.DR > 0 && !k_rope_pre) || (a.s.D - a.s.DR > 0 && !w_uk)) return B200MM_ERR_ARG;
+  if (!c_kv || !kscale || (a.s.D - a.s.DR > 0 && !w_uk)) return B200MM_ERR_ARG;
+  if (a.s.DR > 0 && (!k_rope_pre || !kz || !k_norm_w || !rope_inv_freq)) return B200MM_ERR_ARG;
   if (t0 < 0 || t1 < t0 || t1 >= (int64_t(1) << 31)) return B200MM_ERR_SHAPE;
   if (t1 == t0 || a.s.B == 0) return B200MM_OK;
   st = check_device();
   if (st != B200MM_OK) return st;
-  st = mla_scales_launch(a);
+  st = mla_append_launch(a);
   if (st != B200MM_OK) return st;
   return launch_status();
 }
@@ -177,7 +183,7 @@ size_t b200mm_mla_decode_workspace_size(const b200mm_mla_shape* shape, int64_t L
 }
 
 int b200mm_mla_decode(const b200mm_mla_shape* shape, const void* q, int64_t q_sb, const void* c_kv,
-                      int64_t c_sb, int64_t c_st, const void* k_rope_pre, int64_t r_sb, int64_t r_st,
+                      int64_t c_sb, int64_t c_st, const void* kz, int64_t z_sb, int64_t z_st,
                       const float* kscale, int64_t s_sb, int64_t s_st, const void* w_uk,
                       const void* w_uv, const float* k_norm_w, const float* rope_inv_freq,
                       float scale, int64_t L, void* out, int64_t o_sb, void* workspace,
@@ -187,7 +193,7 @@ int b200mm_mla_decode(const b200mm_mla_shape* shape, const void* q, int64_t q_sb
   a.s = *shape;
   a.q = q; a.q_sb = q_sb;
   a.c_kv = c_kv; a.c_sb = c_sb; a.c_st = c_st;
-  a.kr = k_rope_pre; a.r_sb = r_sb; a.r_st = r_st;
+  a.kz = kz; a.z_sb = z_sb; a.z_st = z_st;
   a.kscale = kscale; a.s_sb = s_sb; a.s_st = s_st;
   a.w_uk = w_uk; a.w_uv = w_uv; a.k_norm_w = k_norm_w; a.inv_freq = rope_inv_freq;
   a.scale = scale; a.L = L; a.out = out; a.o_sb = o_sb;
@@ -197,7 +203,7 @@ int b200mm_mla_decode(const b200mm_mla_shape* shape, const void* q, int64_t q_sb
   if (st != B200MM_OK) return st;
   if (L < 1 || L >= (int64_t(1) << 31)) return B200MM_ERR_SHAPE;
   if (!q || !c_kv || !kscale || !w_uv || !k_norm_w || !out) return B200MM_ERR_ARG;
-  if (a.s.DR > 0 && (!k_rope_pre || !rope_inv_freq)) return B200MM_ERR_ARG;
+  if (a.s.DR > 0 && (!kz || !rope_inv_freq)) return B200MM_ERR_ARG;
   if (a.s.D - a.s.DR > 0 && !w_uk) return B200MM_ERR_ARG;
   if (!(scale > 0.f)) return B200MM_ERR_ARG;
   if (a.s.B == 0) return B200MM_OK;

@@ -28,6 +28,8 @@ int dense_dispatch(const DenseArgs& a);
 bool gemv_supported(const DenseArgs& a);
 int gemv_launch(const DenseArgs& a);
 int tiled_launch(const DenseArgs& a);
+bool mmv_supported(const DenseArgs& a);
+int mmv_launch(const DenseArgs& a);
 bool tc_supported(const DenseArgs& a);
 int tc_launch(const DenseArgs& a);
 

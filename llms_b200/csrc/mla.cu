@@ -6,9 +6,10 @@
 // each cached token once, in latent form:
 //
 //   s_t,g     = rsqrt(mean_d k_t,g[d]^2 + eps)        (side-band, written at append)
+//   z_t,g     = rope_t(w_k[DN:] * kr_t,g)              (side-band, written at append)
 //   qt_h      = W_uk,g^T (w_k[:DN] * q_h[:DN])         (absorbed query, per step)
 //   qr_h      = rope_{L-1}(q_h[DN:])
-//   score_t,h = scale * s_t,g * (qt_h . c_t + qr_h . rope_t(w_k[DN:] * kr_t,g))
+//   score_t,h = scale * s_t,g * (qt_h . c_t + qr_h . z_t,g)
 //   out_h     = W_uv,g (sum_t softmax(score)_t,h c_t)
 //
 // which equals the reference because k_norm multiplies the raw head by the
@@ -30,13 +31,13 @@ inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 template <typename T>
 __device__ __forceinline__ float ldf(const T* p, int64_t i) { return to_f<T>(p[i]); }
 
-// --- per-token k RMS side-band --------------------------------------------
+// --- per-token side-bands (at append) ----------------------------------------
 // grid: (ceil((t1-t0)/8), B); block 256.  Each CTA handles 8 tokens of one
 // batch row; warps walk the KV*DN rows of W_uk, lanes split the rank.
 template <typename T>
-__global__ void __launch_bounds__(kThreads) mla_scales_kernel(const MlaScalesArgs a) {
+__global__ void __launch_bounds__(kThreads) mla_append_kernel(const MlaAppendArgs a) {
   extern __shared__ float sm[];
-  const int R = a.s.R, KV = a.s.KV, D = a.s.D, DR = a.s.DR, DN = D - DR;
+  const int R = a.s.R, KV = a.s.KV, D = a.s.D, DR = a.s.DR, DN = D - DR, half = DR / 2;
   constexpr int TT = 8;
   float* cs = sm;                 // [TT][R]
   float* ssq = sm + TT * R;       // [TT][KV]
@@ -53,17 +54,23 @@ __global__ void __launch_bounds__(kThreads) mla_scales_kernel(const MlaScalesArg
     const int t = i / R, r = i % R;
     cs[i] = t < nt ? ldf(c, (tb + t) * a.c_st + r) : 0.f;
   }
-  // rope-half contribution: sum of squares of kr
-  for (int i = threadIdx.x; i < TT * KV; i += blockDim.x) {
-    const int t = i / KV, g = i % KV;
-    float acc = 0.f;
-    if (t < nt && DR > 0) {
-      const T* p = kr + (int64_t)b * a.r_sb + (tb + t) * a.r_st + (int64_t)g * DR;
-      for (int d = 0; d < DR; ++d) { const float v = ldf(p, d); acc = fmaf(v, v, acc); }
-    }
-    ssq[i] = acc;
-  }
+  for (int i = threadIdx.x; i < TT * KV; i += blockDim.x) ssq[i] = 0.f;
   __syncthreads();
+  // rope half: its sum of squares, and z = rope_t(w_k[DN:] * kr)
+  for (int i = threadIdx.x; i < TT * KV * DR; i += blockDim.x) {
+    const int t = i / (KV * DR), rem = i % (KV * DR), g = rem / DR, j = rem % DR;
+    if (t >= nt) continue;
+    const T* p = kr + (int64_t)b * a.r_sb + (tb + t) * a.r_st + (int64_t)g * DR;
+    const float x = ldf(p, j);
+    atomicAdd(&ssq[t * KV + g], x * x);
+    const int ii = j < half ? j : j - half;
+    float sn, cn;
+    sincosf((float)(tb + t) * a.inv_freq[ii], &sn, &cn);
+    const float rot = j < half ? -a.k_norm_w[DN + j + half] * ldf(p, j + half)
+                               : a.k_norm_w[DN + j - half] * ldf(p, j - half);
+    T* zp = static_cast<T*>(a.kz) + (int64_t)b * a.z_sb + (tb + t) * a.z_st + (int64_t)g * DR;
+    zp[j] = from_f<T>(a.k_norm_w[DN + j] * x * cn + rot * sn);
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   for (int row = warp; row < KV * DN; row += nw) {
     const int g = row / DN;
@@ -108,13 +115,37 @@ __global__ void __launch_bounds__(kThreads) mla_absorb_kernel(const MlaDecodeArg
     *reinterpret_cast<int*>(static_cast<unsigned char*>(a.ws) + w.off_err) = 0;
   for (int d = threadIdx.x; d < D; d += blockDim.x) qn[d] = ldf(q, d);
   __syncthreads();
-  // qt[r] = sum_i W_uk[g, i, r] * w_k[i] * q[i]
-  const T* wuk = static_cast<const T*>(a.w_uk) + (int64_t)g * DN * R;
-  for (int r = threadIdx.x; r < R; r += blockDim.x) {
-    float acc = 0.f;
-#pragma unroll 8
-    for (int i = 0; i < DN; ++i) acc = fmaf(ldf(wuk, (int64_t)i * R + r), a.k_norm_w[i] * qn[i], acc);
-    qt[r] = acc;
+  // qt[r] = sum_i W_uk[g, i, r] * w_k[i] * q[i]: warps split i, lanes split r,
+  // so each thread issues its loads back to back; partial sums meet in shared memory.
+  {
+    const T* wuk = static_cast<const T*>(a.w_uk) + (int64_t)g * DN * R;
+    float* part = sm + D;  // [nwarps][R]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int per = (DN + nw - 1) / nw, i0 = warp * per, i1 = min(DN, i0 + per);
+    for (int r0 = 0; r0 < R; r0 += 32 * 8) {
+      float acc[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+      for (int i = i0; i < i1; ++i) {
+        const float qi = a.k_norm_w[i] * qn[i];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int r = r0 + lane + 32 * j;
+          if (r < R) acc[j] = fmaf(ldf(wuk, (int64_t)i * R + r), qi, acc[j]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int r = r0 + lane + 32 * j;
+        if (r < R) part[warp * R + r] = acc[j];
+      }
+    }
+    __syncthreads();
+    for (int r = threadIdx.x; r < R; r += blockDim.x) {
+      float v = 0.f;
+      for (int w2 = 0; w2 < nw; ++w2) v += part[w2 * R + r];
+      qt[r] = v;
+    }
   }
   // qr = rope at position L-1 (rotate-half convention, angle = pos * inv_freq)
   const int half = DR / 2;
@@ -138,7 +169,7 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads) mla_split_kernel(const MlaDecodeArgs a, MlaWorkspace w) {
   extern __shared__ float sm[];
   const int H = a.s.H, KV = a.s.KV, D = a.s.D, DR = a.s.DR, DN = D - DR, R = a.s.R;
-  const int hpg = H / KV, half = DR / 2;
+  const int hpg = H / KV;
   const int cta = blockIdx.x;
   float* qt = sm;
   float* qr = qt + H * R;
@@ -161,7 +192,7 @@ __global__ void __launch_bounds__(kThreads) mla_split_kernel(const MlaDecodeArgs
     const int b = (int)(u / w.ntiles);
     const int64_t u_stop = imin64(u_end, (int64_t)(b + 1) * w.ntiles);  // units of row b in this range
     const T* c = static_cast<const T*>(a.c_kv) + (int64_t)b * a.c_sb;
-    const T* kr = static_cast<const T*>(a.kr) + (int64_t)b * a.r_sb;
+    const T* kz = static_cast<const T*>(a.kz) + (int64_t)b * a.z_sb;
     const float* ks = a.kscale + (int64_t)b * a.s_sb;
     for (int i = threadIdx.x; i < H * R; i += blockDim.x) {
       qt[i] = ws[w.off_qt / 4 + (int64_t)b * H * R + i];
@@ -179,19 +210,8 @@ __global__ void __launch_bounds__(kThreads) mla_split_kernel(const MlaDecodeArgs
         cs[i] = t < nt ? ldf(c, (t0 + t) * a.c_st + r) : 0.f;
       }
       for (int i = threadIdx.x; i < kTileT * KV * DR; i += blockDim.x) {
-        const int t = i / (KV * DR), rem = i % (KV * DR), g = rem / DR, j = rem % DR;
-        float v = 0.f;
-        if (t < nt) {
-          const T* p = kr + (t0 + t) * a.r_st + (int64_t)g * DR;
-          const int ii = j < half ? j : j - half;
-          float sn, cn;
-          sincosf((float)(t0 + t) * a.inv_freq[ii], &sn, &cn);
-          const float x = a.k_norm_w[DN + j] * ldf(p, j);
-          const float rot = j < half ? -a.k_norm_w[DN + j + half] * ldf(p, j + half)
-                                     : a.k_norm_w[DN + j - half] * ldf(p, j - half);
-          v = x * cn + rot * sn;
-        }
-        z[i] = v;
+        const int t = i / (KV * DR), rem = i % (KV * DR);
+        z[i] = t < nt ? ldf(kz, (t0 + t) * a.z_st + rem) : 0.f;
       }
       for (int i = threadIdx.x; i < kTileT * KV; i += blockDim.x) {
         const int t = i / KV, g = i % KV;
@@ -282,21 +302,35 @@ __global__ void __launch_bounds__(kThreads) mla_combine_kernel(const MlaDecodeAr
     if (lane == 0) s_inv_l = 1.f / l;
   }
   __syncthreads();
-  for (int r = threadIdx.x; r < R; r += blockDim.x) {
-    float v0 = 0.f, v1 = 0.f, v2 = 0.f, v3 = 0.f;
-    const float* pc = pacc + (((int64_t)i0 + b) * H + h) * R + r;
-    const int64_t step = (int64_t)H * R;
-    int k = 0;
-    for (; k + 4 <= n; k += 4) {
-      const float p0 = pc[(k + 0) * step], p1 = pc[(k + 1) * step];
-      const float p2 = pc[(k + 2) * step], p3 = pc[(k + 3) * step];
-      v0 = fmaf(wgt[k], p0, v0);
-      v1 = fmaf(wgt[k + 1], p1, v1);
-      v2 = fmaf(wgt[k + 2], p2, v2);
-      v3 = fmaf(wgt[k + 3], p3, v3);
+  {
+    // warps split the partials, lanes split the rank; per-warp sums meet in shared memory
+    float* part = wgt + w.G + 1;  // [nwarps][R]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int r0 = 0; r0 < R; r0 += 32 * 8) {
+      float acc[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+      for (int k = warp; k < n; k += nw) {
+        const float wk = wgt[k];
+        const float* pc = pacc + (((int64_t)i0 + k + b) * H + h) * R;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int r = r0 + lane + 32 * j;
+          if (r < R) acc[j] = fmaf(wk, pc[r], acc[j]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int r = r0 + lane + 32 * j;
+        if (r < R) part[warp * R + r] = acc[j];
+      }
     }
-    for (; k < n; ++k) v0 = fmaf(wgt[k], pc[k * step], v0);
-    av[r] = ((v0 + v1) + (v2 + v3)) * s_inv_l;
+    __syncthreads();
+    for (int r = threadIdx.x; r < R; r += blockDim.x) {
+      float v = 0.f;
+      for (int w2 = 0; w2 < nw; ++w2) v += part[w2 * R + r];
+      av[r] = v * s_inv_l;
+    }
   }
   __syncthreads();
   const T* wuv = static_cast<const T*>(a.w_uv) + (int64_t)g * D * R;
@@ -304,11 +338,19 @@ __global__ void __launch_bounds__(kThreads) mla_combine_kernel(const MlaDecodeAr
   // a split kernel that gave up on a bounded wait leaves NaN, never a silent result
   const bool failed = *reinterpret_cast<const int*>(static_cast<const unsigned char*>(a.ws) + w.off_err) != 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (int d = warp; d < D; d += nw) {
-    float v = 0.f;
-    for (int r = lane; r < R; r += 32) v = fmaf(ldf(wuv, (int64_t)d * R + r), av[r], v);
-    v = warp_sum(v);
-    if (lane == 0) out[d] = from_f<T>(failed ? __int_as_float(0x7fc00000) : v);
+  for (int d0 = warp * 4; d0 < D; d0 += nw * 4) {  // 4 rows per step: more loads in flight
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int r = lane; r < R; r += 32) {
+      const float ar = av[r];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (d0 + j < D) v[j] = fmaf(ldf(wuv, (int64_t)(d0 + j) * R + r), ar, v[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float sum = warp_sum(v[j]);
+      if (lane == 0 && d0 + j < D) out[d0 + j] = from_f<T>(failed ? __int_as_float(0x7fc00000) : sum);
+    }
   }
 }
 
@@ -335,7 +377,7 @@ int decode_t(const MlaDecodeArgs& a) {
       !g_force_generic.load(std::memory_order_relaxed) && mla_fast_supported(a) && mla_fast_maps(a, &maps);
   const MlaWorkspace w = mla_plan(a.s, a.L, fast);
   const int B = a.s.B, H = a.s.H;
-  int st = launch_smem(mla_absorb_kernel<T>, dim3(H, B), sizeof(float) * a.s.D, a.stream, a, w);
+  int st = launch_smem(mla_absorb_kernel<T>, dim3(H, B), sizeof(float) * (a.s.D + (kThreads / 32) * a.s.R), a.stream, a, w);
   if (st) return st;
   if (fast) {
     st = mla_fast_split_launch(a, w, maps);
@@ -343,15 +385,15 @@ int decode_t(const MlaDecodeArgs& a) {
     st = launch_smem(mla_split_kernel<T>, dim3(w.G), split_smem_bytes(a.s), a.stream, a, w);
   }
   if (st) return st;
-  return launch_smem(mla_combine_kernel<T>, dim3(H, B), sizeof(float) * (a.s.R + w.G + 1), a.stream, a, w);
+  return launch_smem(mla_combine_kernel<T>, dim3(H, B), sizeof(float) * (a.s.R + w.G + 1 + (kThreads / 32) * a.s.R), a.stream, a, w);
 }
 
 template <typename T>
-int scales_t(const MlaScalesArgs& a) {
+int append_t(const MlaAppendArgs& a) {
   const int64_t n = a.t1 - a.t0;
   dim3 grid((unsigned)((n + 7) / 8), (unsigned)a.s.B);
   const size_t smem = sizeof(float) * (8 * (size_t)a.s.R + 8 * (size_t)a.s.KV);
-  return launch_smem(mla_scales_kernel<T>, grid, smem, a.stream, a);
+  return launch_smem(mla_append_kernel<T>, grid, smem, a.stream, a);
 }
 
 }  // namespace
@@ -389,10 +431,10 @@ size_t mla_workspace_bytes(const b200mm_mla_shape& s, int64_t L) {
   return a > b ? a : b;
 }
 
-int mla_scales_launch(const MlaScalesArgs& a) {
-  if (a.s.dtype == B200MM_BF16) return scales_t<__nv_bfloat16>(a);
-  if (a.s.dtype == B200MM_F16) return scales_t<__half>(a);
-  return scales_t<float>(a);
+int mla_append_launch(const MlaAppendArgs& a) {
+  if (a.s.dtype == B200MM_BF16) return append_t<__nv_bfloat16>(a);
+  if (a.s.dtype == B200MM_F16) return append_t<__half>(a);
+  return append_t<float>(a);
 }
 
 int mla_decode_launch(const MlaDecodeArgs& a) {

@@ -5,12 +5,14 @@
 
 namespace b200mm {
 
-struct MlaScalesArgs {
+struct MlaAppendArgs {
   b200mm_mla_shape s;
   const void* c_kv; int64_t c_sb, c_st;
-  const void* kr; int64_t r_sb, r_st;
+  const void* kr; int64_t r_sb, r_st;     // k_rope_pre
   const void* w_uk;
+  const float* k_norm_w; const float* inv_freq;
   float* kscale; int64_t s_sb, s_st;
+  void* kz; int64_t z_sb, z_st;
   int64_t t0, t1;
   cudaStream_t stream;
 };
@@ -19,7 +21,7 @@ struct MlaDecodeArgs {
   b200mm_mla_shape s;
   const void* q; int64_t q_sb;
   const void* c_kv; int64_t c_sb, c_st;
-  const void* kr; int64_t r_sb, r_st;
+  const void* kz; int64_t z_sb, z_st;     // RoPE'd rope-half side-band
   const float* kscale; int64_t s_sb, s_st;
   const void* w_uk; const void* w_uv;
   const float* k_norm_w; const float* inv_freq;
@@ -58,12 +60,12 @@ __host__ __device__ inline int64_t mla_range_begin(const MlaWorkspace& w, int i)
 int mla_validate_shape(const b200mm_mla_shape& s);
 MlaWorkspace mla_plan(const b200mm_mla_shape& s, int64_t L, bool fast);
 size_t mla_workspace_bytes(const b200mm_mla_shape& s, int64_t L);
-int mla_scales_launch(const MlaScalesArgs& a);
+int mla_append_launch(const MlaAppendArgs& a);
 int mla_decode_launch(const MlaDecodeArgs& a);
 
 // production-shape split kernel (R=256, D=128, DR=32, H=32, KV=8, 16-bit dtype)
 struct MlaMaps {
-  CUtensorMap c, kr, ks;  // TMA maps of c_kv, k_rope_pre and the k-RMS side-band (token extent = L)
+  CUtensorMap c, kz, ks;  // TMA maps of c_kv, k_rope_pre and the k-RMS side-band (token extent = L)
 };
 bool mla_fast_supported(const MlaDecodeArgs& a);
 bool mla_fast_maps(const MlaDecodeArgs& a, MlaMaps* maps);  // false if the driver rejects a map

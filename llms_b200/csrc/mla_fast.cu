@@ -4,17 +4,19 @@
 // One persistent CTA per SM walks its range of 64-token units (see the plan
 // in mla.cuh).  Per unit:
 //   1. TMA tensor loads (3-D maps over [batch, token, channel], token extent
-//      L so rows past the context arrive as zeros) bring c [64 x 256] and
-//      k_rope_pre [64 x 8*32] as four 64-column boxes each, 128-byte swizzled,
-//      and the k-RMS side-band [64 x 8]; completion on an mbarrier; two
-//      stages, so the next unit streams while this one computes;
-//   2. z = rope_t(w_k[DN:] * kr) per (token, group) on CUDA cores, written
-//      over k_rope_pre in place;
-//   3. scores S[64 x 32] = C . Qt^T (K = 256) + Z . Qr^T (per group, K = 64)
-//      on mma.sync m16n8k16 (fp32 accumulate), then * s_t,g * scale;
-//   4. online softmax per head (running max / sum in shared memory);
-//   5. acc[32 x 256] = acc * alpha + P . C on mma.sync (registers, 32 fp32
-//      per thread), P in the storage dtype.
+//      L so rows past the context arrive as zeros) bring c [64 x 256] and the
+//      RoPE'd key side-band z [64 x 8*32] as four 64-column boxes each,
+//      128-byte swizzled, and the k-RMS side-band s [64 x 8]; completion on an
+//      mbarrier; two stages, so the next unit streams while this one computes;
+//   2. scores S[64 x 32] = C . Qt^T (K = 256) + Z . Qr^T (per 8-head n-tile,
+//      the 64 z columns of its two groups) on mma.sync m16n8k16, fp32
+//      accumulate, two independent accumulator chains per tile;
+//   3. S * s_t,g * scale stays in the MMA fragments; per-head max across the
+//      four token warps through shared memory; P = exp(S - m) in the storage
+//      dtype; per-head sums;
+//   4. acc[32 x 256] = acc * alpha + P . C on mma.sync (registers, 32 fp32 per
+//      thread).  The running max is double-buffered by unit parity, so a unit
+//      needs three CTA barriers.
 // A CTA writes one (acc, max, sum) partial per batch row it touched.
 //
 // Every mbarrier wait is bounded (%globaltimer); on expiry the kernel sets
@@ -22,39 +24,34 @@
 // returns; the combine kernel then writes NaN outputs.
 #include "mla.cuh"
 
-#ifndef MLA_SKIP
-#define MLA_SKIP 0  // development knob: bitmask of phases to skip when timing (0 in every build)
-#endif
-
 namespace b200mm {
 
 namespace {
 
-constexpr int FR = 256, FD = 128, FDR = 32, FDN = 96, FH = 32, FKV = 8;
+constexpr int FR = 256, FD = 128, FDR = 32, FH = 32, FKV = 8;
 constexpr int TT = kMlaUnit;      // 64 tokens per unit
 constexpr int NT = 256;           // threads
-constexpr int CP = FR + 8;        // padded row pitch (elements) of c / kr / z / qt: 528 bytes
+constexpr int CP = FR + 8;        // padded row pitch (elements) of qt: 528 bytes
 constexpr int PP = TT + 8;        // P row pitch: 144 bytes
 constexpr int RP = 64 + 8;        // rope-query row pitch
-constexpr int SCP = FH + 1;       // score row pitch (fp32)
 
-constexpr uint32_t kTileBytes = TT * FR * 2;                 // one [64 x 256] 16-bit tile: 32 KB
-constexpr uint32_t kUnitBytes = 2 * kTileBytes + TT * FKV * 4;  // c + kr + side-band per unit
+constexpr uint32_t kTileBytes = TT * FR * 2;                     // one [64 x 256] 16-bit tile: 32 KB
+constexpr uint32_t kUnitBytes = 2 * kTileBytes + TT * FKV * 4;    // c + z + s per unit
 
-// c and kr tiles are four [64 rows x 128 B] boxes in the TMA 128-byte swizzle
+// c and z tiles are four [64 rows x 128 B] boxes in the TMA 128-byte swizzle
 // (see sw128_off); the struct is placed at a 1024-byte aligned address.
 template <typename T>
 struct __align__(1024) FastSmem {
   unsigned char c[2][kTileBytes];
-  unsigned char kr[2][kTileBytes];
+  unsigned char z[2][kTileBytes];
   float s[2][TT][FKV];
   T qt[FH][CP];
   T qrb[FH][RP];
   T p[FH][PP];
-  float sc[TT][SCP];
-  float cs[TT][16];
-  float sn[TT][16];
-  float m[FH], l[FH], alpha[FH];
+  float red_max[4][FH];  // per token m-tile, per head
+  float red_sum[4][FH];
+  float m[2][FH];        // running max, double-buffered by unit parity
+  float l[FH];
   unsigned long long bar[2];
 };
 
@@ -103,13 +100,6 @@ template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) 
   __half2 v = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&v);
 }
-template <typename T> __device__ __forceinline__ float2 unpack2(uint32_t v);
-template <> __device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t v) {
-  return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
-}
-template <> __device__ __forceinline__ float2 unpack2<__half>(uint32_t v) {
-  return __half22float2(*reinterpret_cast<__half2*>(&v));
-}
 
 struct Unit {
   int b;
@@ -117,10 +107,14 @@ struct Unit {
   int nv;
 };
 
+__device__ __forceinline__ float max4(const float (*rm)[FH], int h) {
+  return fmaxf(fmaxf(rm[0][h], rm[1][h]), fmaxf(rm[2][h], rm[3][h]));
+}
+
 template <typename T>
 __global__ void __launch_bounds__(NT, 1)
     mla_fast_split_kernel(const MlaDecodeArgs a, MlaWorkspace w, const __grid_constant__ CUtensorMap map_c,
-                          const __grid_constant__ CUtensorMap map_kr, const __grid_constant__ CUtensorMap map_s) {
+                          const __grid_constant__ CUtensorMap map_z, const __grid_constant__ CUtensorMap map_s) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   FastSmem<T>& S = *reinterpret_cast<FastSmem<T>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -143,7 +137,7 @@ __global__ void __launch_bounds__(NT, 1)
     mbar_expect_tx(&S.bar[st], kUnitBytes);
     for (int j = 0; j < 4; ++j) {
       tma_load_3d(S.c[st] + j * TT * 128, &map_c, 64 * j, (int)un.t0, un.b, &S.bar[st]);
-      tma_load_3d(S.kr[st] + j * TT * 128, &map_kr, 64 * j, (int)un.t0, un.b, &S.bar[st]);
+      tma_load_3d(S.z[st] + j * TT * 128, &map_z, 64 * j, (int)un.t0, un.b, &S.bar[st]);
     }
     tma_load_3d(&S.s[st][0][0], &map_s, 0, (int)un.t0, un.b, &S.bar[st]);
   };
@@ -153,29 +147,23 @@ __global__ void __launch_bounds__(NT, 1)
     mbar_init(&S.bar[1], 1);
     mbar_init_fence();
     prefetch_map(&map_c);
-    prefetch_map(&map_kr);
+    prefetch_map(&map_z);
     prefetch_map(&map_s);
   }
   __syncthreads();
   pdl_trigger();
-  pdl_wait();  // the cache, side-band and absorbed query come from earlier kernels
-
+  pdl_wait();  // the cache, side-bands and absorbed query come from earlier kernels
   if (tid == 0) {
     issue(u_begin, 0);
     if (u_begin + 1 < u_end) issue(u_begin + 1, 1);
   }
 
-  // per-thread constants: the rope weights / frequencies this thread uses
-  const int zi2 = tid & 7;  // pair index: dims i = 2*zi2, 2*zi2+1 (and +16)
-  float wlo[2], whi[2];
-#pragma unroll
-  for (int e = 0; e < 2; ++e) {
-    wlo[e] = a.k_norm_w[FDN + 2 * zi2 + e];
-    whi[e] = a.k_norm_w[FDN + 16 + 2 * zi2 + e];
-  }
-  const float my_freq = a.inv_freq[tid & 15];
+  // scores: warp -> token m-tile mt_s (16 tokens), head n-tiles nt0, nt0 + 1
+  const int mt_s = warp >> 1, nt0 = (warp & 1) * 2;
+  const int r0 = 16 * mt_s + (lane >> 2);  // this lane's fragment rows r0, r0 + 8
+  const int cq = 2 * (lane & 3);           // fragment column pair
 
-  float acc[2][4][4];
+  float acc[2][4][4];  // P.C: heads 16*mt + lane/4 (+8), latent 32*warp + 8*nt + cq (+1)
   int cur_b = -1;
   bool bad = false;
   int64_t k = 0;  // local unit counter (stage = k & 1, parity = (k >> 1) & 1)
@@ -190,24 +178,24 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
           const int h = 16 * mt + (lane >> 2) + 8 * hf;
-          const int r = 32 * warp + 8 * nt + 2 * (lane & 3);
+          const int r = 32 * warp + 8 * nt + cq;
           *reinterpret_cast<float2*>(pacc + (int64_t)h * FR + r) =
               make_float2(acc[mt][nt][2 * hf], acc[mt][nt][2 * hf + 1]);
         }
     if (tid < FH) {
       float* pml = ws + w.off_pml / 4 + slot * FH * 2;
-      pml[2 * tid] = S.m[tid];
+      pml[2 * tid] = S.m[k & 1][tid];
       pml[2 * tid + 1] = S.l[tid];
     }
   };
 
   for (int64_t u = u_begin; u < u_end; ++u, ++k) {
     const Unit un = unit_of(u);
-    const int st = (int)(k & 1);
+    const int st = (int)(k & 1), mb = (int)(k & 1);  // stage; running-max buffer read this unit
     if (un.b != cur_b) {
       if (cur_b >= 0) flush(cur_b);
       __syncthreads();
-      // absorbed query of row b -> shared (storage dtype), rope query -> block layout
+      // absorbed query of row b -> shared (storage dtype); rope query -> per-n-tile block layout
       const float* qt = ws + w.off_qt / 4 + (int64_t)un.b * FH * FR;
       for (int i = tid; i < FH * FR / 2; i += NT) {
         const int h = (2 * i) / FR, r = (2 * i) % FR;
@@ -221,7 +209,7 @@ __global__ void __launch_bounds__(NT, 1)
         const float v = (kk / 32 == lg) ? qr[h * FDR + (kk & 31)] : 0.f;
         S.qrb[h][kk] = from_f<T>(v);
       }
-      if (tid < FH) { S.m[tid] = -INFINITY; S.l[tid] = 0.f; }
+      if (tid < FH) { S.m[mb][tid] = -INFINITY; S.l[tid] = 0.f; }
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
@@ -229,134 +217,124 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
           for (int e = 0; e < 4; ++e) acc[mt][nt][e] = 0.f;
       cur_b = un.b;
+      __syncthreads();
     }
-    // cos / sin of this unit's positions (independent of the copies)
-    for (int i = tid; i < TT * 16; i += NT) {
-      const int t = i >> 4;
-      float sv, cv;
-      if (MLA_SKIP & 1) { sv = 0.5f; cv = 0.5f; } else
-      sincosf((float)(un.t0 + t) * my_freq, &sv, &cv);
-      S.cs[t][i & 15] = cv;
-      S.sn[t][i & 15] = sv;
-    }
-    if (!mbar_wait(&S.bar[st], (uint32_t)((k >> 1) & 1))) {
-      bad = true;
-    }
+
+    if (!mbar_wait(&S.bar[st], (uint32_t)((k >> 1) & 1))) bad = true;
     if (__syncthreads_or(bad)) {
       bad = true;
       break;
     }
-    __syncthreads();
 
-    // ---- z[t][g*32 + j] = rope_t(w_r * kr[t][g])[j], in place over kr ----
-    for (int it = tid; it < ((MLA_SKIP & 2) ? 0 : TT * FKV * 8); it += NT) {
-      const int tg = it >> 3, t = tg >> 3, g = tg & 7;
-      const int i = 2 * zi2;
-      unsigned char* base = S.kr[st];
-      uint32_t* plo = reinterpret_cast<uint32_t*>(base + sw128_off(t, g * FDR + i, TT));
-      uint32_t* phi = reinterpret_cast<uint32_t*>(base + sw128_off(t, g * FDR + 16 + i, TT));
-      const float2 lo = unpack2<T>(*plo);
-      const float2 hi = unpack2<T>(*phi);
-      const float c0 = S.cs[t][i], c1 = S.cs[t][i + 1], s0 = S.sn[t][i], s1 = S.sn[t][i + 1];
-      const float l0 = wlo[0] * lo.x, l1 = wlo[1] * lo.y, h0 = whi[0] * hi.x, h1 = whi[1] * hi.y;
-      *plo = pack2<T>(l0 * c0 - h0 * s0, l1 * c1 - h1 * s1);
-      *phi = pack2<T>(h0 * c0 + l0 * s0, h1 * c1 + l1 * s1);
-    }
-    __syncthreads();
-
-    // ---- scores: warp -> token m-tile (warp>>1), head n-tiles 2*(warp&1) + {0,1} ----
+    // ---- scores S[t][h] = c_t . qt_h + z_t,g . qr_h ----
+    float sacc[2][4], sacc2[2][4];
+#pragma unroll
+    for (int q = 0; q < 2; ++q)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sacc[q][e] = sacc2[q][e] = 0.f;
     {
-      const int mt = warp >> 1, nt0 = (warp & 1) * 2;
-      float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      const int arow = 16 * mt + (lane & 15), acol = 8 * (lane >> 4);
+      const unsigned char* cbase = S.c[st];
+      const int arow = 16 * mt_s + (lane & 15), acol = 8 * (lane >> 4);
       const int bmat = lane >> 3, brow = 8 * nt0 + (bmat >> 1) * 8 + (lane & 7), bcol = (bmat & 1) * 8;
 #pragma unroll 4
-      for (int ks = 0; ks < ((MLA_SKIP & 4) ? 0 : FR / 16); ++ks) {
-        uint32_t af[4], b0, b1, b2, b3;
-        ldsm_x4(S.c[st] + sw128_off(arow, 16 * ks + acol, TT), af[0], af[1], af[2], af[3]);
+      for (int ks = 0; ks < FR / 16; ks += 2) {
+        uint32_t af[4], ag[4], b0, b1, b2, b3, d0, d1, d2, d3;
+        ldsm_x4(cbase + sw128_off(arow, 16 * ks + acol, TT), af[0], af[1], af[2], af[3]);
         ldsm_x4(&S.qt[brow][16 * ks + bcol], b0, b1, b2, b3);
+        ldsm_x4(cbase + sw128_off(arow, 16 * ks + 16 + acol, TT), ag[0], ag[1], ag[2], ag[3]);
+        ldsm_x4(&S.qt[brow][16 * ks + 16 + bcol], d0, d1, d2, d3);
         Mma<T>::run(sacc[0], af, b0, b1);
         Mma<T>::run(sacc[1], af, b2, b3);
+        Mma<T>::run(sacc2[0], ag, d0, d1);
+        Mma<T>::run(sacc2[1], ag, d2, d3);
       }
+      // rope part: n-tile np uses the 64 z columns of its groups 2np, 2np+1
+      const unsigned char* zbase = S.z[st];
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
-        const int np = nt0 + q;  // covers groups 2np, 2np+1 -> z columns [64np, 64np+64)
+        const int np = nt0 + q;
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
           uint32_t af[4], b0, b1;
-          ldsm_x4(S.kr[st] + sw128_off(arow, 64 * np + 16 * ks + acol, TT), af[0], af[1], af[2], af[3]);
+          ldsm_x4(zbase + sw128_off(arow, 64 * np + 16 * ks + acol, TT), af[0], af[1], af[2], af[3]);
           ldsm_x2(&S.qrb[8 * np + (lane & 7)][16 * ks + ((lane >> 3) & 1) * 8], b0, b1);
-          Mma<T>::run(sacc[q], af, b0, b1);
+          Mma<T>::run((ks & 1) ? sacc2[q] : sacc[q], af, b0, b1);
         }
       }
-#pragma unroll
-      for (int q = 0; q < 2; ++q)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int t = 16 * mt + (lane >> 2) + 8 * (e >> 1);
-          const int h = 8 * (nt0 + q) + 2 * (lane & 3) + (e & 1);
-          const float v = sacc[q][e] * S.s[st][t][h >> 2] * a.scale;
-          S.sc[t][h] = t < un.nv ? v : -INFINITY;
-        }
     }
-    __syncthreads();
-
-    // ---- online softmax: 8 threads per head, 8 tokens each ----
-    {
-      const int h = tid >> 3, sub = tid & 7;
-      float v[8], mx = -INFINITY;
+    // scale by s_t,g * scale, mask tokens past the context, per-head max over this warp's 16 rows
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        v[j] = S.sc[sub * 8 + j][h];
-        mx = fmaxf(mx, v[j]);
-      }
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-      const float m_old = S.m[h];
-      const float m_new = fmaxf(m_old, mx);  // finite: every unit has >= 1 valid token
-      float sum = 0.f;
+    for (int q = 0; q < 2; ++q) {
 #pragma unroll
-      for (int j = 0; j < 8; j += 2) {
-        const float p0 = __expf(v[j] - m_new), p1 = __expf(v[j + 1] - m_new);
-        sum += p0 + p1;
-        *reinterpret_cast<uint32_t*>(&S.p[h][sub * 8 + j]) = pack2<T>(p0, p1);
+      for (int e = 0; e < 4; ++e) {
+        const int t = r0 + 8 * (e >> 1);
+        const int h = 8 * (nt0 + q) + cq + (e & 1);
+        const float v = (sacc[q][e] + sacc2[q][e]) * S.s[st][t][h >> 2] * a.scale;
+        sacc[q][e] = t < un.nv ? v : -INFINITY;
       }
-      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-      __syncwarp();
-      if (sub == 0) {
-        const float al = __expf(m_old - m_new);
-        S.alpha[h] = al;
-        S.l[h] = S.l[h] * al + sum;
-        S.m[h] = m_new;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        float m = fmaxf(sacc[q][c], sacc[q][2 + c]);
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+        if (lane < 4) S.red_max[mt_s][8 * (nt0 + q) + cq + c] = m;
       }
     }
     __syncthreads();
-
+    // ---- softmax numerators: p = exp(s - m_new), P[h][t] in the storage dtype ----
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int h = 8 * (nt0 + q) + cq + c;
+        const float m_new = fmaxf(max4(S.red_max, h), S.m[mb][h]);  // finite: every unit has a valid token
+        const float p0 = __expf(sacc[q][c] - m_new), p1 = __expf(sacc[q][2 + c] - m_new);
+        S.p[h][r0] = from_f<T>(p0);
+        S.p[h][r0 + 8] = from_f<T>(p1);
+        float sum = p0 + p1;
+        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+        if (lane < 4) S.red_sum[mt_s][h] = sum;
+      }
+    }
+    __syncthreads();
     // ---- acc = acc * alpha + P . C ; warp -> latent cols [32*warp, +32) ----
     {
+      if (tid < FH) {  // running statistics; the new max goes to the other buffer
+        const float m_old = S.m[mb][tid];
+        const float m_new = fmaxf(max4(S.red_max, tid), m_old);
+        const float tsum = (S.red_sum[0][tid] + S.red_sum[1][tid]) + (S.red_sum[2][tid] + S.red_sum[3][tid]);
+        S.l[tid] = S.l[tid] * __expf(m_old - m_new) + tsum;
+        S.m[mb ^ 1][tid] = m_new;
+      }
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt) {
-        const float a0 = S.alpha[16 * mt + (lane >> 2)], a1 = S.alpha[16 * mt + 8 + (lane >> 2)];
 #pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-          acc[mt][nt][0] *= a0; acc[mt][nt][1] *= a0;
-          acc[mt][nt][2] *= a1; acc[mt][nt][3] *= a1;
+        for (int hf = 0; hf < 2; ++hf) {
+          const int h = 16 * mt + (lane >> 2) + 8 * hf;
+          const float m_old = S.m[mb][h];
+          const float al = __expf(m_old - fmaxf(max4(S.red_max, h), m_old));
+#pragma unroll
+          for (int nt = 0; nt < 4; ++nt) {
+            acc[mt][nt][2 * hf] *= al;
+            acc[mt][nt][2 * hf + 1] *= al;
+          }
         }
       }
       const int prow = lane & 15, pcol = 8 * (lane >> 4);
       const int bk = ((lane >> 3) & 1) * 8 + (lane & 7), bn = (lane >> 4) * 8;
+      const unsigned char* cbase = S.c[st];
 #pragma unroll
-      for (int ks = 0; ks < ((MLA_SKIP & 8) ? 0 : TT / 16); ++ks) {
+      for (int ks = 0; ks < TT / 16; ++ks) {
         uint32_t pa[2][4];
         ldsm_x4(&S.p[prow][16 * ks + pcol], pa[0][0], pa[0][1], pa[0][2], pa[0][3]);
         ldsm_x4(&S.p[16 + prow][16 * ks + pcol], pa[1][0], pa[1][1], pa[1][2], pa[1][3]);
 #pragma unroll
         for (int pp = 0; pp < 2; ++pp) {
           uint32_t b0, b1, b2, b3;
-          ldsm_x4_t(S.c[st] + sw128_off(16 * ks + bk, 32 * warp + 16 * pp + bn, TT), b0, b1, b2, b3);
+          ldsm_x4_t(cbase + sw128_off(16 * ks + bk, 32 * warp + 16 * pp + bn, TT), b0, b1, b2, b3);
 #pragma unroll
           for (int mt = 0; mt < 2; ++mt) {
             Mma<T>::run(acc[mt][2 * pp], pa[mt], b0, b1);
@@ -365,16 +343,16 @@ __global__ void __launch_bounds__(NT, 1)
         }
       }
     }
-    fence_proxy_async();  // order this thread's generic accesses of stage st before the async refill
-    __syncthreads();      // every read of stage st is done
+    fence_proxy_async();  // order this thread's shared-memory accesses before the async refill
+    __syncthreads();      // every read of stage st, P and the reduction buffers is done
     if (tid == 0 && u + 2 < u_end) issue(u + 2, st);
   }
 
   if (bad) {
     if (tid == 0) atomicExch(err, 1);
     // let copies still in flight land before the CTA's shared memory goes away
-    const int64_t issued = (u_end - u_begin) < 2 ? (u_end - u_begin) : 2;
-    for (int64_t j = k; j < k + issued && j < (u_end - u_begin); ++j) mbar_wait(&S.bar[j & 1], (uint32_t)((j >> 1) & 1));
+    const int64_t n = u_end - u_begin;
+    for (int64_t j = k; j < k + 2 && j < n; ++j) mbar_wait(&S.bar[j & 1], (uint32_t)((j >> 1) & 1));
     return;
   }
   if (cur_b >= 0) flush(cur_b);
@@ -392,7 +370,7 @@ int launch_fast(const MlaDecodeArgs& a, const MlaWorkspace& w, const MlaMaps& m)
       return B200MM_ERR_LAUNCH;
     configured[dev] = true;
   }
-  return launch_pdl(kern, dim3(w.G), dim3(NT), smem, a.stream, a, w, m.c, m.kr, m.ks) == cudaSuccess
+  return launch_pdl(kern, dim3(w.G), dim3(NT), smem, a.stream, a, w, m.c, m.kz, m.ks) == cudaSuccess
              ? B200MM_OK
              : B200MM_ERR_LAUNCH;
 }
@@ -410,7 +388,7 @@ bool mla_fast_supported(const MlaDecodeArgs& a) {
   if (a.L > (int64_t(1) << 30) || s.B < 1) return false;
   // TMA: 16-byte aligned bases and strides, rows no shorter than their content
   if (!al16(a.c_kv) || (a.c_st * 2) % 16 || (a.c_sb * 2) % 16 || a.c_st < FR) return false;
-  if (!al16(a.kr) || (a.r_st * 2) % 16 || (a.r_sb * 2) % 16 || a.r_st < FKV * FDR) return false;
+  if (!al16(a.kz) || (a.z_st * 2) % 16 || (a.z_sb * 2) % 16 || a.z_st < FKV * FDR) return false;
   if (!al16(a.kscale) || (a.s_st * 4) % 16 || (a.s_sb * 4) % 16 || a.s_st < FKV) return false;
   return true;
 }
@@ -421,10 +399,10 @@ bool mla_fast_maps(const MlaDecodeArgs& a, MlaMaps* m) {
   const uint64_t L = (uint64_t)a.L, B = (uint64_t)a.s.B;
   // a single batch row may come with any batch stride; give the map a valid one
   const uint64_t csb = B > 1 ? (uint64_t)a.c_sb * 2 : L * a.c_st * 2;
-  const uint64_t rsb = B > 1 ? (uint64_t)a.r_sb * 2 : L * a.r_st * 2;
+  const uint64_t zsb = B > 1 ? (uint64_t)a.z_sb * 2 : L * a.z_st * 2;
   const uint64_t ssb = B > 1 ? (uint64_t)a.s_sb * 4 : L * a.s_st * 4;
   return make_map_3d(&m->c, dt, a.c_kv, FR, L, B, (uint64_t)a.c_st * 2, csb, 64, TT, 1, CU_TENSOR_MAP_SWIZZLE_128B) &&
-         make_map_3d(&m->kr, dt, a.kr, FKV * FDR, L, B, (uint64_t)a.r_st * 2, rsb, 64, TT, 1,
+         make_map_3d(&m->kz, dt, a.kz, FKV * FDR, L, B, (uint64_t)a.z_st * 2, zsb, 64, TT, 1,
                      CU_TENSOR_MAP_SWIZZLE_128B) &&
          make_map_3d(&m->ks, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.kscale, FKV, L, B, (uint64_t)a.s_st * 4, ssb, FKV,
                      TT, 1, CU_TENSOR_MAP_SWIZZLE_NONE);

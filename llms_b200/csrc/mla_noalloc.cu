@@ -46,8 +46,8 @@ int scratch_address(void** out) {
 }  // namespace b200mm
 
 extern "C" int b200mm_mla_decode_noalloc(const b200mm_mla_shape* shape, const void* q, int64_t q_sb,
-                                         const void* c_kv, int64_t c_sb, int64_t c_st, const void* k_rope_pre,
-                                         int64_t r_sb, int64_t r_st, const float* kscale, int64_t s_sb,
+                                         const void* c_kv, int64_t c_sb, int64_t c_st, const void* kz,
+                                         int64_t z_sb, int64_t z_st, const float* kscale, int64_t s_sb,
                                          int64_t s_st, const void* w_uk, const void* w_uv, const float* k_norm_w,
                                          const float* rope_inv_freq, float scale, int64_t L, void* out,
                                          int64_t o_sb, void* stream) {
@@ -65,6 +65,6 @@ extern "C" int b200mm_mla_decode_noalloc(const b200mm_mla_shape* shape, const vo
   // Same kernels as b200mm_mla_decode.  They write every workspace byte they
   // read (the absorbed query, the partials and the error flag) before reading
   // it, so the array's contents from the previous call need no clearing.
-  return b200mm_mla_decode(shape, q, q_sb, c_kv, c_sb, c_st, k_rope_pre, r_sb, r_st, kscale, s_sb, s_st, w_uk, w_uv,
+  return b200mm_mla_decode(shape, q, q_sb, c_kv, c_sb, c_st, kz, z_sb, z_st, kscale, s_sb, s_st, w_uk, w_uv,
                            k_norm_w, rope_inv_freq, scale, L, out, o_sb, ws, kScratchBytes, stream);
 }

@@ -319,7 +319,7 @@ int launch_t(const DenseArgs& a) {
 
 bool tc_supported(const DenseArgs& a) {
   if (a.w8 || (a.dtype != B200MM_BF16 && a.dtype != B200MM_F16)) return false;
-  if (a.M < 128) return false;
+  if (a.M < 65) return false;
   if (!al16(a.x) || !al16(a.w0) || !al16(a.y) || (a.gate && !al16(a.w1))) return false;
   if ((a.ldx * 2) % 16 || (a.ldw0 * 2) % 16 || (a.ldy * 2) % 16 || (a.gate && (a.ldw1 * 2) % 16)) return false;
   if ((a.K * 2) % 16) return false;

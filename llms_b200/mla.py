@@ -6,17 +6,21 @@ cache (``MLAKVCache``: ``c_kv`` and ``k_rope_pre``, engine/mla.py:41-87) and
 its module parameters, and runs the attention core in one pass over the
 latent cache through ``b200mm_mla_decode``:
 
-* per-token k-RMS factors (the scalar the ``k_norm`` RMSNorm multiplies each
-  reconstructed K head by) are kept in a float32 side-band ``[B, S, KV]``
-  attached to the cache object and filled once per token by
-  ``b200mm_mla_kv_scales`` -- lazily for tokens a prefill wrote, and for the
-  new token of each decode step;
+* two per-token side-bands are attached to the cache object and filled once
+  per token by ``b200mm_mla_append`` (lazily for tokens a prefill wrote, and
+  for the new token of each decode step): the k-RMS factor ``kscale[B, S, KV]``
+  (fp32; the scalar the ``k_norm`` RMSNorm multiplies each reconstructed K
+  head by) and the RoPE'd, k_norm-weighted rope half of K, ``kz[B, S, KV, DR]``
+  (model dtype).  A decode step therefore reads the latent, ``kz`` and
+  ``kscale`` -- the same 1056 bytes per token as latent + ``k_rope_pre`` +
+  ``kscale`` -- and never rotates keys;
 * the query is absorbed through ``W_uk`` and the context is split across CTAs
   with an online-softmax merge; ``W_uv`` is applied once per head.
 
 Public pieces:
   mla_decode(...)       functional core (q already q_norm'ed)
-  mla_kv_scales(...)    side-band fill for a token range
+  mla_append(...)       side-band fill for a token range
+  mla_sidebands(...)    allocate + fill both side-bands for positions [0, L)
   B200MLAttention       drop-in module (same constructor / forward signature
                         as the reference ``MLAttention``)
   apply_b200_mla(model) in-place swap walker, mirroring ``apply_mla``
@@ -55,32 +59,50 @@ def workspace_bytes(B: int, H: int, KV: int, D: int, DR: int, R: int, L: int, dt
     return int(_capi.lib.b200mm_mla_decode_workspace_size(ctypes.byref(shp), L))
 
 
-def mla_kv_scales(c_kv: torch.Tensor, k_rope_pre: torch.Tensor | None, w_uk: torch.Tensor | None,
-                  kscale: torch.Tensor, *, B: int, t0: int, t1: int, num_kv_heads: int, head_dim: int,
-                  eps: float) -> None:
-    """Fill ``kscale[:B, t0:t1, :]`` from the cached latent / rope keys.
+def mla_append(c_kv: torch.Tensor, k_rope_pre: torch.Tensor | None, w_uk: torch.Tensor | None,
+               k_norm_w: torch.Tensor, inv_freq: torch.Tensor | None, kscale: torch.Tensor,
+               kz: torch.Tensor | None, *, B: int, t0: int, t1: int, num_kv_heads: int, head_dim: int,
+               eps: float) -> None:
+    """Fill the side-bands ``kscale[:B, t0:t1]`` and ``kz[:B, t0:t1]``.
 
-    c_kv [*, S, R]; k_rope_pre [*, S, KV, DR] or None (DR == 0);
-    w_uk [KV, DN, R] or None (DN == 0); kscale float32 [*, S, KV].
+    c_kv [*, S, R]; k_rope_pre, kz [*, S, KV, DR] or None (DR == 0);
+    w_uk [KV, DN, R] or None (DN == 0); k_norm_w fp32 [D]; inv_freq fp32
+    [DR/2]; kscale fp32 [*, S, KV].
     """
     _capi.require_cuda(c_kv, kscale)
     R = c_kv.shape[-1]
     DR = 0 if k_rope_pre is None else k_rope_pre.shape[-1]
-    shp = _shape(B, 1 * num_kv_heads, num_kv_heads, head_dim, DR, R, c_kv.dtype, eps)
+    shp = _shape(B, num_kv_heads, num_kv_heads, head_dim, DR, R, c_kv.dtype, eps)
     if kscale.dtype != torch.float32 or kscale.stride(-1) != 1:
         raise ValueError("kscale must be float32 with a dense last dim")
     with torch.cuda.device(c_kv.device):
-        st = _capi.lib.b200mm_mla_kv_scales(
+        st = _capi.lib.b200mm_mla_append(
             ctypes.byref(shp), c_kv.data_ptr(), c_kv.stride(0), c_kv.stride(1),
             _ptr(k_rope_pre), 0 if k_rope_pre is None else k_rope_pre.stride(0),
             0 if k_rope_pre is None else k_rope_pre.stride(1),
-            _ptr(w_uk), kscale.data_ptr(), kscale.stride(0), kscale.stride(1), t0, t1,
-            _capi.stream_of(c_kv),
+            _ptr(w_uk), k_norm_w.data_ptr(), _ptr(inv_freq),
+            kscale.data_ptr(), kscale.stride(0), kscale.stride(1),
+            _ptr(kz), 0 if kz is None else kz.stride(0), 0 if kz is None else kz.stride(1),
+            t0, t1, _capi.stream_of(c_kv),
         )
-    _capi.check(st, "b200mm_mla_kv_scales")
+    _capi.check(st, "b200mm_mla_append")
 
 
-def mla_decode(q: torch.Tensor, c_kv: torch.Tensor, k_rope_pre: torch.Tensor | None, kscale: torch.Tensor,
+def mla_sidebands(c_kv: torch.Tensor, k_rope_pre: torch.Tensor | None, w_uk: torch.Tensor | None,
+                  k_norm_w: torch.Tensor, inv_freq: torch.Tensor | None, *, B: int, L: int, num_kv_heads: int,
+                  head_dim: int, eps: float):
+    """Allocate the two side-bands for a cache of ``c_kv.shape[1]`` positions
+    and fill positions ``[0, L)`` of rows ``0..B-1``.  Returns (kscale, kz)."""
+    S = c_kv.shape[1]
+    DR = 0 if k_rope_pre is None else k_rope_pre.shape[-1]
+    kscale = torch.empty((c_kv.shape[0], S, num_kv_heads), dtype=torch.float32, device=c_kv.device)
+    kz = torch.empty((c_kv.shape[0], S, num_kv_heads, DR), dtype=c_kv.dtype, device=c_kv.device) if DR else None
+    mla_append(c_kv, k_rope_pre, w_uk, k_norm_w, inv_freq, kscale, kz, B=B, t0=0, t1=L,
+               num_kv_heads=num_kv_heads, head_dim=head_dim, eps=eps)
+    return kscale, kz
+
+
+def mla_decode(q: torch.Tensor, c_kv: torch.Tensor, kz: torch.Tensor | None, kscale: torch.Tensor,
                w_uk: torch.Tensor | None, w_uv: torch.Tensor, k_norm_w: torch.Tensor,
                inv_freq: torch.Tensor | None, *, L: int, scale: float, eps: float,
                out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
@@ -89,8 +111,8 @@ def mla_decode(q: torch.Tensor, c_kv: torch.Tensor, k_rope_pre: torch.Tensor | N
     Args:
         q: ``(B, H, D)`` query after ``q_norm``, before RoPE.
         c_kv: ``(*, S, R)`` latent cache (rows ``0..B-1`` used), S >= L.
-        k_rope_pre: ``(*, S, KV, DR)`` un-normed rope keys, or None if DR == 0.
-        kscale: ``(*, S, KV)`` float32 side-band, valid for positions < L.
+        kz: ``(*, S, KV, DR)`` RoPE'd key side-band, or None if DR == 0.
+        kscale: ``(*, S, KV)`` float32 side-band; both valid for positions < L.
         w_uk: ``(KV, DN, R)``, or None if DN == 0.  w_uv: ``(KV, D, R)``.
         k_norm_w: ``(D,)`` float32.  inv_freq: ``(DR/2,)`` float32.
     Returns:
@@ -99,7 +121,7 @@ def mla_decode(q: torch.Tensor, c_kv: torch.Tensor, k_rope_pre: torch.Tensor | N
     B, H, D = q.shape
     R = c_kv.shape[-1]
     KV = w_uv.shape[0]
-    DR = 0 if k_rope_pre is None else k_rope_pre.shape[-1]
+    DR = 0 if kz is None else kz.shape[-1]
     _capi.require_cuda(q, c_kv, kscale, w_uv)
     if q.stride(-1) != 1 or q.stride(1) != D:
         q = q.contiguous()
@@ -113,8 +135,7 @@ def mla_decode(q: torch.Tensor, c_kv: torch.Tensor, k_rope_pre: torch.Tensor | N
         st = _capi.lib.b200mm_mla_decode(
             ctypes.byref(shp), q.data_ptr(), q.stride(0),
             c_kv.data_ptr(), c_kv.stride(0), c_kv.stride(1),
-            _ptr(k_rope_pre), 0 if k_rope_pre is None else k_rope_pre.stride(0),
-            0 if k_rope_pre is None else k_rope_pre.stride(1),
+            _ptr(kz), 0 if kz is None else kz.stride(0), 0 if kz is None else kz.stride(1),
             kscale.data_ptr(), kscale.stride(0), kscale.stride(1),
             _ptr(w_uk), w_uv.data_ptr(), k_norm_w.data_ptr(), _ptr(inv_freq),
             float(scale), L, out.data_ptr(), out.stride(0),
@@ -139,19 +160,23 @@ class _RMSNorm(nn.Module):
         return self.weight * xf.to(x.dtype)
 
 
-def _sideband(kv_cache, layer_idx: int, KV: int, like: torch.Tensor):
-    """The float32 k-RMS side-band for ``layer_idx`` (allocated on first use)
-    and the number of leading positions it currently covers."""
+def _sideband(kv_cache, layer_idx: int, KV: int, DR: int):
+    """The side-bands of ``layer_idx`` (allocated on first use): fp32 ``kscale``
+    [max_batch, S, KV], ``kz`` [max_batch, S, KV, DR] in the cache dtype (None
+    if DR == 0), and the dict of how many leading positions they cover."""
     bands = getattr(kv_cache, "_b200_kscale", None)
     if bands is None:
         bands = {}
         kv_cache._b200_kscale = bands
+        kv_cache._b200_kz = {}
         kv_cache._b200_kscale_len = {}
     if layer_idx not in bands:
         c = kv_cache.c_kv[layer_idx]
         bands[layer_idx] = torch.empty((c.shape[0], c.shape[1], KV), dtype=torch.float32, device=c.device)
+        kv_cache._b200_kz[layer_idx] = (
+            torch.empty((c.shape[0], c.shape[1], KV, DR), dtype=c.dtype, device=c.device) if DR > 0 else None)
         kv_cache._b200_kscale_len[layer_idx] = 0
-    return bands[layer_idx], kv_cache._b200_kscale_len
+    return bands[layer_idx], kv_cache._b200_kz[layer_idx], kv_cache._b200_kscale_len
 
 
 class B200MLAttention(nn.Module):
@@ -253,13 +278,13 @@ class B200MLAttention(nn.Module):
         kr = kv_cache.k_rope_pre[layer_idx] if DR > 0 else None
         w_uk = self.uk_nope.weight.view(KV, DN, self.rank) if DN > 0 else None
         w_uv = self.uv.weight.view(KV, D, self.rank)
-        kscale, lens = _sideband(kv_cache, layer_idx, KV, c)
+        kscale, kz, lens = _sideband(kv_cache, layer_idx, KV, DR)
         valid = min(lens[layer_idx], start_pos)
-        mla_kv_scales(c, kr, w_uk, kscale, B=B, t0=valid, t1=end, num_kv_heads=KV, head_dim=D,
-                      eps=self.k_norm.eps)
-        lens[layer_idx] = end
         kw, inv = self._consts(x.device)
-        attn = mla_decode(q.view(B, H, D), c, kr, kscale, w_uk, w_uv, kw, inv, L=end, scale=D ** -0.5,
+        mla_append(c, kr, w_uk, kw, inv, kscale, kz, B=B, t0=valid, t1=end, num_kv_heads=KV, head_dim=D,
+                   eps=self.k_norm.eps)
+        lens[layer_idx] = end
+        attn = mla_decode(q.view(B, H, D), c, kz, kscale, w_uk, w_uv, kw, inv, L=end, scale=D ** -0.5,
                           eps=self.k_norm.eps)
         return self.o(attn.view(B, 1, H * D))
 

@@ -119,3 +119,15 @@ def mla_kv_scales(c_kv, k_rope_pre, w_uk, eps, D):
     if k_rope_pre is not None and k_rope_pre.shape[-1] > 0:
         ss = ss + (np.asarray(k_rope_pre, np.float64) ** 2).sum(-1)
     return 1.0 / np.sqrt(ss / D + eps)
+
+
+def mla_rope_keys(k_rope_pre, k_norm_w, inv_freq, t0=0):
+    """The RoPE'd rope half of the normed K head divided by its k_norm factor
+    (engine/mla.py:221-242 with the per-token scalar factored out):
+    rope_t(w_k[DN:] * kr_t) for positions t0, t0+1, ...  (B, T, KV, DR)."""
+    kr = np.asarray(k_rope_pre, np.float64)
+    DR = kr.shape[-1]
+    w = np.asarray(k_norm_w, np.float64)[-DR:]
+    cos, sin = rope_cos_sin(np.arange(t0, t0 + kr.shape[1]), inv_freq)
+    z = kr * w
+    return z * cos[None, :, None, :] + rotate_half(z) * sin[None, :, None, :]

@@ -217,3 +217,56 @@ def test_modules_match_eager():
     x = torch.randn(2, 3, 256, device="cuda")
     with torch.no_grad():
         torch.testing.assert_close(fused(x), eager(x), rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("M", [5, 7, 12, 24, 48, 64, 65, 100])
+@pytest.mark.parametrize("gate", [False, True])
+def test_mid_m_tensor_core_gemv(M, gate):
+    """5 <= M <= 64 runs the tensor-core GEMV (K split over a 4-CTA cluster);
+    65 <= M < 128 the tcgen05 kernel with a partly filled tile."""
+    from llms_b200.kernels import triton_fused_gate_up_silu, triton_fused_qkv
+    rng = np.random.default_rng(M + 100 * gate)
+    K, N = 2560, 1000  # N not a multiple of the 128-row group
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    w0 = rng.standard_normal((N, K), dtype=np.float32) * 0.02
+    xd, w0d = dev(x), dev(w0)
+    if gate:
+        w1d = dev(rng.standard_normal((N, K), dtype=np.float32) * 0.02)
+        y = triton_fused_gate_up_silu(xd, w0d, w1d)
+        e = O.gate_up_silu(host(xd), host(w0d), host(w1d))
+    else:
+        q, k, v = triton_fused_qkv(xd, w0d, n_q=N - 200, n_k=100)
+        y = torch.cat([q, k, v], -1)
+        e = host(xd).astype(np.float64) @ host(w0d).astype(np.float64).T
+    bf16_check(host(y), e)
+
+
+@pytest.mark.parametrize("M", [2, 5, 16, 33, 64])
+def test_mid_m_int8_and_fp16(M):
+    from llms_b200.kernels import int8_fused_gate_up_silu, int8_fused_qkv, triton_fused_qkv
+    lay = I.cfg5_layer(M=M, seed=M)
+    to = lambda a: torch.from_numpy(a[:1500]).cuda()
+    x = dev(lay["x"])
+    y = int8_fused_gate_up_silu(x, to(lay["gate_q"]), to(lay["gate_s"]), to(lay["up_q"]), to(lay["up_s"]))
+    e = O.gate_up_silu(lay["x"], O.dequant(lay["gate_q"][:1500], lay["gate_s"][:1500]),
+                       O.dequant(lay["up_q"][:1500], lay["up_s"][:1500]))
+    bf16_check(host(y), e)
+    q, k, v = int8_fused_qkv(x, to(lay["qkv_q"]), to(lay["qkv_s"]), n_q=1300, n_k=100)
+    e = lay["x"].astype(np.float64) @ O.dequant(lay["qkv_q"][:1500], lay["qkv_s"][:1500]).T
+    bf16_check(host(torch.cat([q, k, v], -1)), e)
+    xh = dev(lay["x"], torch.float16)
+    wh = dev(lay["qkv_q"][:768].astype(np.float32) * 0.01, torch.float16)
+    q, k, v = triton_fused_qkv(xh, wh, n_q=512, n_k=128)
+    e = host(xh).astype(np.float64) @ host(wh).astype(np.float64).T
+    bf16_check(host(torch.cat([q, k, v], -1)), e)
+
+
+@pytest.mark.parametrize("K", [2536, 1000])
+def test_mid_m_k_tails(K):
+    from llms_b200.kernels import triton_fused_gate_up_silu
+    rng = np.random.default_rng(K)
+    x = dev(rng.standard_normal((16, K), dtype=np.float32))
+    wg = dev(rng.standard_normal((700, K), dtype=np.float32) * 0.03)
+    wu = dev(rng.standard_normal((700, K), dtype=np.float32) * 0.03)
+    y = triton_fused_gate_up_silu(x, wg, wu)
+    bf16_check(host(y), O.gate_up_silu(host(x), host(wg), host(wu)))

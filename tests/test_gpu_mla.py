@@ -35,12 +35,15 @@ def run_kernel(d, L, dims, dtype, *, S=None, theta=1e6, eps=1e-6):
         kr[:, :L] = dev(d["k_rope_pre"][:, :L], dtype)
     w_uk = dev(d["w_uk"], dtype) if D - DR else None
     w_uv = dev(d["w_uv"], dtype)
-    ks = torch.full((B, S, KV), float("nan"), dtype=torch.float32, device="cuda")
-    mla.mla_kv_scales(c, kr, w_uk, ks, B=B, t0=0, t1=L, num_kv_heads=KV, head_dim=D, eps=eps)
     kw = dev(d["k_norm_w"], torch.float32)
     inv = mla.rope_inv_freq(D, DR, theta, "cuda") if DR else None
-    out = mla.mla_decode(dev(d["q"], dtype), c, kr, ks, w_uk, w_uv, kw, inv, L=L, scale=D ** -0.5, eps=eps)
+    # side-bands start as NaN: every position the decode reads must have been written
+    ks = torch.full((B, S, KV), float("nan"), dtype=torch.float32, device="cuda")
+    kz = torch.full((B, S, KV, DR), float("nan"), dtype=dtype, device="cuda") if DR else None
+    mla.mla_append(c, kr, w_uk, kw, inv, ks, kz, B=B, t0=0, t1=L, num_kv_heads=KV, head_dim=D, eps=eps)
+    out = mla.mla_decode(dev(d["q"], dtype), c, kz, ks, w_uk, w_uv, kw, inv, L=L, scale=D ** -0.5, eps=eps)
     torch.cuda.synchronize()
+    run_kernel.last_kz = kz
     return out, ks
 
 
@@ -75,6 +78,8 @@ def test_kv_scales_vs_oracle():
     _, ks = run_kernel(d, 100, dims, torch.bfloat16)
     e = O.mla_kv_scales(d["c_kv"], d["k_rope_pre"], d["w_uk"], 1e-6, 128)
     np.testing.assert_allclose(host(ks[:, :100]), e, rtol=2e-5, atol=0)
+    ez = O.mla_rope_keys(d["k_rope_pre"], d["k_norm_w"], O.mla_inv_freq(128, 32, 1e6), 0)
+    bf16_check(host(run_kernel.last_kz[:, :100]), ez)
 
 
 @pytest.mark.parametrize("B,L", [(1, 1), (1, 63), (1, 64), (1, 65), (1, 512), (8, 512), (2, 4096), (8, 4096),
@@ -108,10 +113,9 @@ def test_constant_cache_property():
     w_uv = torch.randn(KV, D, R, device="cuda", dtype=torch.bfloat16) * 0.25
     q = torch.randn(B, H, D, device="cuda", dtype=torch.bfloat16)
     kr[:] = kr[:, :1]  # identical rope keys too -> identical scores up to RoPE phase
-    ks = torch.empty(B, L, KV, device="cuda")
-    mla.mla_kv_scales(c, kr, w_uk, ks, B=B, t0=0, t1=L, num_kv_heads=KV, head_dim=D, eps=1e-6)
-    out = mla.mla_decode(q, c, kr, ks, w_uk, w_uv, torch.ones(D, device="cuda"),
-                         mla.rope_inv_freq(D, DR, 1e6, "cuda"), L=L, scale=D ** -0.5, eps=1e-6)
+    kw, inv = torch.ones(D, device="cuda"), mla.rope_inv_freq(D, DR, 1e6, "cuda")
+    ks, kz = mla.mla_sidebands(c, kr, w_uk, kw, inv, B=B, L=L, num_kv_heads=KV, head_dim=D, eps=1e-6)
+    out = mla.mla_decode(q, c, kz, ks, w_uk, w_uv, kw, inv, L=L, scale=D ** -0.5, eps=1e-6)
     g_of = np.arange(H) // (H // KV)
     e = np.einsum("hdr,r->hd", host(w_uv)[g_of].astype(np.float64), host(c[0, 0]).astype(np.float64))
     bf16_check(host(out), np.broadcast_to(e, (B, H, D)))

@@ -25,9 +25,9 @@ from tests.conftest import bf16_check
 pytestmark = pytest.mark.gpu
 
 
-def _args(shp, q, c, kr, ks, wuk, wuv, kw, inv, L, out):
+def _args(shp, q, c, kz, ks, wuk, wuv, kw, inv, L, out):
     return (ctypes.byref(shp), q.data_ptr(), q.stride(0), c.data_ptr(), c.stride(0), c.stride(1),
-            kr.data_ptr(), kr.stride(0), kr.stride(1), ks.data_ptr(), ks.stride(0), ks.stride(1),
+            kz.data_ptr(), kz.stride(0), kz.stride(1), ks.data_ptr(), ks.stride(0), ks.stride(1),
             wuk.data_ptr(), wuv.data_ptr(), kw.data_ptr(), inv.data_ptr(), ctypes.c_float(128 ** -0.5), L,
             out.data_ptr(), out.stride(0))
 
@@ -43,23 +43,22 @@ def test_noalloc_matches_workspace_entry_point():
         d = I.cfg4(B, L, seed=seed)
         to = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda().to(torch.bfloat16)
         c, kr, wuk, wuv, q = to(d["c_kv"]), to(d["k_rope_pre"]), to(d["w_uk"]), to(d["w_uv"]), to(d["q"])
-        ks = torch.empty(B, L, KV, device="cuda")
-        mla.mla_kv_scales(c, kr, wuk, ks, B=B, t0=0, t1=L, num_kv_heads=KV, head_dim=D, eps=1e-6)
         kw = torch.ones(D, device="cuda")
         inv = mla.rope_inv_freq(D, DR, 1e6, "cuda")
+        ks, kz = mla.mla_sidebands(c, kr, wuk, kw, inv, B=B, L=L, num_kv_heads=KV, head_dim=D, eps=1e-6)
         shp = _capi.MlaShape(B=B, H=H, KV=KV, D=D, DR=DR, R=R, dtype=2, eps=1e-6)
         stream = torch.cuda.current_stream().cuda_stream
 
         ref = torch.empty(B, H, D, device="cuda", dtype=torch.bfloat16)
         nbytes = lib.b200mm_mla_decode_workspace_size(ctypes.byref(shp), L)
         ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
-        st = lib.b200mm_mla_decode(*_args(shp, q, c, kr, ks, wuk, wuv, kw, inv, L, ref), ws.data_ptr(), nbytes,
+        st = lib.b200mm_mla_decode(*_args(shp, q, c, kz, ks, wuk, wuv, kw, inv, L, ref), ws.data_ptr(), nbytes,
                                    stream)
         assert st == 0, lib.b200mm_status_string(st)
 
         for _ in range(2):  # two calls in a row share the library's array
             out = torch.full((B, H, D), float("nan"), device="cuda", dtype=torch.bfloat16)
-            st = lib.b200mm_mla_decode_noalloc(*_args(shp, q, c, kr, ks, wuk, wuv, kw, inv, L, out), stream)
+            st = lib.b200mm_mla_decode_noalloc(*_args(shp, q, c, kz, ks, wuk, wuv, kw, inv, L, out), stream)
             assert st == 0, lib.b200mm_status_string(st)
             torch.cuda.synchronize()
             assert torch.isfinite(out.float()).all()
