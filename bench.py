@@ -328,14 +328,13 @@ def time_graph(graph, steps, warmup, world, post=None):
 
 
 def parity_layer0(job, rank, world):
-    """Layer 0 of this rank's shard vs the float64 oracle (cheap spot check)."""
-    from oracle import reference_math as O
-
-    x = job.x[0].float().cpu().numpy()
-    w = job.wqkv[0].float().cpu().numpy()
-    e = x.astype(np.float64) @ w.astype(np.float64).T
+    """Layer 0 of this rank's shard vs float64 torch math on the host (a cheap
+    spot check; the full parity suite is tests/)."""
+    x = job.x[0].double().cpu()
+    e = (x @ job.wqkv[0].double().cpu().T).numpy()
     a = job.yqkv[0].float().cpu().numpy()
-    eg = O.gate_up_silu(x, job.wg[0].float().cpu().numpy(), job.wu[0].float().cpu().numpy())
+    g = x @ job.wg[0].double().cpu().T
+    eg = (g / (1 + torch.exp(-g)) * (x @ job.wu[0].double().cpu().T)).numpy()
     ag = job.yffn[0].float().cpu().numpy()
     md = max(float(np.abs(a - e).max()), float(np.abs(ag - eg).max()))
     rl = max(float(np.linalg.norm(a - e) / np.linalg.norm(e)), float(np.linalg.norm(ag - eg) / np.linalg.norm(eg)))
@@ -447,7 +446,57 @@ def suite(job):
                                                "side-band + weights + q/out"}
         del g, c, kz, ks, ws
     torch.cuda.empty_cache()
+    out.update(qwen3_8b_int8_decode())
     return out
+
+
+def qwen3_8b_int8_decode(batches=(1, 16, 64), prompt=16):
+    """a Qwen3-8B-shaped (36 layers, random init) decode
+    step with int8 fused QKV / gate-up (per-row scales), bf16 elsewhere.
+    One step = the whole model for one new token per sequence, replayed as a
+    CUDA graph; tok/s = batch / step time.  Greedy agreement is checked
+    against the same model in fp32 with dequantised weights on rows whose
+    fp32 top-2 gap exceeds 4x the observed logit error."""
+    from llms_b200.qwen3 import greedy, synthetic_int8_model
+
+    model = synthetic_int8_model(seed=4)
+    res = {}
+    for B in batches:
+        g = torch.Generator(device="cuda").manual_seed(100 + B)
+        ids = torch.randint(0, model.shape.vocab_size, (B, prompt), generator=g, device="cuda")
+        nxt = torch.randint(0, model.shape.vocab_size, (B, 1), generator=g, device="cuda")
+        with torch.inference_mode():
+            cache = model.alloc_cache(prompt + 8, max_batch=B)
+            model(ids, cache, start_pos=0)
+            logits = model(nxt, cache, start_pos=prompt)[:, -1].float()
+            ref_cache = model.alloc_cache(prompt + 8, max_batch=B, dtype=torch.float32)
+            model.forward_fp32_dequant(ids, ref_cache, 0)
+            ref = model.forward_fp32_dequant(nxt, ref_cache, prompt)[:, -1]
+            del ref_cache
+            err = (logits - ref).abs().max().item()
+            top2 = ref.topk(2, dim=-1).values
+            decided = (top2[:, 0] - top2[:, 1]) > 4 * err
+            agree = greedy(logits) == greedy(ref)
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                model(nxt, cache, start_pos=prompt)
+            torch.cuda.current_stream().wait_stream(s)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                model(nxt, cache, start_pos=prompt)
+            sec = time_graph(graph, 20, 3, 1)
+            del graph, cache
+        res[f"qwen3_8b_int8_decode_b{B}"] = {
+            "ms_per_step": sec / 20 * 1e3, "tok/s": B * 20 / sec,
+            "argmax_agree_decided": bool(agree[decided].all().item()),
+            "decided_rows": int(decided.sum().item()), "rows": B,
+            "argmax_agree_all": float(agree.float().mean().item()),
+            "logits_rel_l2": float(((logits - ref).norm() / ref.norm()).item()),
+        }
+    del model
+    torch.cuda.empty_cache()
+    return res
 
 
 def measured_peaks():

@@ -1,0 +1,273 @@
+"""Qwen3-shaped decoder around the B200 projections (caller of the hot path).
+
+The reference engine's model (engine/model.py:27-185) restated just far
+enough to run a decode step: embedding, decoder blocks (pre-norm GQA
+attention with QK-norm and RoPE, SwiGLU FFN), final norm, LM head, and the
+contiguous KV cache of engine/kv_cache.py.  Module and parameter names match
+the reference, so `apply_triton_kernels` / `apply_int8_kernels` swap the same
+attributes they swap in the reference engine.
+
+`synthetic_int8_model` builds BASELINE config 5 directly in int8
+(per-output-row scales), without materialising a bf16 copy of the fused
+projections, and `Qwen3Model.forward_fp32_dequant` is the fp32 check path:
+the same model run eagerly in fp32 with every int8 weight dequantised, one
+layer at a time, TF32 disabled.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from .kernels._eager import rope
+from .kernels.quant import Int8Attention, Int8FFN, dequantize_per_row
+
+
+@dataclass(frozen=True)
+class Qwen3Shape:
+    vocab_size: int = 151936
+    hidden_size: int = 4096
+    num_hidden_layers: int = 36
+    num_attention_heads: int = 32
+    num_key_value_heads: int = 8
+    head_dim: int = 128
+    intermediate_size: int = 12288
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 1e6
+    max_position_embeddings: int = 4096
+
+
+QWEN3_8B = Qwen3Shape()
+
+
+class RMSNorm(nn.Module):
+    """fp32 normalise, cast back, multiply by the weight (engine/attention.py:20-33)."""
+
+    def __init__(self, dim: int, eps: float) -> None:
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(dim))
+        self.eps = eps
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        xf = x.float()
+        xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
+        return self.weight * xf.to(x.dtype)
+
+
+@dataclass
+class KVCache:
+    """Per-layer (max_batch, num_kv_heads, max_seq_len, head_dim) K and V."""
+
+    k: list
+    v: list
+    cur_len: int = 0
+
+    @classmethod
+    def alloc(cls, *, num_layers, max_batch, num_kv_heads, max_seq_len, head_dim, dtype, device) -> "KVCache":
+        shape = (max_batch, num_kv_heads, max_seq_len, head_dim)
+        return cls(k=[torch.zeros(shape, dtype=dtype, device=device) for _ in range(num_layers)],
+                   v=[torch.zeros(shape, dtype=dtype, device=device) for _ in range(num_layers)])
+
+
+def rope_tables(head_dim: int, max_pos: int, theta: float, device=None):
+    """cos/sin (max_pos, head_dim), concat convention (engine/attention.py:36-55)."""
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim))
+    ang = torch.outer(torch.arange(max_pos, dtype=torch.float32), inv)
+    emb = torch.cat([ang, ang], dim=-1)
+    return emb.cos().to(device), emb.sin().to(device)
+
+
+def attention_core(q, k, v, kv_cache, layer_idx, start_pos, n_rep):
+    """Cache write + GQA SDPA of engine/attention.py:122-149 (q, k, v: B, H, T, D)."""
+    B, _, T, _ = q.shape
+    end = start_pos + T
+    kv_cache.k[layer_idx][:B, :, start_pos:end] = k
+    kv_cache.v[layer_idx][:B, :, start_pos:end] = v
+    fk = kv_cache.k[layer_idx][:B, :, :end]
+    fv = kv_cache.v[layer_idx][:B, :, :end]
+    if n_rep > 1:
+        fk = fk.repeat_interleave(n_rep, dim=1)
+        fv = fv.repeat_interleave(n_rep, dim=1)
+    if T == 1:
+        return F.scaled_dot_product_attention(q, fk, fv, is_causal=False)
+    qp = torch.arange(start_pos, end, device=q.device).unsqueeze(1)
+    kp = torch.arange(0, end, device=q.device).unsqueeze(0)
+    return F.scaled_dot_product_attention(q, fk, fv, attn_mask=qp >= kp)
+
+
+class Attention(nn.Module):
+    """Eager GQA attention with QK-norm and RoPE (engine/attention.py:79-163)."""
+
+    def __init__(self, shape: Qwen3Shape) -> None:
+        super().__init__()
+        H, KV, D, C = shape.num_attention_heads, shape.num_key_value_heads, shape.head_dim, shape.hidden_size
+        self.num_heads, self.num_kv_heads, self.head_dim = H, KV, D
+        self.q = nn.Linear(C, H * D, bias=False)
+        self.k = nn.Linear(C, KV * D, bias=False)
+        self.v = nn.Linear(C, KV * D, bias=False)
+        self.o = nn.Linear(H * D, C, bias=False)
+        self.q_norm = RMSNorm(D, shape.rms_norm_eps)
+        self.k_norm = RMSNorm(D, shape.rms_norm_eps)
+
+    def forward(self, x, *, kv_cache, layer_idx, cos, sin, start_pos):
+        B, T, _ = x.shape
+        q = self.q_norm(self.q(x).view(B, T, self.num_heads, self.head_dim)).transpose(1, 2)
+        k = self.k_norm(self.k(x).view(B, T, self.num_kv_heads, self.head_dim)).transpose(1, 2)
+        v = self.v(x).view(B, T, self.num_kv_heads, self.head_dim).transpose(1, 2)
+        q, k = rope(q, cos, sin), rope(k, cos, sin)
+        a = attention_core(q, k, v, kv_cache, layer_idx, start_pos, self.num_heads // self.num_kv_heads)
+        return self.o(a.transpose(1, 2).reshape(B, T, self.num_heads * self.head_dim))
+
+
+class FFN(nn.Module):
+    """SwiGLU: down(silu(gate(x)) * up(x)) (engine/model.py:27-37)."""
+
+    def __init__(self, hidden: int, inter: int) -> None:
+        super().__init__()
+        self.gate = nn.Linear(hidden, inter, bias=False)
+        self.up = nn.Linear(hidden, inter, bias=False)
+        self.down = nn.Linear(inter, hidden, bias=False)
+
+    def forward(self, x):
+        return self.down(F.silu(self.gate(x)) * self.up(x))
+
+
+class DecoderBlock(nn.Module):
+    def __init__(self, shape: Qwen3Shape, *, build_projections: bool = True) -> None:
+        super().__init__()
+        self.norm1 = RMSNorm(shape.hidden_size, shape.rms_norm_eps)
+        self.norm2 = RMSNorm(shape.hidden_size, shape.rms_norm_eps)
+        if build_projections:
+            self.attn = Attention(shape)
+            self.ffn = FFN(shape.hidden_size, shape.intermediate_size)
+
+    def forward(self, x, *, kv_cache, layer_idx, cos, sin, start_pos):
+        h = x + self.attn(self.norm1(x), kv_cache=kv_cache, layer_idx=layer_idx, cos=cos, sin=sin,
+                          start_pos=start_pos)
+        return h + self.ffn(self.norm2(h))
+
+
+class Qwen3Model(nn.Module):
+    """engine/model.py:76-185 (untied LM head)."""
+
+    def __init__(self, shape: Qwen3Shape, *, build_projections: bool = True) -> None:
+        super().__init__()
+        self.shape = shape
+        self.embed = nn.Embedding(shape.vocab_size, shape.hidden_size)
+        self.layers = nn.ModuleList(
+            [DecoderBlock(shape, build_projections=build_projections) for _ in range(shape.num_hidden_layers)])
+        self.final_norm = RMSNorm(shape.hidden_size, shape.rms_norm_eps)
+        self.lm_head = nn.Linear(shape.hidden_size, shape.vocab_size, bias=False)
+        cos, sin = rope_tables(shape.head_dim, shape.max_position_embeddings, shape.rope_theta)
+        self.register_buffer("rope_cos", cos, persistent=False)
+        self.register_buffer("rope_sin", sin, persistent=False)
+
+    def forward(self, input_ids, kv_cache, start_pos=None):
+        if start_pos is None:
+            start_pos = kv_cache.cur_len
+        T = input_ids.shape[1]
+        h = self.embed(input_ids)
+        cos = self.rope_cos[start_pos:start_pos + T].to(h.dtype)
+        sin = self.rope_sin[start_pos:start_pos + T].to(h.dtype)
+        for i, layer in enumerate(self.layers):
+            h = layer(h, kv_cache=kv_cache, layer_idx=i, cos=cos, sin=sin, start_pos=start_pos)
+        logits = self.lm_head(self.final_norm(h))
+        kv_cache.cur_len = start_pos + T
+        return logits
+
+    def alloc_cache(self, max_seq_len, *, max_batch=1, dtype=None, device=None) -> KVCache:
+        p = self.lm_head.weight
+        return KVCache.alloc(num_layers=len(self.layers), max_batch=max_batch,
+                             num_kv_heads=self.shape.num_key_value_heads, max_seq_len=max_seq_len,
+                             head_dim=self.shape.head_dim, dtype=dtype or p.dtype, device=device or p.device)
+
+    # ---- fp32 check path ----------------------------------------------------
+    @torch.no_grad()
+    def forward_fp32_dequant(self, input_ids, kv_cache, start_pos):
+        """The same forward in fp32 eager torch, every int8 weight dequantised
+        (W = q * s), one layer at a time; TF32 off.  `kv_cache` must be fp32."""
+        prev = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = False
+        try:
+            S = self.shape
+            T = input_ids.shape[1]
+            h = self.embed(input_ids).float()
+            cos = self.rope_cos[start_pos:start_pos + T].float()
+            sin = self.rope_sin[start_pos:start_pos + T].float()
+            nq, nk = S.num_attention_heads * S.head_dim, S.num_key_value_heads * S.head_dim
+            for i, blk in enumerate(self.layers):
+                a, f = blk.attn, blk.ffn
+                B = h.shape[0]
+                x = blk.norm1(h)
+                W = dequantize_per_row(a.q_qkv, a.s_qkv)
+                y = x @ W.T
+                del W
+                q = y[..., :nq].view(B, T, S.num_attention_heads, S.head_dim)
+                k = y[..., nq:nq + nk].view(B, T, S.num_key_value_heads, S.head_dim)
+                v = y[..., nq + nk:].view(B, T, S.num_key_value_heads, S.head_dim)
+                q = a.q_norm(q).float().transpose(1, 2)
+                k = a.k_norm(k).float().transpose(1, 2)
+                v = v.transpose(1, 2)
+                q, k = rope(q, cos, sin), rope(k, cos, sin)
+                att = attention_core(q, k, v, kv_cache, i, start_pos, S.num_attention_heads // S.num_key_value_heads)
+                h = h + att.transpose(1, 2).reshape(B, T, nq) @ a.o.weight.float().T
+                x = blk.norm2(h)
+                g = x @ dequantize_per_row(f.qg, f.sg).T
+                u = x @ dequantize_per_row(f.qu, f.su).T
+                h = h + (F.silu(g) * u) @ f.down.weight.float().T
+            return self.final_norm(h) @ self.lm_head.weight.float().T
+        finally:
+            torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+def greedy(logits: torch.Tensor) -> torch.Tensor:
+    """Argmax along the vocabulary (engine/sampler.py:17-19)."""
+    return logits.argmax(dim=-1)
+
+
+@torch.no_grad()
+def synthetic_int8_model(shape: Qwen3Shape = QWEN3_8B, *, seed: int = 4, device="cuda",
+                         dtype=torch.bfloat16) -> Qwen3Model:
+    """fused QKV and gate/up weights int8 ~ U{-127..127}
+    with per-output-row scales ~ U(1e-4, 1e-3); everything else (embedding,
+    o, down, LM head) bf16 ~ N(0, 0.02), norms 1.  Seeded on `device`."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    m = Qwen3Model(shape, build_projections=False)
+    m.to(device=device, dtype=dtype)
+    C, I = shape.hidden_size, shape.intermediate_size
+    H, KV, D = shape.num_attention_heads, shape.num_key_value_heads, shape.head_dim
+
+    def normal_(t):
+        t.copy_(torch.randn(t.shape, generator=g, device=device, dtype=torch.float32) * 0.02)
+
+    def int8(n, k):
+        q = torch.randint(-127, 128, (n, k), generator=g, device=device, dtype=torch.int8)
+        s = torch.rand(n, generator=g, device=device) * 9e-4 + 1e-4
+        return q, s
+
+    normal_(m.embed.weight)
+    normal_(m.lm_head.weight)
+    for blk in m.layers:
+        att = Int8Attention.__new__(Int8Attention)
+        nn.Module.__init__(att)
+        att.hidden_size, att.num_heads, att.num_kv_heads, att.head_dim = C, H, KV, D
+        att.n_q, att.n_k = H * D, KV * D
+        q, s = int8(H * D + 2 * KV * D, C)
+        att.register_buffer("q_qkv", q)
+        att.register_buffer("s_qkv", s)
+        att.o = nn.Linear(H * D, C, bias=False).to(device=device, dtype=dtype)
+        normal_(att.o.weight)
+        att.q_norm = RMSNorm(D, shape.rms_norm_eps).to(device=device, dtype=dtype)
+        att.k_norm = RMSNorm(D, shape.rms_norm_eps).to(device=device, dtype=dtype)
+        ffn = Int8FFN.__new__(Int8FFN)
+        nn.Module.__init__(ffn)
+        for name, (qq, ss) in (("g", int8(I, C)), ("u", int8(I, C))):
+            ffn.register_buffer("q" + name, qq)
+            ffn.register_buffer("s" + name, ss)
+        ffn.down = nn.Linear(I, C, bias=False).to(device=device, dtype=dtype)
+        normal_(ffn.down.weight)
+        blk.attn, blk.ffn = att, ffn
+    return m.eval()

@@ -1,0 +1,76 @@
+"""Qwen3-8B-shaped int8 decode step: the model with the
+int8 fused projections agrees with the same model run in fp32 with
+dequantised weights, and its greedy next token matches wherever the fp32
+top-2 gap exceeds the bf16 noise floor."""
+
+import dataclasses
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def model4():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from llms_b200.qwen3 import QWEN3_8B, synthetic_int8_model
+    shape = dataclasses.replace(QWEN3_8B, num_hidden_layers=4, max_position_embeddings=256)
+    return synthetic_int8_model(shape, seed=4)
+
+
+@pytest.mark.parametrize("B", [1, 16, 64])
+def test_int8_decode_step_matches_fp32_dequant(model4, B):
+    from llms_b200.qwen3 import greedy
+    m = model4
+    g = torch.Generator(device="cuda").manual_seed(B)
+    P = 12
+    prompt = torch.randint(0, m.shape.vocab_size, (B, P), generator=g, device="cuda")
+    nxt = torch.randint(0, m.shape.vocab_size, (B, 1), generator=g, device="cuda")
+    with torch.inference_mode():
+        cache = m.alloc_cache(P + 4, max_batch=B)
+        m(prompt, cache, start_pos=0)
+        logits = m(nxt, cache, start_pos=P)[:, -1].float()
+        ref_cache = m.alloc_cache(P + 4, max_batch=B, dtype=torch.float32)
+        m.forward_fp32_dequant(prompt, ref_cache, 0)
+        ref = m.forward_fp32_dequant(nxt, ref_cache, P)[:, -1]
+    err = (logits - ref).abs().max().item()
+    scale = ref.abs().max().item()
+    rel = ((logits - ref).norm() / ref.norm()).item()
+    assert rel < 2e-2, f"logits rel-L2 {rel:.3e} (max abs {err:.3e}, |ref| max {scale:.3e})"
+    top2 = ref.topk(2, dim=-1).values
+    gap = top2[:, 0] - top2[:, 1]
+    decided = gap > 4 * err  # rows whose argmax is not within the bf16 noise floor
+    ours, theirs = greedy(logits), greedy(ref)
+    assert decided.any(), "every row is a near-tie; widen the test"
+    assert torch.equal(ours[decided], theirs[decided]), (
+        f"argmax differs on decided rows: {(ours != theirs)[decided].sum().item()} of {decided.sum().item()}")
+
+
+def test_swap_kernels_on_eager_model():
+    """apply_int8_kernels on the eager model: the int8 model's output equals an
+    eager model holding the dequantised weights."""
+    from llms_b200.kernels import apply_int8_kernels, dequantize_per_row
+    from llms_b200.qwen3 import Qwen3Model, Qwen3Shape
+    shape = Qwen3Shape(vocab_size=512, hidden_size=256, num_hidden_layers=2, num_attention_heads=4,
+                       num_key_value_heads=2, head_dim=64, intermediate_size=512, max_position_embeddings=64)
+    torch.manual_seed(0)
+    m = Qwen3Model(shape).cuda().to(torch.bfloat16).eval()
+    for p in m.parameters():
+        torch.nn.init.normal_(p, std=0.05)
+    ids = torch.randint(0, 512, (2, 6), device="cuda")
+    with torch.inference_mode():
+        eager = m(ids, m.alloc_cache(16, max_batch=2), start_pos=0).float()
+        apply_int8_kernels(m)
+        ref = Qwen3Model(shape).cuda().to(torch.bfloat16).eval()
+        ref.load_state_dict({k: v for k, v in m.state_dict().items() if k in ref.state_dict()}, strict=False)
+        for rb, mb in zip(ref.layers, m.layers):
+            W = dequantize_per_row(mb.attn.q_qkv, mb.attn.s_qkv).to(torch.bfloat16)
+            rb.attn.q.weight.copy_(W[:256]); rb.attn.k.weight.copy_(W[256:384]); rb.attn.v.weight.copy_(W[384:])
+            rb.ffn.gate.weight.copy_(dequantize_per_row(mb.ffn.qg, mb.ffn.sg).to(torch.bfloat16))
+            rb.ffn.up.weight.copy_(dequantize_per_row(mb.ffn.qu, mb.ffn.su).to(torch.bfloat16))
+        r = ref(ids, ref.alloc_cache(16, max_batch=2), start_pos=0).float()
+        q = m(ids, m.alloc_cache(16, max_batch=2), start_pos=0).float()
+    assert ((q - r).norm() / r.norm()).item() < 2e-2
+    assert ((q - eager).norm() / eager.norm()).item() < 0.2  # int8 rounding of the weights
