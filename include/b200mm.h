@@ -216,7 +216,7 @@ int b200mm_mla_decode(const b200mm_mla_shape* shape,
  * owns every allocation): same arguments minus the workspace, same kernels,
  * same results.  The workspace comes from one array compiled into the library
  * (8 MiB, 256-byte aligned; B = 32, L = 32768 at the Qwen3-4B MLA shape needs
- * about 7.1 MiB).  Every GPU that loads the library holds that array until the
+ * about 7.8 MiB).  Every GPU that loads the library holds that array until the
  * process exits.
  *   - A call whose workspace would exceed 8 MiB returns B200MM_ERR_WORKSPACE
  *     and launches nothing (b200mm_mla_decode_workspace_size gives the need).

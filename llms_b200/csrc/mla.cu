@@ -97,66 +97,94 @@ __global__ void __launch_bounds__(kThreads) mla_append_kernel(const MlaAppendArg
 }
 
 // --- absorbed query --------------------------------------------------------
-// grid: (H, B); block 256.
+// grid: (KV, B); block 256.  One CTA per (batch row, group): W_uk,g is staged
+// in shared memory (16-byte loads, up to 48 KB of rows per pass) and serves
+// all H/KV heads of the group; a thread owns one latent column and keeps the
+// heads' sums as independent accumulators.
+//   qt[b,h,r] = sum_i W_uk[g,i,r] * k_norm_w[i] * q[b,h,i]     (i < DN)
+//   qr[b,h,:] = rope_{L-1}(q[b,h,DN:])
+__host__ __device__ inline int absorb_chunk_rows(int R, int esz, int DN) {
+  const int rows = 49152 / (R * esz);
+  return rows < 1 ? 1 : (rows < DN ? rows : (DN > 0 ? DN : 1));
+}
+
+size_t absorb_smem_bytes(const b200mm_mla_shape& s) {
+  const int hpg = s.H / s.KV, DN = s.D - s.DR;
+  const int esz = s.dtype == B200MM_F32 ? 4 : 2;
+  return sizeof(float) * ((size_t)hpg * s.D + (size_t)hpg * s.R) + (size_t)absorb_chunk_rows(s.R, esz, DN) * s.R * esz +
+         16;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads) mla_absorb_kernel(const MlaDecodeArgs a, MlaWorkspace w) {
   extern __shared__ float sm[];
   const int H = a.s.H, KV = a.s.KV, D = a.s.D, DR = a.s.DR, DN = D - DR, R = a.s.R;
-  const int h = blockIdx.x, b = blockIdx.y, g = h / (H / KV);
-  float* qn = sm;  // [D]
-  const T* q = static_cast<const T*>(a.q) + (int64_t)b * a.q_sb + (int64_t)h * D;
+  const int hpg = H / KV, g = blockIdx.x, b = blockIdx.y, h0 = g * hpg;
+  const int IC = absorb_chunk_rows(R, (int)sizeof(T), DN);
+  float* qn = sm;                 // [hpg][D]   q, times k_norm_w on the first DN dims
+  float* acc = qn + hpg * D;      // [hpg][R]
+  T* wch = reinterpret_cast<T*>((reinterpret_cast<uintptr_t>(acc + hpg * R) + 15) & ~uintptr_t(15));  // [IC][R]
   float* ws = static_cast<float*>(a.ws);
-  float* qt = ws + w.off_qt / 4 + ((int64_t)b * H + h) * R;
-  float* qr = ws + w.off_qr / 4 + ((int64_t)b * H + h) * DR;
 
   pdl_trigger();
   pdl_wait();
   if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0)
     *reinterpret_cast<int*>(static_cast<unsigned char*>(a.ws) + w.off_err) = 0;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) qn[d] = ldf(q, d);
-  __syncthreads();
-  // qt[r] = sum_i W_uk[g, i, r] * w_k[i] * q[i]: warps split i, lanes split r,
-  // so each thread issues its loads back to back; partial sums meet in shared memory.
-  {
-    const T* wuk = static_cast<const T*>(a.w_uk) + (int64_t)g * DN * R;
-    float* part = sm + D;  // [nwarps][R]
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    const int per = (DN + nw - 1) / nw, i0 = warp * per, i1 = min(DN, i0 + per);
-    for (int r0 = 0; r0 < R; r0 += 32 * 8) {
-      float acc[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-      for (int i = i0; i < i1; ++i) {
-        const float qi = a.k_norm_w[i] * qn[i];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int r = r0 + lane + 32 * j;
-          if (r < R) acc[j] = fmaf(ldf(wuk, (int64_t)i * R + r), qi, acc[j]);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int r = r0 + lane + 32 * j;
-        if (r < R) part[warp * R + r] = acc[j];
-      }
+  const T* q = static_cast<const T*>(a.q) + (int64_t)b * a.q_sb + (int64_t)h0 * D;
+  for (int i = threadIdx.x; i < hpg * D; i += blockDim.x) {
+    const int d = i % D;
+    const float v = ldf(q, i);
+    qn[i] = d < DN ? a.k_norm_w[d] * v : v;
+  }
+  for (int i = threadIdx.x; i < hpg * R; i += blockDim.x) acc[i] = 0.f;
+  const T* wuk = static_cast<const T*>(a.w_uk) + (int64_t)g * DN * R;
+  constexpr int HB = 8;  // heads accumulated together per pass (independent FMA chains)
+  for (int i0 = 0; i0 < DN; i0 += IC) {
+    const int ni = min(IC, DN - i0);
+    __syncthreads();
+    {
+      const T* src = wuk + (int64_t)i0 * R;
+      constexpr int VE = 16 / sizeof(T);
+      const int n16 = ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) ? (ni * R) / VE : 0;
+#pragma unroll 4
+      for (int e = threadIdx.x; e < n16; e += blockDim.x)
+        reinterpret_cast<uint4*>(wch)[e] = reinterpret_cast<const uint4*>(src)[e];
+      for (int e = n16 * VE + threadIdx.x; e < ni * R; e += blockDim.x) wch[e] = src[e];
     }
     __syncthreads();
-    for (int r = threadIdx.x; r < R; r += blockDim.x) {
-      float v = 0.f;
-      for (int w2 = 0; w2 < nw; ++w2) v += part[w2 * R + r];
-      qt[r] = v;
+    for (int hb = 0; hb < hpg; hb += HB) {
+      for (int r = threadIdx.x; r < R; r += blockDim.x) {
+        float v[HB];
+#pragma unroll
+        for (int j = 0; j < HB; ++j) v[j] = 0.f;
+#pragma unroll 4
+        for (int i = 0; i < ni; ++i) {
+          const float wv = to_f<T>(wch[i * R + r]);
+#pragma unroll
+          for (int j = 0; j < HB; ++j)
+            if (hb + j < hpg) v[j] = fmaf(wv, qn[(hb + j) * D + i0 + i], v[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < HB; ++j)
+          if (hb + j < hpg) acc[(hb + j) * R + r] += v[j];
+      }
     }
   }
+  __syncthreads();
+  float* qt = ws + w.off_qt / 4 + ((int64_t)b * H + h0) * R;
+  for (int o = threadIdx.x; o < hpg * R; o += blockDim.x) qt[o] = acc[o];
   // qr = rope at position L-1 (rotate-half convention, angle = pos * inv_freq)
   const int half = DR / 2;
   const float pos = (float)(a.L - 1);
-  for (int j = threadIdx.x; j < DR; j += blockDim.x) {
+  float* qr = ws + w.off_qr / 4 + ((int64_t)b * H + h0) * DR;
+  for (int o = threadIdx.x; o < hpg * DR; o += blockDim.x) {
+    const int hh = o / DR, j = o % DR;
     const int i = j < half ? j : j - half;
     float sn, cs;
     sincosf(pos * a.inv_freq[i], &sn, &cs);
-    const float x = qn[DN + j];
-    const float rot = j < half ? -qn[DN + j + half] : qn[DN + j - half];
-    qr[j] = x * cs + rot * sn;
+    const float* qh = qn + hh * D + DN;
+    const float rot = j < half ? -qh[j + half] : qh[j - half];
+    qr[o] = qh[j] * cs + rot * sn;
   }
 }
 
@@ -263,30 +291,31 @@ __global__ void __launch_bounds__(kThreads) mla_split_kernel(const MlaDecodeArgs
   }
 }
 
-// --- combine: merge partials, apply W_uv ----------------------------------
-// grid: (H, B); block 256.  Partials of row b: slot i + b for every range i
-// overlapping [b*ntiles, (b+1)*ntiles).
+// --- combine, step 1: merge the split partials ---------------------------
+// grid: (H, B, rchunks); block 256.  Partials of row b: slot i + b for every
+// range i overlapping [b*ntiles, (b+1)*ntiles).  Warps split the partials,
+// lanes split the latent chunk; av[b,h,:] = sum_k e^(m_k - M) acc_k / sum_k e^(m_k - M) l_k.
 template <typename T>
-__global__ void __launch_bounds__(kThreads) mla_combine_kernel(const MlaDecodeArgs a, MlaWorkspace w) {
+__global__ void __launch_bounds__(kThreads) mla_merge_kernel(const MlaDecodeArgs a, MlaWorkspace w) {
   extern __shared__ float sm[];
-  const int H = a.s.H, KV = a.s.KV, D = a.s.D, R = a.s.R;
-  const int h = blockIdx.x, b = blockIdx.y, g = h / (H / KV);
-  float* av = sm;          // [R]
-  float* wgt = sm + R;     // [G + 1] merge weight per range (0 if not overlapping)
+  const int H = a.s.H, R = a.s.R;
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int rw = (R + w.rchunks - 1) / w.rchunks, r0 = blockIdx.z * rw, r1 = min(R, r0 + rw);
   const float* ws = static_cast<const float*>(a.ws);
   const float* pml = ws + w.off_pml / 4;
   const float* pacc = ws + w.off_pacc / 4;
   const int64_t lo = (int64_t)b * w.ntiles, hi = lo + w.ntiles;
+  const int i0 = (int)(((lo + 1) * w.G - 1) / w.T);  // ranges overlapping [lo, hi)
+  const int i1 = (int)((hi * w.G - 1) / w.T);
+  const int n = i1 - i0 + 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  float* wgt = sm;                 // [n]
+  float* part = sm + w.G + 1;      // [nw][rw]
+  __shared__ float s_inv_l;
 
   pdl_trigger();
   pdl_wait();
-  __shared__ float s_inv_l;
-  // ranges overlapping [lo, hi): range i holds units [floor(i*T/G), floor((i+1)*T/G))
-  const int i0 = (int)(((lo + 1) * w.G - 1) / w.T);
-  const int i1 = (int)((hi * w.G - 1) / w.T);
-  const int n = i1 - i0 + 1;
-  if (threadIdx.x < 32) {
-    const int lane = threadIdx.x;
+  if (warp == 0) {
     float mx = -INFINITY;
     for (int k = lane; k < n; k += 32) mx = fmaxf(mx, pml[(((int64_t)i0 + k + b) * H + h) * 2]);
 #pragma unroll
@@ -302,54 +331,78 @@ __global__ void __launch_bounds__(kThreads) mla_combine_kernel(const MlaDecodeAr
     if (lane == 0) s_inv_l = 1.f / l;
   }
   __syncthreads();
-  {
-    // warps split the partials, lanes split the rank; per-warp sums meet in shared memory
-    float* part = wgt + w.G + 1;  // [nwarps][R]
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    for (int r0 = 0; r0 < R; r0 += 32 * 8) {
-      float acc[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-      for (int k = warp; k < n; k += nw) {
-        const float wk = wgt[k];
-        const float* pc = pacc + (((int64_t)i0 + k + b) * H + h) * R;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int r = r0 + lane + 32 * j;
-          if (r < R) acc[j] = fmaf(wk, pc[r], acc[j]);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int r = r0 + lane + 32 * j;
-        if (r < R) part[warp * R + r] = acc[j];
-      }
+  const int64_t step = (int64_t)H * R;
+  for (int rr = r0 + lane; rr < r1; rr += 32) {
+    const float* pc = pacc + (((int64_t)i0 + b) * H + h) * R + rr;
+    float v0 = 0.f, v1 = 0.f;
+    int k = warp;
+    for (; k + nw < n; k += 2 * nw) {
+      const float p0 = pc[k * step], p1 = pc[(k + nw) * step];
+      v0 = fmaf(wgt[k], p0, v0);
+      v1 = fmaf(wgt[k + nw], p1, v1);
     }
-    __syncthreads();
-    for (int r = threadIdx.x; r < R; r += blockDim.x) {
-      float v = 0.f;
-      for (int w2 = 0; w2 < nw; ++w2) v += part[w2 * R + r];
-      av[r] = v * s_inv_l;
-    }
+    if (k < n) v0 = fmaf(wgt[k], pc[k * step], v0);
+    part[warp * rw + (rr - r0)] = v0 + v1;
   }
   __syncthreads();
-  const T* wuv = static_cast<const T*>(a.w_uv) + (int64_t)g * D * R;
-  T* out = static_cast<T*>(a.out) + (int64_t)b * a.o_sb + (int64_t)h * D;
+  float* av = const_cast<float*>(ws) + w.off_av / 4 + ((int64_t)b * H + h) * R;
+  for (int rr = r0 + threadIdx.x; rr < r1; rr += blockDim.x) {
+    float v = 0.f;
+    for (int q = 0; q < nw; ++q) v += part[q * rw + (rr - r0)];
+    av[rr] = v * s_inv_l;
+  }
+}
+
+// --- combine, step 2: out[b,h,:] = W_uv,g . av[b,h,:] ----------------------
+// grid: (KV, B); block 256.  One CTA per (row, group): the group's heads share
+// W_uv,g, read once with 16-byte loads when the rank allows.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) mla_combine_kernel(const MlaDecodeArgs a, MlaWorkspace w) {
+  extern __shared__ float sm[];
+  const int H = a.s.H, KV = a.s.KV, D = a.s.D, R = a.s.R;
+  const int hpg = H / KV, g = blockIdx.x, b = blockIdx.y, h0 = g * hpg;
+  float* av = sm;  // [hpg][R]
+  pdl_trigger();
+  pdl_wait();
+  const float* src = static_cast<const float*>(a.ws) + w.off_av / 4 + ((int64_t)b * H + h0) * R;
+  for (int o = threadIdx.x; o < hpg * R; o += blockDim.x) av[o] = src[o];
+  __syncthreads();
   // a split kernel that gave up on a bounded wait leaves NaN, never a silent result
   const bool failed = *reinterpret_cast<const int*>(static_cast<const unsigned char*>(a.ws) + w.off_err) != 0;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (int d0 = warp * 4; d0 < D; d0 += nw * 4) {  // 4 rows per step: more loads in flight
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int r = lane; r < R; r += 32) {
-      const float ar = av[r];
+  const T* wuv = static_cast<const T*>(a.w_uv) + (int64_t)g * D * R;
+  constexpr int HB = 4;
+  constexpr int VE = 16 / sizeof(T);  // elements per 16-byte load
+  const bool vec = (R % VE) == 0 && ((reinterpret_cast<uintptr_t>(wuv) & 15u) == 0);
+  for (int o = threadIdx.x; o < D * ((hpg + HB - 1) / HB); o += blockDim.x) {
+    const int d = o % D, hb = (o / D) * HB;
+    const T* wr = wuv + (int64_t)d * R;
+    float v[HB] = {0.f, 0.f, 0.f, 0.f};
+    if (vec) {
+#pragma unroll 4
+      for (int r = 0; r < R; r += VE) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(wr + r);
+        const T* e = reinterpret_cast<const T*>(&raw);
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (d0 + j < D) v[j] = fmaf(ldf(wuv, (int64_t)(d0 + j) * R + r), ar, v[j]);
+        for (int q = 0; q < VE; ++q) {
+          const float wv = to_f<T>(e[q]);
+#pragma unroll
+          for (int j = 0; j < HB; ++j)
+            if (hb + j < hpg) v[j] = fmaf(wv, av[(hb + j) * R + r + q], v[j]);
+        }
+      }
+    } else {
+      for (int r = 0; r < R; ++r) {
+        const float wv = ldf(wr, r);
+#pragma unroll
+        for (int j = 0; j < HB; ++j)
+          if (hb + j < hpg) v[j] = fmaf(wv, av[(hb + j) * R + r], v[j]);
+      }
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float sum = warp_sum(v[j]);
-      if (lane == 0 && d0 + j < D) out[d0 + j] = from_f<T>(failed ? __int_as_float(0x7fc00000) : sum);
+    for (int j = 0; j < HB; ++j) {
+      if (hb + j >= hpg) break;
+      T* out = static_cast<T*>(a.out) + (int64_t)b * a.o_sb + (int64_t)(h0 + hb + j) * D;
+      out[d] = from_f<T>(failed ? __int_as_float(0x7fc00000) : v[j]);
     }
   }
 }
@@ -377,7 +430,7 @@ int decode_t(const MlaDecodeArgs& a) {
       !g_force_generic.load(std::memory_order_relaxed) && mla_fast_supported(a) && mla_fast_maps(a, &maps);
   const MlaWorkspace w = mla_plan(a.s, a.L, fast);
   const int B = a.s.B, H = a.s.H;
-  int st = launch_smem(mla_absorb_kernel<T>, dim3(H, B), sizeof(float) * (a.s.D + (kThreads / 32) * a.s.R), a.stream, a, w);
+  int st = launch_smem(mla_absorb_kernel<T>, dim3(a.s.KV, B), absorb_smem_bytes(a.s), a.stream, a, w);
   if (st) return st;
   if (fast) {
     st = mla_fast_split_launch(a, w, maps);
@@ -385,7 +438,11 @@ int decode_t(const MlaDecodeArgs& a) {
     st = launch_smem(mla_split_kernel<T>, dim3(w.G), split_smem_bytes(a.s), a.stream, a, w);
   }
   if (st) return st;
-  return launch_smem(mla_combine_kernel<T>, dim3(H, B), sizeof(float) * (a.s.R + w.G + 1 + (kThreads / 32) * a.s.R), a.stream, a, w);
+  const int rw = (a.s.R + w.rchunks - 1) / w.rchunks;
+  st = launch_smem(mla_merge_kernel<T>, dim3(H, B, w.rchunks), sizeof(float) * (w.G + 1 + (kThreads / 32) * rw),
+                   a.stream, a, w);
+  if (st) return st;
+  return launch_smem(mla_combine_kernel<T>, dim3(a.s.KV, B), sizeof(float) * (H / a.s.KV) * a.s.R, a.stream, a, w);
 }
 
 template <typename T>
@@ -404,7 +461,7 @@ int mla_validate_shape(const b200mm_mla_shape& s) {
   if (s.D < 1 || s.D > 1024 || s.DR < 0 || s.DR > s.D || (s.DR & 1)) return B200MM_ERR_SHAPE;
   if (s.R < 1 || s.R > 4096) return B200MM_ERR_SHAPE;
   if (!(s.eps >= 0.f)) return B200MM_ERR_ARG;
-  if (split_smem_bytes(s) > 200 * 1024) return B200MM_ERR_SHAPE;
+  if (split_smem_bytes(s) > 200 * 1024 || absorb_smem_bytes(s) > 200 * 1024) return B200MM_ERR_SHAPE;
   return B200MM_OK;
 }
 
@@ -413,7 +470,7 @@ MlaWorkspace mla_plan(const b200mm_mla_shape& s, int64_t L, bool fast) {
   const int B = s.B > 0 ? s.B : 1;
   w.ntiles = (L + kMlaUnit - 1) / kMlaUnit;
   w.T = (int64_t)B * w.ntiles;
-  const int64_t want = fast ? mla_fast_ctas() : 2 * num_sms(current_device());
+  const int64_t want = fast ? mla_fast_ctas() : num_sms(current_device());
   w.G = (int)(want < w.T ? want : w.T);
   const size_t BH = (size_t)B * s.H;
   const size_t slots = (size_t)w.G + B;
@@ -421,7 +478,12 @@ MlaWorkspace mla_plan(const b200mm_mla_shape& s, int64_t L, bool fast) {
   w.off_qr = align256(w.off_qt + sizeof(float) * BH * s.R);
   w.off_pacc = align256(w.off_qr + sizeof(float) * BH * (s.DR > 0 ? s.DR : 1));
   w.off_pml = align256(w.off_pacc + sizeof(float) * slots * s.H * s.R);
-  w.off_err = align256(w.off_pml + sizeof(float) * slots * s.H * 2);
+  w.off_av = align256(w.off_pml + sizeof(float) * slots * s.H * 2);
+  w.off_err = align256(w.off_av + sizeof(float) * BH * s.R);
+  // merge parallelism: about 16 partials per CTA, latent chunks of >= 32
+  const int64_t parts = (w.G + B - 1) / B + 1;
+  const int rc = (int)((parts + 15) / 16), max_rc = (s.R + 31) / 32;
+  w.rchunks = rc < 1 ? 1 : (rc > max_rc ? max_rc : rc);
   w.total = align256(w.off_err + 16);
   return w;
 }

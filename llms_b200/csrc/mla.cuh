@@ -43,6 +43,7 @@ struct MlaDecodeArgs {
 //   qr   fp32 [B, H, DR]       RoPE'd query rope half at position L-1
 //   pacc fp32 [G+B, H, R]      per-partial sum_t p_t c_t (p relative to the partial max)
 //   pml  fp32 [G+B, H, 2]      per-partial (max score, sum p)
+//   av   fp32 [B, H, R]        merged sum_t softmax_t c_t (input of the W_uv step)
 //   err  int32[4]              error flag of bounded waits (0 = ok)
 constexpr int kMlaUnit = 64;  // tokens per work unit
 
@@ -50,7 +51,8 @@ struct MlaWorkspace {
   int G;                  // split CTAs (work ranges)
   int64_t ntiles;         // 64-token units per batch row
   int64_t T;              // B * ntiles
-  size_t off_qt, off_qr, off_pacc, off_pml, off_err, total;
+  int rchunks;            // latent chunks per (row, head) in the merge kernel
+  size_t off_qt, off_qr, off_pacc, off_pml, off_av, off_err, total;
 };
 
 __host__ __device__ inline int64_t mla_range_begin(const MlaWorkspace& w, int i) {

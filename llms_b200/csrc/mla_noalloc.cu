@@ -16,7 +16,7 @@
 namespace b200mm {
 namespace {
 
-constexpr size_t kScratchBytes = size_t(8) << 20;  // 8 MiB: B = 32, L = 32768 needs ~7.1 MiB
+constexpr size_t kScratchBytes = size_t(8) << 20;  // 8 MiB: B = 32, L = 32768 needs ~7.8 MiB
 __device__ __align__(256) unsigned char g_mla_scratch[kScratchBytes];
 
 constexpr int kMaxDev = 64;

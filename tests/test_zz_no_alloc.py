@@ -81,3 +81,14 @@ def test_noalloc_refuses_oversized_workspace():
                                        4096, None)
     assert st == 6  # B200MM_ERR_WORKSPACE
     assert lib.b200mm_launch_count() == before
+
+
+def test_documented_noalloc_case_fits_the_array():
+    """B = 32, L = 32768 at the Qwen3-4B MLA shape is documented to fit 8 MiB."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from llms_b200 import _capi
+
+    shp = _capi.MlaShape(B=32, H=32, KV=8, D=128, DR=32, R=256, dtype=2, eps=1e-6)
+    need = _capi.lib.b200mm_mla_decode_workspace_size(ctypes.byref(shp), 32768)
+    assert 0 < need <= 8 << 20, need
