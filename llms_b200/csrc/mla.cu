@@ -97,22 +97,18 @@ __global__ void __launch_bounds__(kThreads) mla_append_kernel(const MlaAppendArg
 }
 
 // --- absorbed query --------------------------------------------------------
-// grid: (KV, B); block 256.  One CTA per (batch row, group): W_uk,g is staged
-// in shared memory (16-byte loads, up to 48 KB of rows per pass) and serves
-// all H/KV heads of the group; a thread owns one latent column and keeps the
-// heads' sums as independent accumulators.
+// grid: (KV, B, ceil(R / 64)); block 256.  One CTA per (batch row, group,
+// 64 latent columns).  Thread (column tid % 64, slice tid / 64) sums every
+// fourth W_uk row for up to four heads at once, reading the rows straight
+// from global memory (64 consecutive columns: coalesced); the four slices
+// meet in shared memory.
 //   qt[b,h,r] = sum_i W_uk[g,i,r] * k_norm_w[i] * q[b,h,i]     (i < DN)
-//   qr[b,h,:] = rope_{L-1}(q[b,h,DN:])
-__host__ __device__ inline int absorb_chunk_rows(int R, int esz, int DN) {
-  const int rows = 49152 / (R * esz);
-  return rows < 1 ? 1 : (rows < DN ? rows : (DN > 0 ? DN : 1));
-}
+//   qr[b,h,:] = rope_{L-1}(q[b,h,DN:])                         (z-block 0 only)
+constexpr int kAbsCols = 64, kAbsSlices = kThreads / kAbsCols, kAbsHB = kThreads / kAbsCols;
 
 size_t absorb_smem_bytes(const b200mm_mla_shape& s) {
-  const int hpg = s.H / s.KV, DN = s.D - s.DR;
-  const int esz = s.dtype == B200MM_F32 ? 4 : 2;
-  return sizeof(float) * ((size_t)hpg * s.D + (size_t)hpg * s.R) + (size_t)absorb_chunk_rows(s.R, esz, DN) * s.R * esz +
-         16;
+  const int hpg = s.H / s.KV;
+  return sizeof(float) * ((size_t)hpg * s.D + (size_t)kAbsSlices * kAbsHB * kAbsCols);
 }
 
 template <typename T>
@@ -120,15 +116,13 @@ __global__ void __launch_bounds__(kThreads) mla_absorb_kernel(const MlaDecodeArg
   extern __shared__ float sm[];
   const int H = a.s.H, KV = a.s.KV, D = a.s.D, DR = a.s.DR, DN = D - DR, R = a.s.R;
   const int hpg = H / KV, g = blockIdx.x, b = blockIdx.y, h0 = g * hpg;
-  const int IC = absorb_chunk_rows(R, (int)sizeof(T), DN);
-  float* qn = sm;                 // [hpg][D]   q, times k_norm_w on the first DN dims
-  float* acc = qn + hpg * D;      // [hpg][R]
-  T* wch = reinterpret_cast<T*>((reinterpret_cast<uintptr_t>(acc + hpg * R) + 15) & ~uintptr_t(15));  // [IC][R]
+  float* qn = sm;              // [hpg][D]   q, times k_norm_w on the first DN dims
+  float* red = qn + hpg * D;   // [slice][head in block][column]
   float* ws = static_cast<float*>(a.ws);
 
   pdl_trigger();
   pdl_wait();
-  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0)
+  if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 0)
     *reinterpret_cast<int*>(static_cast<unsigned char*>(a.ws) + w.off_err) = 0;
   const T* q = static_cast<const T*>(a.q) + (int64_t)b * a.q_sb + (int64_t)h0 * D;
   for (int i = threadIdx.x; i < hpg * D; i += blockDim.x) {
@@ -136,43 +130,39 @@ __global__ void __launch_bounds__(kThreads) mla_absorb_kernel(const MlaDecodeArg
     const float v = ldf(q, i);
     qn[i] = d < DN ? a.k_norm_w[d] * v : v;
   }
-  for (int i = threadIdx.x; i < hpg * R; i += blockDim.x) acc[i] = 0.f;
+  __syncthreads();
+  const int col = threadIdx.x % kAbsCols, sl = threadIdx.x / kAbsCols;
+  const int c = blockIdx.z * kAbsCols + col;
   const T* wuk = static_cast<const T*>(a.w_uk) + (int64_t)g * DN * R;
-  constexpr int HB = 8;  // heads accumulated together per pass (independent FMA chains)
-  for (int i0 = 0; i0 < DN; i0 += IC) {
-    const int ni = min(IC, DN - i0);
-    __syncthreads();
-    {
-      const T* src = wuk + (int64_t)i0 * R;
-      constexpr int VE = 16 / sizeof(T);
-      const int n16 = ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) ? (ni * R) / VE : 0;
+  float* qt = ws + w.off_qt / 4 + ((int64_t)b * H + h0) * R;
+  for (int hb = 0; hb < hpg; hb += kAbsHB) {
+    float v[kAbsHB];
+#pragma unroll
+    for (int j = 0; j < kAbsHB; ++j) v[j] = 0.f;
+    if (c < R) {
 #pragma unroll 4
-      for (int e = threadIdx.x; e < n16; e += blockDim.x)
-        reinterpret_cast<uint4*>(wch)[e] = reinterpret_cast<const uint4*>(src)[e];
-      for (int e = n16 * VE + threadIdx.x; e < ni * R; e += blockDim.x) wch[e] = src[e];
-    }
-    __syncthreads();
-    for (int hb = 0; hb < hpg; hb += HB) {
-      for (int r = threadIdx.x; r < R; r += blockDim.x) {
-        float v[HB];
+      for (int i = sl; i < DN; i += kAbsSlices) {
+        const float wv = ldf(wuk, (int64_t)i * R + c);
 #pragma unroll
-        for (int j = 0; j < HB; ++j) v[j] = 0.f;
-#pragma unroll 4
-        for (int i = 0; i < ni; ++i) {
-          const float wv = to_f<T>(wch[i * R + r]);
-#pragma unroll
-          for (int j = 0; j < HB; ++j)
-            if (hb + j < hpg) v[j] = fmaf(wv, qn[(hb + j) * D + i0 + i], v[j]);
-        }
-#pragma unroll
-        for (int j = 0; j < HB; ++j)
-          if (hb + j < hpg) acc[(hb + j) * R + r] += v[j];
+        for (int j = 0; j < kAbsHB; ++j)
+          if (hb + j < hpg) v[j] = fmaf(wv, qn[(hb + j) * D + i], v[j]);
       }
     }
+#pragma unroll
+    for (int j = 0; j < kAbsHB; ++j) red[(sl * kAbsHB + j) * kAbsCols + col] = v[j];
+    __syncthreads();
+    {
+      const int j = threadIdx.x / kAbsCols, cc = blockIdx.z * kAbsCols + col;
+      if (hb + j < hpg && cc < R) {
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < kAbsSlices; ++k) s += red[(k * kAbsHB + j) * kAbsCols + col];
+        qt[(int64_t)(hb + j) * R + cc] = s;
+      }
+    }
+    __syncthreads();
   }
-  __syncthreads();
-  float* qt = ws + w.off_qt / 4 + ((int64_t)b * H + h0) * R;
-  for (int o = threadIdx.x; o < hpg * R; o += blockDim.x) qt[o] = acc[o];
+  if (blockIdx.z != 0) return;
   // qr = rope at position L-1 (rotate-half convention, angle = pos * inv_freq)
   const int half = DR / 2;
   const float pos = (float)(a.L - 1);
@@ -293,14 +283,61 @@ __global__ void __launch_bounds__(kThreads) mla_split_kernel(const MlaDecodeArgs
 
 // --- combine, step 1: merge the split partials ---------------------------
 // grid: (H, B, rchunks); block 256.  Partials of row b: slot i + b for every
-// range i overlapping [b*ntiles, (b+1)*ntiles).  Warps split the partials,
-// lanes split the latent chunk; av[b,h,:] = sum_k e^(m_k - M) acc_k / sum_k e^(m_k - M) l_k.
+// range i overlapping [b*ntiles, (b+1)*ntiles).  Threads split the chunk's
+// columns (float4 when R % 4 == 0) and the partials; the partial slices meet
+// in shared memory.
+//   av[b,h,:] = sum_k e^(m_k - M) acc_k / sum_k e^(m_k - M) l_k
+template <typename V>
+__device__ __forceinline__ void merge_cols(const float* pc, int64_t step, const float* wgt, int n, int width,
+                                           float inv_l, float* av, float* red) {
+  constexpr int VW = sizeof(V) / sizeof(float);
+  const int nc = width / VW;
+  if (nc <= 0) return;
+  const int nps = nc >= (int)blockDim.x ? 1 : (int)blockDim.x / nc;
+  const int ps = threadIdx.x / (nc >= (int)blockDim.x ? (int)blockDim.x : nc);
+  if (nps == 1) {  // wide chunk: each thread owns columns, walks every partial
+    for (int c = threadIdx.x; c < nc; c += blockDim.x) {
+      float s[VW] = {};
+      for (int k = 0; k < n; ++k) {
+        const V p = *reinterpret_cast<const V*>(pc + k * step + c * VW);
+        const float* pf = reinterpret_cast<const float*>(&p);
+#pragma unroll
+        for (int e = 0; e < VW; ++e) s[e] = fmaf(wgt[k], pf[e], s[e]);
+      }
+#pragma unroll
+      for (int e = 0; e < VW; ++e) av[c * VW + e] = s[e] * inv_l;
+    }
+    return;
+  }
+  const int c = threadIdx.x % nc;
+  if (ps < nps) {
+    float s[VW] = {};
+#pragma unroll 4
+    for (int k = ps; k < n; k += nps) {
+      const V p = *reinterpret_cast<const V*>(pc + k * step + c * VW);
+      const float* pf = reinterpret_cast<const float*>(&p);
+#pragma unroll
+      for (int e = 0; e < VW; ++e) s[e] = fmaf(wgt[k], pf[e], s[e]);
+    }
+#pragma unroll
+    for (int e = 0; e < VW; ++e) red[ps * width + c * VW + e] = s[e];
+  }
+  __syncthreads();
+  for (int o = threadIdx.x; o < width; o += blockDim.x) {
+    float s = 0.f;
+    for (int k = 0; k < nps; ++k) s += red[k * width + o];
+    av[o] = s * inv_l;
+  }
+}
+
+size_t merge_smem_bytes(const MlaWorkspace& w) { return sizeof(float) * (w.G + 2 + 4 * kThreads); }
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads) mla_merge_kernel(const MlaDecodeArgs a, MlaWorkspace w) {
   extern __shared__ float sm[];
   const int H = a.s.H, R = a.s.R;
   const int h = blockIdx.x, b = blockIdx.y;
-  const int rw = (R + w.rchunks - 1) / w.rchunks, r0 = blockIdx.z * rw, r1 = min(R, r0 + rw);
+  const int r0 = blockIdx.z * w.rw, r1 = min(R, r0 + w.rw);
   const float* ws = static_cast<const float*>(a.ws);
   const float* pml = ws + w.off_pml / 4;
   const float* pacc = ws + w.off_pacc / 4;
@@ -308,9 +345,9 @@ __global__ void __launch_bounds__(kThreads) mla_merge_kernel(const MlaDecodeArgs
   const int i0 = (int)(((lo + 1) * w.G - 1) / w.T);  // ranges overlapping [lo, hi)
   const int i1 = (int)((hi * w.G - 1) / w.T);
   const int n = i1 - i0 + 1;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* wgt = sm;                 // [n]
-  float* part = sm + w.G + 1;      // [nw][rw]
+  float* red = sm + w.G + 2;       // [partial slices][width], at most 4 * kThreads floats
   __shared__ float s_inv_l;
 
   pdl_trigger();
@@ -332,35 +369,26 @@ __global__ void __launch_bounds__(kThreads) mla_merge_kernel(const MlaDecodeArgs
   }
   __syncthreads();
   const int64_t step = (int64_t)H * R;
-  for (int rr = r0 + lane; rr < r1; rr += 32) {
-    const float* pc = pacc + (((int64_t)i0 + b) * H + h) * R + rr;
-    float v0 = 0.f, v1 = 0.f;
-    int k = warp;
-    for (; k + nw < n; k += 2 * nw) {
-      const float p0 = pc[k * step], p1 = pc[(k + nw) * step];
-      v0 = fmaf(wgt[k], p0, v0);
-      v1 = fmaf(wgt[k + nw], p1, v1);
-    }
-    if (k < n) v0 = fmaf(wgt[k], pc[k * step], v0);
-    part[warp * rw + (rr - r0)] = v0 + v1;
-  }
-  __syncthreads();
-  float* av = const_cast<float*>(ws) + w.off_av / 4 + ((int64_t)b * H + h) * R;
-  for (int rr = r0 + threadIdx.x; rr < r1; rr += blockDim.x) {
-    float v = 0.f;
-    for (int q = 0; q < nw; ++q) v += part[q * rw + (rr - r0)];
-    av[rr] = v * s_inv_l;
-  }
+  const float* pc = pacc + (((int64_t)i0 + b) * H + h) * R + r0;
+  float* av = const_cast<float*>(ws) + w.off_av / 4 + ((int64_t)b * H + h) * R + r0;
+  if ((R & 3) == 0)
+    merge_cols<float4>(pc, step, wgt, n, r1 - r0, s_inv_l, av, red);
+  else
+    merge_cols<float>(pc, step, wgt, n, r1 - r0, s_inv_l, av, red);
 }
 
-// --- combine, step 2: out[b,h,:] = W_uv,g . av[b,h,:] ----------------------
-// grid: (KV, B); block 256.  One CTA per (row, group): the group's heads share
-// W_uv,g, read once with 16-byte loads when the rank allows.
+// --- combine, step 2: out[b,h,d] = W_uv[g,d,:] . av[b,h,:] ------------------
+// grid: (KV, B, ceil(D / 16)); block 256.  One CTA per (row, group, 16 output
+// dims); warp w owns dims 2w, 2w+1 of the block, lanes split the latent rank
+// (16-byte loads of W_uv when the rank allows), warp sums finish each dot.
+constexpr int kCombDims = 2 * (kThreads / 32);
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads) mla_combine_kernel(const MlaDecodeArgs a, MlaWorkspace w) {
   extern __shared__ float sm[];
   const int H = a.s.H, KV = a.s.KV, D = a.s.D, R = a.s.R;
   const int hpg = H / KV, g = blockIdx.x, b = blockIdx.y, h0 = g * hpg;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* av = sm;  // [hpg][R]
   pdl_trigger();
   pdl_wait();
@@ -371,38 +399,43 @@ __global__ void __launch_bounds__(kThreads) mla_combine_kernel(const MlaDecodeAr
   const bool failed = *reinterpret_cast<const int*>(static_cast<const unsigned char*>(a.ws) + w.off_err) != 0;
   const T* wuv = static_cast<const T*>(a.w_uv) + (int64_t)g * D * R;
   constexpr int HB = 4;
-  constexpr int VE = 16 / sizeof(T);  // elements per 16-byte load
+  constexpr int VE = Chunk<T>::kElems;  // elements per 16-byte load
   const bool vec = (R % VE) == 0 && ((reinterpret_cast<uintptr_t>(wuv) & 15u) == 0);
-  for (int o = threadIdx.x; o < D * ((hpg + HB - 1) / HB); o += blockDim.x) {
-    const int d = o % D, hb = (o / D) * HB;
+  for (int dd = 0; dd < 2; ++dd) {
+    const int d = blockIdx.z * kCombDims + 2 * warp + dd;
+    if (d >= D) break;
     const T* wr = wuv + (int64_t)d * R;
-    float v[HB] = {0.f, 0.f, 0.f, 0.f};
-    if (vec) {
-#pragma unroll 4
-      for (int r = 0; r < R; r += VE) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(wr + r);
-        const T* e = reinterpret_cast<const T*>(&raw);
+    for (int hb = 0; hb < hpg; hb += HB) {
+      float v[HB] = {0.f, 0.f, 0.f, 0.f};
+      if (vec) {
+        for (int r = VE * lane; r < R; r += 32 * VE) {
+          float f[VE];
+          Chunk<T>::unpack(*reinterpret_cast<const uint4*>(wr + r), f);
 #pragma unroll
-        for (int q = 0; q < VE; ++q) {
-          const float wv = to_f<T>(e[q]);
+          for (int j = 0; j < HB; ++j) {
+            if (hb + j >= hpg) break;
+            const float* ar = av + (hb + j) * R + r;
+#pragma unroll
+            for (int e = 0; e < VE; ++e) v[j] = fmaf(f[e], ar[e], v[j]);
+          }
+        }
+      } else {
+        for (int r = lane; r < R; r += 32) {
+          const float wv = ldf(wr, r);
 #pragma unroll
           for (int j = 0; j < HB; ++j)
-            if (hb + j < hpg) v[j] = fmaf(wv, av[(hb + j) * R + r + q], v[j]);
+            if (hb + j < hpg) v[j] = fmaf(wv, av[(hb + j) * R + r], v[j]);
         }
       }
-    } else {
-      for (int r = 0; r < R; ++r) {
-        const float wv = ldf(wr, r);
 #pragma unroll
-        for (int j = 0; j < HB; ++j)
-          if (hb + j < hpg) v[j] = fmaf(wv, av[(hb + j) * R + r], v[j]);
+      for (int j = 0; j < HB; ++j) {
+        if (hb + j >= hpg) break;
+        const float s = warp_sum(v[j]);
+        if (lane == 0) {
+          T* out = static_cast<T*>(a.out) + (int64_t)b * a.o_sb + (int64_t)(h0 + hb + j) * D;
+          out[d] = from_f<T>(failed ? __int_as_float(0x7fc00000) : s);
+        }
       }
-    }
-#pragma unroll
-    for (int j = 0; j < HB; ++j) {
-      if (hb + j >= hpg) break;
-      T* out = static_cast<T*>(a.out) + (int64_t)b * a.o_sb + (int64_t)(h0 + hb + j) * D;
-      out[d] = from_f<T>(failed ? __int_as_float(0x7fc00000) : v[j]);
     }
   }
 }
@@ -430,7 +463,8 @@ int decode_t(const MlaDecodeArgs& a) {
       !g_force_generic.load(std::memory_order_relaxed) && mla_fast_supported(a) && mla_fast_maps(a, &maps);
   const MlaWorkspace w = mla_plan(a.s, a.L, fast);
   const int B = a.s.B, H = a.s.H;
-  int st = launch_smem(mla_absorb_kernel<T>, dim3(a.s.KV, B), absorb_smem_bytes(a.s), a.stream, a, w);
+  int st = launch_smem(mla_absorb_kernel<T>, dim3(a.s.KV, B, (a.s.R + kAbsCols - 1) / kAbsCols),
+                       absorb_smem_bytes(a.s), a.stream, a, w);
   if (st) return st;
   if (fast) {
     st = mla_fast_split_launch(a, w, maps);
@@ -438,11 +472,10 @@ int decode_t(const MlaDecodeArgs& a) {
     st = launch_smem(mla_split_kernel<T>, dim3(w.G), split_smem_bytes(a.s), a.stream, a, w);
   }
   if (st) return st;
-  const int rw = (a.s.R + w.rchunks - 1) / w.rchunks;
-  st = launch_smem(mla_merge_kernel<T>, dim3(H, B, w.rchunks), sizeof(float) * (w.G + 1 + (kThreads / 32) * rw),
-                   a.stream, a, w);
+  st = launch_smem(mla_merge_kernel<T>, dim3(H, B, w.rchunks), merge_smem_bytes(w), a.stream, a, w);
   if (st) return st;
-  return launch_smem(mla_combine_kernel<T>, dim3(a.s.KV, B), sizeof(float) * (H / a.s.KV) * a.s.R, a.stream, a, w);
+  return launch_smem(mla_combine_kernel<T>, dim3(a.s.KV, B, (a.s.D + kCombDims - 1) / kCombDims),
+                     sizeof(float) * (H / a.s.KV) * a.s.R, a.stream, a, w);
 }
 
 template <typename T>
@@ -462,6 +495,7 @@ int mla_validate_shape(const b200mm_mla_shape& s) {
   if (s.R < 1 || s.R > 4096) return B200MM_ERR_SHAPE;
   if (!(s.eps >= 0.f)) return B200MM_ERR_ARG;
   if (split_smem_bytes(s) > 200 * 1024 || absorb_smem_bytes(s) > 200 * 1024) return B200MM_ERR_SHAPE;
+  if (sizeof(float) * (size_t)(s.H / s.KV) * s.R > 200 * 1024) return B200MM_ERR_SHAPE;  // combine's av
   return B200MM_OK;
 }
 
@@ -484,6 +518,9 @@ MlaWorkspace mla_plan(const b200mm_mla_shape& s, int64_t L, bool fast) {
   const int64_t parts = (w.G + B - 1) / B + 1;
   const int rc = (int)((parts + 15) / 16), max_rc = (s.R + 31) / 32;
   w.rchunks = rc < 1 ? 1 : (rc > max_rc ? max_rc : rc);
+  w.rw = (s.R + w.rchunks - 1) / w.rchunks;
+  if ((s.R & 3) == 0) w.rw = (w.rw + 3) & ~3;  // float4 columns in the merge
+  w.rchunks = (s.R + w.rw - 1) / w.rw;
   w.total = align256(w.off_err + 16);
   return w;
 }

@@ -52,6 +52,7 @@ struct MlaWorkspace {
   int64_t ntiles;         // 64-token units per batch row
   int64_t T;              // B * ntiles
   int rchunks;            // latent chunks per (row, head) in the merge kernel
+  int rw;                 // columns per chunk
   size_t off_qt, off_qr, off_pacc, off_pml, off_av, off_err, total;
 };
 

@@ -91,6 +91,18 @@ def test_cfg4_shapes(B, L):
     bf16_check(host(out), oracle_out(d, L, dims))
 
 
+@pytest.mark.parametrize("dims,B,L", [
+    (dict(H=6, KV=2, D=20, DR=4, R=13), 2, 200),     # odd rank: scalar merge / combine columns
+    (dict(H=10, KV=2, D=40, DR=8, R=130), 1, 3000),  # 5 heads per group, rank not a multiple of 64
+    (dict(H=8, KV=8, D=64, DR=0, R=96), 3, 700),     # one head per group, no RoPE part
+])
+def test_generic_odd_shapes_fp32(dims, B, L):
+    """Shapes off the production one run the generic kernels end to end."""
+    d = I.cfg4(B, L, **dims)
+    out, _ = run_kernel(d, L, dims, torch.float32)
+    np.testing.assert_allclose(host(out), oracle_out(d, L, dims, dtype_round=False), rtol=2e-3, atol=2e-4)
+
+
 @pytest.mark.parametrize("B,L", [(1, 32768), (4, 32768)])
 def test_cfg4_long_context(B, L):
     """Full BASELINE context length: oracle on the full input (float64 BLAS)."""
