@@ -378,22 +378,27 @@ __global__ void __launch_bounds__(kThreads) mla_merge_kernel(const MlaDecodeArgs
 }
 
 // --- combine, step 2: out[b,h,d] = W_uv[g,d,:] . av[b,h,:] ------------------
-// grid: (KV, B, ceil(D / 16)); block 256.  One CTA per (row, group, 16 output
-// dims); warp w owns dims 2w, 2w+1 of the block, lanes split the latent rank
-// (16-byte loads of W_uv when the rank allows), warp sums finish each dot.
-constexpr int kCombDims = 2 * (kThreads / 32);
+// grid: (KV, B, ceil(D / 32)); block 256.  One CTA per (row, group, 32 output
+// dims); warp w owns dims 4w .. 4w+3 of the block, lanes split the latent
+// rank (16-byte loads of W_uv and float4 reads of av when the rank allows),
+// warp sums finish each dot.
+constexpr int kCombPerWarp = 4, kCombDims = kCombPerWarp * (kThreads / 32);
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads) mla_combine_kernel(const MlaDecodeArgs a, MlaWorkspace w) {
-  extern __shared__ float sm[];
+  extern __shared__ float4 sm4[];
+  float* av = reinterpret_cast<float*>(sm4);  // [hpg][R]
   const int H = a.s.H, KV = a.s.KV, D = a.s.D, R = a.s.R;
   const int hpg = H / KV, g = blockIdx.x, b = blockIdx.y, h0 = g * hpg;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* av = sm;  // [hpg][R]
   pdl_trigger();
   pdl_wait();
   const float* src = static_cast<const float*>(a.ws) + w.off_av / 4 + ((int64_t)b * H + h0) * R;
-  for (int o = threadIdx.x; o < hpg * R; o += blockDim.x) av[o] = src[o];
+  if ((R & 3) == 0) {  // the workspace's av rows start 16-byte aligned when R % 4 == 0
+    for (int o = threadIdx.x; o < hpg * R / 4; o += blockDim.x) sm4[o] = reinterpret_cast<const float4*>(src)[o];
+  } else {
+    for (int o = threadIdx.x; o < hpg * R; o += blockDim.x) av[o] = src[o];
+  }
   __syncthreads();
   // a split kernel that gave up on a bounded wait leaves NaN, never a silent result
   const bool failed = *reinterpret_cast<const int*>(static_cast<const unsigned char*>(a.ws) + w.off_err) != 0;
@@ -401,8 +406,8 @@ __global__ void __launch_bounds__(kThreads) mla_combine_kernel(const MlaDecodeAr
   constexpr int HB = 4;
   constexpr int VE = Chunk<T>::kElems;  // elements per 16-byte load
   const bool vec = (R % VE) == 0 && ((reinterpret_cast<uintptr_t>(wuv) & 15u) == 0);
-  for (int dd = 0; dd < 2; ++dd) {
-    const int d = blockIdx.z * kCombDims + 2 * warp + dd;
+  for (int dd = 0; dd < kCombPerWarp; ++dd) {
+    const int d = blockIdx.z * kCombDims + kCombPerWarp * warp + dd;
     if (d >= D) break;
     const T* wr = wuv + (int64_t)d * R;
     for (int hb = 0; hb < hpg; hb += HB) {
@@ -414,9 +419,15 @@ __global__ void __launch_bounds__(kThreads) mla_combine_kernel(const MlaDecodeAr
 #pragma unroll
           for (int j = 0; j < HB; ++j) {
             if (hb + j >= hpg) break;
-            const float* ar = av + (hb + j) * R + r;
+            const float4* ar = reinterpret_cast<const float4*>(av + (hb + j) * R + r);
 #pragma unroll
-            for (int e = 0; e < VE; ++e) v[j] = fmaf(f[e], ar[e], v[j]);
+            for (int e4 = 0; e4 < VE / 4; ++e4) {
+              const float4 x = ar[e4];
+              v[j] = fmaf(f[4 * e4], x.x, v[j]);
+              v[j] = fmaf(f[4 * e4 + 1], x.y, v[j]);
+              v[j] = fmaf(f[4 * e4 + 2], x.z, v[j]);
+              v[j] = fmaf(f[4 * e4 + 3], x.w, v[j]);
+            }
           }
         }
       } else {
@@ -467,7 +478,7 @@ int decode_t(const MlaDecodeArgs& a) {
                        absorb_smem_bytes(a.s), a.stream, a, w);
   if (st) return st;
   if (fast) {
-    st = mla_fast_split_launch(a, w, maps);
+    st = mla_tc_split_launch(a, w, maps);
   } else {
     st = launch_smem(mla_split_kernel<T>, dim3(w.G), split_smem_bytes(a.s), a.stream, a, w);
   }

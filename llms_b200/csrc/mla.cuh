@@ -73,6 +73,6 @@ struct MlaMaps {
 bool mla_fast_supported(const MlaDecodeArgs& a);
 bool mla_fast_maps(const MlaDecodeArgs& a, MlaMaps* maps);  // false if the driver rejects a map
 int mla_fast_ctas();                   // G for the production-shape kernel
-int mla_fast_split_launch(const MlaDecodeArgs& a, const MlaWorkspace& w, const MlaMaps& maps);
+int mla_tc_split_launch(const MlaDecodeArgs& a, const MlaWorkspace& w, const MlaMaps& maps);
 
 }  // namespace b200mm

@@ -16,7 +16,7 @@
 // Every mbarrier wait is bounded; a CTA whose wait expires stops issuing,
 // drains its own copies in flight, frees TMEM and writes NaN over its tile.
 #include "dense.cuh"
-#include "tma.cuh"
+#include "tcgen05.cuh"
 
 namespace b200mm {
 
@@ -46,56 +46,10 @@ struct TcParams {
   int64_t ldy;
 };
 
-// UMMA shared-memory descriptor: K-major operand in the 128-byte swizzle,
-// 8-row groups 1024 bytes apart.
-__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
-  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);  // start address
-  d |= (uint64_t)1 << 16;                          // leading byte offset (unused when swizzled)
-  d |= (uint64_t)(1024 >> 4) << 32;                // stride byte offset: 8 rows x 128 B
-  d |= (uint64_t)1 << 46;                          // descriptor version for sm_100
-  d |= (uint64_t)2 << 61;                          // layout: SWIZZLE_128B
-  return d;
-}
-
-template <typename T> constexpr uint32_t ab_format();
-template <> constexpr uint32_t ab_format<__nv_bfloat16>() { return 1; }
-template <> constexpr uint32_t ab_format<__half>() { return 0; }
-
-// kind::f16 instruction descriptor: fp32 accumulate, A/B K-major, M x N.
+// kind::f16 instruction descriptor for this kernel's M = BM tiles.
 template <typename T, int N>
 constexpr uint32_t idesc() {
-  return (1u << 4) | (ab_format<T>() << 7) | (ab_format<T>() << 10) | ((uint32_t)(N >> 3) << 17) |
-         ((uint32_t)(BM >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
-          tmem_d),
-      "l"(a), "l"(b), "r"(id), "r"(acc)
-      : "memory");
-}
-__device__ __forceinline__ void mma_commit(void* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// 32 consecutive fp32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
-      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  return idesc_f16<T>(BM, N);
 }
 
 template <typename T> __device__ __forceinline__ uint32_t pack_out(float a, float b);
@@ -145,10 +99,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (GATE) prefetch_map(&mw1);
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(kTmemCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    tmem_alloc(tmem_slot, kTmemCols);
   }
   tc_fence_before();
   __syncthreads();
@@ -255,7 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 
