@@ -4,6 +4,9 @@
 #include <mutex>
 
 #include "dense.cuh"
+
+#include <cstdlib>
+#include <string>
 #include "mla.cuh"
 
 namespace b200mm {
@@ -50,9 +53,24 @@ int check_device() {
 
 int dense_dispatch(const DenseArgs& a) {
   if (g_force_generic.load(std::memory_order_relaxed)) return tiled_launch(a);
-  // M >= 65: tcgen05 GEMM; M <= 4: CUDA-core GEMV; 5..64: tensor-core GEMV
-  if (tc_supported(a)) return tc_launch(a);
+#ifdef SWAP_TRACE
+  // development builds only: force one family ("gemv", "mmv", "swap", "tc")
+  if (const char* f = getenv("B200MM_DENSE_FAMILY")) {
+    const std::string fam(f);
+    if (fam == "gemv" && gemv_supported(a)) return gemv_launch(a);
+    if (fam == "mmv" && mmv_supported(a)) return mmv_launch(a);
+    if (fam == "swap" && swap_supported(a)) return swap_launch(a);
+    if (fam == "tc" && tc_supported(a)) return tc_launch(a);
+  }
+#endif
+  // measured on B200 at the Qwen3 shapes: M <= 4 CUDA-core GEMV; small M the
+  // mma.sync GEMV (bf16 M <= 16, int8 M <= 32); then tcgen05 with the weights
+  // as the MMA's M side (bf16 up to M = 64, int8 any M); bf16 M >= 65 the
+  // tcgen05 GEMM tiled over X
   if (a.M <= 4 && gemv_supported(a)) return gemv_launch(a);
+  if (a.M <= (a.w8 ? 32 : 16) && mmv_supported(a)) return mmv_launch(a);
+  if ((a.w8 || a.M <= 64) && swap_supported(a)) return swap_launch(a);
+  if (tc_supported(a)) return tc_launch(a);
   if (mmv_supported(a)) return mmv_launch(a);
   if (gemv_supported(a)) return gemv_launch(a);
   return tiled_launch(a);

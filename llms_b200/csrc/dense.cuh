@@ -30,6 +30,8 @@ int gemv_launch(const DenseArgs& a);
 int tiled_launch(const DenseArgs& a);
 bool mmv_supported(const DenseArgs& a);
 int mmv_launch(const DenseArgs& a);
+bool swap_supported(const DenseArgs& a);
+int swap_launch(const DenseArgs& a);
 bool tc_supported(const DenseArgs& a);
 int tc_launch(const DenseArgs& a);
 

@@ -67,33 +67,6 @@ template <> struct MmaOp<__half> {
   }
 };
 
-// int8 pair (bytes 2j, 2j+1 of the sign-flipped word) -> fp16x2, exact.
-__device__ __forceinline__ uint32_t i8x2_to_h2(uint32_t wflip, int j) {
-  const uint32_t h = __byte_perm(wflip, 0x64646464u, j == 0 ? 0x4140u : 0x4342u);  // 1024 + (q + 128)
-  const __half2 v =
-      __hsub2(*reinterpret_cast<const __half2*>(&h), __half2(__float2half(1152.f), __float2half(1152.f)));
-  return *reinterpret_cast<const uint32_t*>(&v);
-}
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
-  uint32_t out;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
-               : "=r"(out)
-               : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))), "r"(rank));
-  return out;
-}
-__device__ __forceinline__ void st_cluster_f2(uint32_t addr, float a, float b) {
-  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
-}
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
 // TX: activation dtype in memory; TM: MMA input dtype (== TX, or fp16 for int8
 // weights); TW: weight dtype; MT: n-tiles of 8 activation rows.
 template <typename TX, typename TM, typename TW, int MT, bool GATE>
@@ -294,22 +267,9 @@ int launch_mmv(const DenseArgs& a, int kslice) {
   }
   MmvParams p{a.x, a.ldx, a.w0, a.ldw0, a.w1, a.ldw1, a.s0, a.s1, a.y, a.ldy, a.M, a.N, a.K, kslice};
   const int groups = (a.N + kRows - 1) / kRows;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(groups * kCluster);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = a.stream;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = kCluster;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 2;
-  count_launch();
-  return cudaLaunchKernelEx(&cfg, kern, p) == cudaSuccess ? B200MM_OK : B200MM_ERR_LAUNCH;
+  return launch_pdl_cluster(kern, dim3(groups * kCluster), dim3(kThreads), smem, a.stream, kCluster, p) == cudaSuccess
+             ? B200MM_OK
+             : B200MM_ERR_LAUNCH;
 }
 
 template <typename TX, typename TM, typename TW, bool GATE>

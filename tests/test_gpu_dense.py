@@ -222,8 +222,9 @@ def test_modules_match_eager():
 @pytest.mark.parametrize("M", [5, 7, 12, 24, 48, 64, 65, 100])
 @pytest.mark.parametrize("gate", [False, True])
 def test_mid_m_tensor_core_gemv(M, gate):
-    """5 <= M <= 64 runs the tensor-core GEMV (K split over a 4-CTA cluster);
-    65 <= M < 128 the tcgen05 kernel with a partly filled tile."""
+    """5 <= M <= 16 runs the mma.sync GEMV (K split over a 4-CTA cluster),
+    17 <= M <= 64 the tcgen05 kernel with the weights on the MMA's M side,
+    65 <= M < 128 the tcgen05 GEMM with a partly filled tile."""
     from llms_b200.kernels import triton_fused_gate_up_silu, triton_fused_qkv
     rng = np.random.default_rng(M + 100 * gate)
     K, N = 2560, 1000  # N not a multiple of the 128-row group
@@ -270,3 +271,37 @@ def test_mid_m_k_tails(K):
     wu = dev(rng.standard_normal((700, K), dtype=np.float32) * 0.03)
     y = triton_fused_gate_up_silu(x, wg, wu)
     bf16_check(host(y), O.gate_up_silu(host(x), host(wg), host(wu)))
+
+
+@pytest.mark.parametrize("M,gate", [(129, False), (200, True), (256, False), (256, True)])
+def test_tcgen05_partial_m_tiles(M, gate):
+    """129 <= M <= 256: the tcgen05 GEMM with a partly filled second tile."""
+    from llms_b200.kernels import triton_fused_gate_up_silu, triton_fused_qkv
+    rng = np.random.default_rng(M)
+    K, N = 1536, 640
+    xd = dev(rng.standard_normal((M, K), dtype=np.float32))
+    w0d = dev(rng.standard_normal((N, K), dtype=np.float32) * 0.03)
+    if gate:
+        w1d = dev(rng.standard_normal((N, K), dtype=np.float32) * 0.03)
+        bf16_check(host(triton_fused_gate_up_silu(xd, w0d, w1d)), O.gate_up_silu(host(xd), host(w0d), host(w1d)))
+    else:
+        q, k, v = triton_fused_qkv(xd, w0d, n_q=512, n_k=64)
+        e = host(xd).astype(np.float64) @ host(w0d).astype(np.float64).T
+        bf16_check(host(torch.cat([q, k, v], -1)), e)
+
+
+@pytest.mark.parametrize("M", [100, 300, 2048])
+def test_int8_prefill_m(M):
+    """int8 weights at prefill sizes: several 256-row N tiles of activations."""
+    from llms_b200.kernels import int8_fused_gate_up_silu, int8_fused_qkv
+    lay = I.cfg5_layer(M=M, seed=M)
+    rows = _rows_subset(M, 24)
+    to = lambda a: torch.from_numpy(a[:1024]).cuda()
+    x = dev(lay["x"])
+    y = int8_fused_gate_up_silu(x, to(lay["gate_q"]), to(lay["gate_s"]), to(lay["up_q"]), to(lay["up_s"]))
+    e = O.gate_up_silu(lay["x"][rows], O.dequant(lay["gate_q"][:1024], lay["gate_s"][:1024]),
+                       O.dequant(lay["up_q"][:1024], lay["up_s"][:1024]))
+    bf16_check(host(y)[rows], e)
+    q, k, v = int8_fused_qkv(x, to(lay["qkv_q"]), to(lay["qkv_s"]), n_q=768, n_k=128)
+    e = lay["x"][rows].astype(np.float64) @ O.dequant(lay["qkv_q"][:1024], lay["qkv_s"][:1024]).T
+    bf16_check(host(torch.cat([q, k, v], -1))[rows], e)
