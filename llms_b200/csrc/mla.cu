@@ -97,33 +97,79 @@ __global__ void __launch_bounds__(kThreads) mla_append_kernel(const MlaAppendArg
 }
 
 // --- absorbed query --------------------------------------------------------
-// grid: (KV, B, ceil(R / 64)); block 256.  One CTA per (batch row, group,
-// 64 latent columns).  Thread (column tid % 64, slice tid / 64) sums every
-// fourth W_uk row for up to four heads at once, reading the rows straight
-// from global memory (64 consecutive columns: coalesced); the four slices
-// meet in shared memory.
+// grid: (KV, B, ceil(R / 64)); block 256.  One CTA per (group, batch row, 64
+// latent columns).  The CTA's W_uk slice [DN x 64] is requested with every
+// 16-byte load in flight at once, before waiting on the previous kernel
+// (weights never come from it), and staged in shared memory in its own dtype.
+// Thread (column pair, row slice of eight) accumulates its rows for four
+// heads in registers; one shared-memory reduction over the slices finishes.
+// The previous kernel is waited on before dependents are released, so the
+// split kernel may fetch the cache as soon as it starts.
 //   qt[b,h,r] = sum_i W_uk[g,i,r] * k_norm_w[i] * q[b,h,i]     (i < DN)
 //   qr[b,h,:] = rope_{L-1}(q[b,h,DN:])                         (z-block 0 only)
-constexpr int kAbsCols = 64, kAbsSlices = kThreads / kAbsCols, kAbsHB = kThreads / kAbsCols;
+constexpr int kAbsCols = 64, kAbsSlices = kThreads / 32, kAbsHB = 4;
 
+template <typename T>
+size_t absorb_smem_t(const b200mm_mla_shape& s) {
+  const int hpg = s.H / s.KV, DN = s.D - s.DR;
+  return sizeof(float) * ((size_t)hpg * s.D + (size_t)kAbsSlices * kAbsHB * kAbsCols) +
+         sizeof(T) * (size_t)DN * kAbsCols + 16;
+}
 size_t absorb_smem_bytes(const b200mm_mla_shape& s) {
-  const int hpg = s.H / s.KV;
-  return sizeof(float) * ((size_t)hpg * s.D + (size_t)kAbsSlices * kAbsHB * kAbsCols);
+  return s.dtype == B200MM_F32 ? absorb_smem_t<float>(s) : absorb_smem_t<__half>(s);
 }
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads) mla_absorb_kernel(const MlaDecodeArgs a, MlaWorkspace w) {
+  MLA_SPAN(0, 0);
   extern __shared__ float sm[];
   const int H = a.s.H, KV = a.s.KV, D = a.s.D, DR = a.s.DR, DN = D - DR, R = a.s.R;
-  const int hpg = H / KV, g = blockIdx.x, b = blockIdx.y, h0 = g * hpg;
-  float* qn = sm;              // [hpg][D]   q, times k_norm_w on the first DN dims
-  float* red = qn + hpg * D;   // [slice][head in block][column]
+  const int hpg = H / KV, g = blockIdx.x, b = blockIdx.y, h0 = g * hpg, c0 = blockIdx.z * kAbsCols;
+  float* qn = sm;                              // [hpg][D]  q, times k_norm_w on the first DN dims
+  float* red = qn + hpg * D;                   // [slice][head][64]
+  T* wsl = reinterpret_cast<T*>((reinterpret_cast<uintptr_t>(red + kAbsSlices * kAbsHB * kAbsCols) + 15) &
+                                ~uintptr_t(15));  // [DN][64]
   float* ws = static_cast<float*>(a.ws);
+  const T* wuk = static_cast<const T*>(a.w_uk) + (int64_t)g * DN * R;
 
-  pdl_trigger();
+  constexpr int VE = 16 / sizeof(T);  // elements per 16-byte load
+  constexpr int U = 4;                // loads per thread per pass
+  const bool vec = (R % VE) == 0 && c0 + kAbsCols <= R && ((reinterpret_cast<uintptr_t>(wuk) & 15u) == 0);
+  const int per_row = kAbsCols / VE, total = DN * per_row;
+  uint4 r[U];
+  if (vec) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int e = u * kThreads + threadIdx.x;
+      if (e < total) r[u] = *reinterpret_cast<const uint4*>(wuk + (int64_t)(e / per_row) * R + c0 + (e % per_row) * VE);
+    }
+  }
   pdl_wait();
+  pdl_trigger();
   if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 0)
     *reinterpret_cast<int*>(static_cast<unsigned char*>(a.ws) + w.off_err) = 0;
+  if (vec) {
+    for (int pass = 0; pass * U * kThreads < total; ++pass) {
+      if (pass > 0) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int e = (pass * U + u) * kThreads + threadIdx.x;
+          if (e < total)
+            r[u] = *reinterpret_cast<const uint4*>(wuk + (int64_t)(e / per_row) * R + c0 + (e % per_row) * VE);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {  // row-major [DN][64]: consecutive threads, consecutive 16 bytes
+        const int e = (pass * U + u) * kThreads + threadIdx.x;
+        if (e < total) reinterpret_cast<uint4*>(wsl)[e] = r[u];
+      }
+    }
+  } else {
+    for (int e = threadIdx.x; e < DN * kAbsCols; e += blockDim.x) {
+      const int i = e / kAbsCols, c = c0 + e % kAbsCols;
+      wsl[e] = c < R ? wuk[(int64_t)i * R + c] : from_f<T>(0.f);
+    }
+  }
   const T* q = static_cast<const T*>(a.q) + (int64_t)b * a.q_sb + (int64_t)h0 * D;
   for (int i = threadIdx.x; i < hpg * D; i += blockDim.x) {
     const int d = i % D;
@@ -131,48 +177,47 @@ __global__ void __launch_bounds__(kThreads) mla_absorb_kernel(const MlaDecodeArg
     qn[i] = d < DN ? a.k_norm_w[d] * v : v;
   }
   __syncthreads();
-  const int col = threadIdx.x % kAbsCols, sl = threadIdx.x / kAbsCols;
-  const int c = blockIdx.z * kAbsCols + col;
-  const T* wuk = static_cast<const T*>(a.w_uk) + (int64_t)g * DN * R;
+  const int cp = threadIdx.x & 31, sl = threadIdx.x >> 5;  // columns 2cp, 2cp+1; rows sl, sl+8, ...
   float* qt = ws + w.off_qt / 4 + ((int64_t)b * H + h0) * R;
   for (int hb = 0; hb < hpg; hb += kAbsHB) {
-    float v[kAbsHB];
+    float acc[kAbsHB][2] = {};
+    for (int i = sl; i < DN; i += kAbsSlices) {
+      const float w0 = to_f<T>(wsl[i * kAbsCols + 2 * cp]), w1 = to_f<T>(wsl[i * kAbsCols + 2 * cp + 1]);
 #pragma unroll
-    for (int j = 0; j < kAbsHB; ++j) v[j] = 0.f;
-    if (c < R) {
-#pragma unroll 4
-      for (int i = sl; i < DN; i += kAbsSlices) {
-        const float wv = ldf(wuk, (int64_t)i * R + c);
-#pragma unroll
-        for (int j = 0; j < kAbsHB; ++j)
-          if (hb + j < hpg) v[j] = fmaf(wv, qn[(hb + j) * D + i], v[j]);
+      for (int j = 0; j < kAbsHB; ++j) {
+        if (hb + j >= hpg) break;
+        const float qv = qn[(hb + j) * D + i];
+        acc[j][0] = fmaf(w0, qv, acc[j][0]);
+        acc[j][1] = fmaf(w1, qv, acc[j][1]);
       }
     }
 #pragma unroll
-    for (int j = 0; j < kAbsHB; ++j) red[(sl * kAbsHB + j) * kAbsCols + col] = v[j];
+    for (int j = 0; j < kAbsHB; ++j)
+      *reinterpret_cast<float2*>(red + (sl * kAbsHB + j) * kAbsCols + 2 * cp) = make_float2(acc[j][0], acc[j][1]);
     __syncthreads();
     {
-      const int j = threadIdx.x / kAbsCols, cc = blockIdx.z * kAbsCols + col;
-      if (hb + j < hpg && cc < R) {
+      const int j = threadIdx.x / kAbsCols, col = threadIdx.x % kAbsCols;
+      if (hb + j < hpg && c0 + col < R) {
         float s = 0.f;
 #pragma unroll
         for (int k = 0; k < kAbsSlices; ++k) s += red[(k * kAbsHB + j) * kAbsCols + col];
-        qt[(int64_t)(hb + j) * R + cc] = s;
+        qt[(int64_t)(hb + j) * R + c0 + col] = s;
       }
     }
     __syncthreads();
   }
+  MLA_SPAN(0, 1);
   if (blockIdx.z != 0) return;
   // qr = rope at position L-1 (rotate-half convention, angle = pos * inv_freq)
   const int half = DR / 2;
   const float pos = (float)(a.L - 1);
   float* qr = ws + w.off_qr / 4 + ((int64_t)b * H + h0) * DR;
   for (int o = threadIdx.x; o < hpg * DR; o += blockDim.x) {
-    const int hh = o / DR, j = o % DR;
+    const int hq = o / DR, j = o % DR;
     const int i = j < half ? j : j - half;
     float sn, cs;
     sincosf(pos * a.inv_freq[i], &sn, &cs);
-    const float* qh = qn + hh * D + DN;
+    const float* qh = qn + hq * D + DN;
     const float rot = j < half ? -qh[j + half] : qh[j - half];
     qr[o] = qh[j] * cs + rot * sn;
   }
@@ -334,6 +379,7 @@ size_t merge_smem_bytes(const MlaWorkspace& w) { return sizeof(float) * (w.G + 2
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads) mla_merge_kernel(const MlaDecodeArgs a, MlaWorkspace w) {
+  MLA_SPAN(2, 0);
   extern __shared__ float sm[];
   const int H = a.s.H, R = a.s.R;
   const int h = blockIdx.x, b = blockIdx.y;
@@ -375,80 +421,128 @@ __global__ void __launch_bounds__(kThreads) mla_merge_kernel(const MlaDecodeArgs
     merge_cols<float4>(pc, step, wgt, n, r1 - r0, s_inv_l, av, red);
   else
     merge_cols<float>(pc, step, wgt, n, r1 - r0, s_inv_l, av, red);
+  MLA_SPAN(2, 1);
 }
 
 // --- combine, step 2: out[b,h,d] = W_uv[g,d,:] . av[b,h,:] ------------------
-// grid: (KV, B, ceil(D / 32)); block 256.  One CTA per (row, group, 32 output
-// dims); warp w owns dims 4w .. 4w+3 of the block, lanes split the latent
-// rank (16-byte loads of W_uv and float4 reads of av when the rank allows),
-// warp sums finish each dot.
-constexpr int kCombPerWarp = 4, kCombDims = kCombPerWarp * (kThreads / 32);
+// grid: (KV, B, ceil(D / 32)); block 256.  One CTA per (group, row, 32 output
+// dims).  The 32 W_uv rows are staged in shared memory (row pitch padded by
+// one word, so lane-per-row reads hit 32 different banks) with every load in flight
+// before waiting on the previous kernel; lane = output dim, warp w sums
+// latent slice [R*w/8, R*(w+1)/8) for up to four heads at once, and one
+// shared-memory reduction over the warps finishes.
+constexpr int kCombDims = 32, kCombHB = 4;
+
+template <typename T>
+size_t combine_smem_t(const b200mm_mla_shape& s) {
+  const int hpg = s.H / s.KV;
+  const size_t pitch = (size_t)s.R * sizeof(T) + 4;
+  return sizeof(float) * ((size_t)hpg * s.R + (size_t)(kThreads / 32) * kCombHB * kCombDims) + kCombDims * pitch + 16;
+}
+size_t combine_smem_bytes(const b200mm_mla_shape& s) {
+  return s.dtype == B200MM_F32 ? combine_smem_t<float>(s) : combine_smem_t<__half>(s);
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads) mla_combine_kernel(const MlaDecodeArgs a, MlaWorkspace w) {
+  MLA_SPAN(3, 0);
   extern __shared__ float4 sm4[];
-  float* av = reinterpret_cast<float*>(sm4);  // [hpg][R]
   const int H = a.s.H, KV = a.s.KV, D = a.s.D, R = a.s.R;
-  const int hpg = H / KV, g = blockIdx.x, b = blockIdx.y, h0 = g * hpg;
+  const int hpg = H / KV, g = blockIdx.x, b = blockIdx.y, h0 = g * hpg, d0 = blockIdx.z * kCombDims;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int NWp = kThreads / 32;
+  float* av = reinterpret_cast<float*>(sm4);   // [hpg][R]
+  float* red = av + hpg * R;                   // [warp][head][dim]
+  unsigned char* wrows = reinterpret_cast<unsigned char*>(red + NWp * kCombHB * kCombDims);
+  const int pitch = R * (int)sizeof(T) + 4;    // bytes per staged W_uv row (4-byte aligned)
+  const T* wuv = static_cast<const T*>(a.w_uv) + (int64_t)g * D * R;
+  constexpr int VE = 16 / sizeof(T);
+  const bool vec = (R % VE) == 0 && ((reinterpret_cast<uintptr_t>(wuv) & 15u) == 0);
+  const int per_row = R / VE, nrows = min(kCombDims, D - d0), total = nrows * per_row;
+  constexpr int U = 4;
+  uint4 r[U];
+  if (vec) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int e = u * kThreads + threadIdx.x;
+      if (e < total) r[u] = *reinterpret_cast<const uint4*>(wuv + (int64_t)(d0 + e / per_row) * R + (e % per_row) * VE);
+    }
+  }
   pdl_trigger();
   pdl_wait();
-  const float* src = static_cast<const float*>(a.ws) + w.off_av / 4 + ((int64_t)b * H + h0) * R;
-  if ((R & 3) == 0) {  // the workspace's av rows start 16-byte aligned when R % 4 == 0
-    for (int o = threadIdx.x; o < hpg * R / 4; o += blockDim.x) sm4[o] = reinterpret_cast<const float4*>(src)[o];
-  } else {
-    for (int o = threadIdx.x; o < hpg * R; o += blockDim.x) av[o] = src[o];
-  }
-  __syncthreads();
-  // a split kernel that gave up on a bounded wait leaves NaN, never a silent result
-  const bool failed = *reinterpret_cast<const int*>(static_cast<const unsigned char*>(a.ws) + w.off_err) != 0;
-  const T* wuv = static_cast<const T*>(a.w_uv) + (int64_t)g * D * R;
-  constexpr int HB = 4;
-  constexpr int VE = Chunk<T>::kElems;  // elements per 16-byte load
-  const bool vec = (R % VE) == 0 && ((reinterpret_cast<uintptr_t>(wuv) & 15u) == 0);
-  for (int dd = 0; dd < kCombPerWarp; ++dd) {
-    const int d = blockIdx.z * kCombDims + kCombPerWarp * warp + dd;
-    if (d >= D) break;
-    const T* wr = wuv + (int64_t)d * R;
-    for (int hb = 0; hb < hpg; hb += HB) {
-      float v[HB] = {0.f, 0.f, 0.f, 0.f};
-      if (vec) {
-        for (int r = VE * lane; r < R; r += 32 * VE) {
-          float f[VE];
-          Chunk<T>::unpack(*reinterpret_cast<const uint4*>(wr + r), f);
+  if (vec) {
+    for (int pass = 0; pass * U * kThreads < total; ++pass) {
+      if (pass > 0) {
 #pragma unroll
-          for (int j = 0; j < HB; ++j) {
-            if (hb + j >= hpg) break;
-            const float4* ar = reinterpret_cast<const float4*>(av + (hb + j) * R + r);
-#pragma unroll
-            for (int e4 = 0; e4 < VE / 4; ++e4) {
-              const float4 x = ar[e4];
-              v[j] = fmaf(f[4 * e4], x.x, v[j]);
-              v[j] = fmaf(f[4 * e4 + 1], x.y, v[j]);
-              v[j] = fmaf(f[4 * e4 + 2], x.z, v[j]);
-              v[j] = fmaf(f[4 * e4 + 3], x.w, v[j]);
-            }
-          }
-        }
-      } else {
-        for (int r = lane; r < R; r += 32) {
-          const float wv = ldf(wr, r);
-#pragma unroll
-          for (int j = 0; j < HB; ++j)
-            if (hb + j < hpg) v[j] = fmaf(wv, av[(hb + j) * R + r], v[j]);
+        for (int u = 0; u < U; ++u) {
+          const int e = (pass * U + u) * kThreads + threadIdx.x;
+          if (e < total)
+            r[u] = *reinterpret_cast<const uint4*>(wuv + (int64_t)(d0 + e / per_row) * R + (e % per_row) * VE);
         }
       }
 #pragma unroll
-      for (int j = 0; j < HB; ++j) {
-        if (hb + j >= hpg) break;
-        const float s = warp_sum(v[j]);
-        if (lane == 0) {
-          T* out = static_cast<T*>(a.out) + (int64_t)b * a.o_sb + (int64_t)(h0 + hb + j) * D;
-          out[d] = from_f<T>(failed ? __int_as_float(0x7fc00000) : s);
+      for (int u = 0; u < U; ++u) {
+        const int e = (pass * U + u) * kThreads + threadIdx.x;
+        if (e < total) {
+          uint32_t* dst = reinterpret_cast<uint32_t*>(wrows + (e / per_row) * pitch + (e % per_row) * 16);
+          dst[0] = r[u].x;
+          dst[1] = r[u].y;
+          dst[2] = r[u].z;
+          dst[3] = r[u].w;
         }
       }
     }
+  } else {
+    for (int e = threadIdx.x; e < nrows * R; e += blockDim.x)
+      reinterpret_cast<T*>(wrows + (e / R) * pitch)[e % R] = wuv[(int64_t)(d0 + e / R) * R + e % R];
   }
+  const float* src = static_cast<const float*>(a.ws) + w.off_av / 4 + ((int64_t)b * H + h0) * R;
+  for (int o = threadIdx.x; o < hpg * R; o += blockDim.x) av[o] = src[o];
+  __syncthreads();
+  // a split kernel that gave up on a bounded wait leaves NaN, never a silent result
+  const bool failed = *reinterpret_cast<const int*>(static_cast<const unsigned char*>(a.ws) + w.off_err) != 0;
+  const int r0 = (int)((int64_t)R * warp / NWp), r1 = (int)((int64_t)R * (warp + 1) / NWp);
+  const T* wr = reinterpret_cast<const T*>(wrows + lane * pitch);
+  for (int hb = 0; hb < hpg; hb += kCombHB) {
+    float v[kCombHB] = {};
+    if (lane < nrows) {
+      int rr = r0;
+      if (sizeof(T) == 2) {  // pairs: one 4-byte read per lane (r0 is even when R % 16 == 0)
+        for (; (r0 & 1) == 0 && rr + 1 < r1; rr += 2) {
+          const uint32_t pr = *reinterpret_cast<const uint32_t*>(wr + rr);
+          const T* pe = reinterpret_cast<const T*>(&pr);
+          const float w0 = to_f<T>(pe[0]), w1 = to_f<T>(pe[1]);
+#pragma unroll
+          for (int j = 0; j < kCombHB; ++j) {
+            if (hb + j >= hpg) break;
+            const float2 x = *reinterpret_cast<const float2*>(av + (hb + j) * R + rr);
+            v[j] = fmaf(w0, x.x, fmaf(w1, x.y, v[j]));
+          }
+        }
+      }
+      for (; rr < r1; ++rr) {
+        const float wv = to_f<T>(wr[rr]);
+#pragma unroll
+        for (int j = 0; j < kCombHB; ++j)
+          if (hb + j < hpg) v[j] = fmaf(wv, av[(hb + j) * R + rr], v[j]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kCombHB; ++j) red[(warp * kCombHB + j) * kCombDims + lane] = v[j];
+    __syncthreads();
+    if (threadIdx.x < kCombHB * kCombDims) {
+      const int j = threadIdx.x / kCombDims, dd = threadIdx.x % kCombDims;
+      if (hb + j < hpg && dd < nrows) {
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < NWp; ++k) s += red[(k * kCombHB + j) * kCombDims + dd];
+        T* out = static_cast<T*>(a.out) + (int64_t)b * a.o_sb + (int64_t)(h0 + hb + j) * D;
+        out[d0 + dd] = from_f<T>(failed ? __int_as_float(0x7fc00000) : s);
+      }
+    }
+    __syncthreads();
+  }
+  MLA_SPAN(3, 1);
 }
 
 size_t split_smem_bytes(const b200mm_mla_shape& s) {
@@ -486,7 +580,7 @@ int decode_t(const MlaDecodeArgs& a) {
   st = launch_smem(mla_merge_kernel<T>, dim3(H, B, w.rchunks), merge_smem_bytes(w), a.stream, a, w);
   if (st) return st;
   return launch_smem(mla_combine_kernel<T>, dim3(a.s.KV, B, (a.s.D + kCombDims - 1) / kCombDims),
-                     sizeof(float) * (H / a.s.KV) * a.s.R, a.stream, a, w);
+                     combine_smem_bytes(a.s), a.stream, a, w);
 }
 
 template <typename T>
@@ -506,7 +600,7 @@ int mla_validate_shape(const b200mm_mla_shape& s) {
   if (s.R < 1 || s.R > 4096) return B200MM_ERR_SHAPE;
   if (!(s.eps >= 0.f)) return B200MM_ERR_ARG;
   if (split_smem_bytes(s) > 200 * 1024 || absorb_smem_bytes(s) > 200 * 1024) return B200MM_ERR_SHAPE;
-  if (sizeof(float) * (size_t)(s.H / s.KV) * s.R > 200 * 1024) return B200MM_ERR_SHAPE;  // combine's av
+  if (combine_smem_bytes(s) > 200 * 1024) return B200MM_ERR_SHAPE;
   return B200MM_OK;
 }
 

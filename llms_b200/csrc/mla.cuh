@@ -61,6 +61,26 @@ __host__ __device__ inline int64_t mla_range_begin(const MlaWorkspace& w, int i)
 }
 
 int mla_validate_shape(const b200mm_mla_shape& s);
+#ifdef MLA_TC_TRACE
+// Development trace (debug builds only): per MLA kernel k (0 absorb, 1 split,
+// 2 merge, 3 combine) the earliest start (stored inverted, so one atomicMax
+// keeps the minimum) and the latest end, written past the end of the planned
+// workspace after the split kernel's own trace.
+#define MLA_SPAN(k, end_)                                                                               \
+  do {                                                                                                  \
+    if (threadIdx.x == 0) {                                                                             \
+      unsigned long long* sp_ = reinterpret_cast<unsigned long long*>(static_cast<unsigned char*>(a.ws) + \
+                                                                      w.total) + (size_t)w.G * 8 * 16; \
+      const unsigned long long t_ = global_ns();                                                        \
+      atomicMax(&sp_[2 * (k) + (end_)], (end_) ? t_ : ~t_);                                              \
+    }                                                                                                   \
+  } while (0)
+#else
+#define MLA_SPAN(k, end_) \
+  do {                    \
+  } while (0)
+#endif
+
 MlaWorkspace mla_plan(const b200mm_mla_shape& s, int64_t L, bool fast);
 size_t mla_workspace_bytes(const b200mm_mla_shape& s, int64_t L);
 int mla_append_launch(const MlaAppendArgs& a);
@@ -68,7 +88,7 @@ int mla_decode_launch(const MlaDecodeArgs& a);
 
 // production-shape split kernel (R=256, D=128, DR=32, H=32, KV=8, 16-bit dtype)
 struct MlaMaps {
-  CUtensorMap c, kz, ks;  // TMA maps of c_kv, k_rope_pre and the k-RMS side-band (token extent = L)
+  CUtensorMap c, kz, ks;  // TMA maps of c_kv, the RoPE'd-key side-band and the k-RMS side-band (token extent = L)
 };
 bool mla_fast_supported(const MlaDecodeArgs& a);
 bool mla_fast_maps(const MlaDecodeArgs& a, MlaMaps* maps);  // false if the driver rejects a map

@@ -1,6 +1,6 @@
 // MLA latent decode, production shape (R=256, D=128, DR=32, H=32, KV=8;
 // bf16 or fp16): when the tensor-core split kernel applies, and its TMA
-// tensor maps (3-D maps over [batch, token, channel]; the token extent is L,
+// tensor maps (the token extent is L,
 // so rows past the context arrive as zeros).
 #include "mla.cuh"
 
@@ -37,9 +37,13 @@ bool mla_fast_maps(const MlaDecodeArgs& a, MlaMaps* m) {
   const uint64_t csb = B > 1 ? (uint64_t)a.c_sb * 2 : L * a.c_st * 2;
   const uint64_t zsb = B > 1 ? (uint64_t)a.z_sb * 2 : L * a.z_st * 2;
   const uint64_t ssb = B > 1 ? (uint64_t)a.s_sb * 4 : L * a.s_st * 4;
-  return make_map_3d(&m->c, dt, a.c_kv, FR, L, B, (uint64_t)a.c_st * 2, csb, 64, TT, 1, CU_TENSOR_MAP_SWIZZLE_128B) &&
-         make_map_3d(&m->kz, dt, a.kz, FKV * FDR, L, B, (uint64_t)a.z_st * 2, zsb, 64, TT, 1,
-                     CU_TENSOR_MAP_SWIZZLE_128B) &&
+  // c and kz as [batch][4 column blocks][token][64]: one TMA instruction brings
+  // a unit's four 64-column boxes, landing as four consecutive swizzled boxes
+  const uint64_t cd[4] = {64, L, 4, B}, zd[4] = {64, L, 4, B};
+  const uint64_t cs[3] = {(uint64_t)a.c_st * 2, 128, csb}, zs[3] = {(uint64_t)a.z_st * 2, 128, zsb};
+  const uint32_t box[4] = {64, (uint32_t)TT, 4, 1};
+  return make_map_4d(&m->c, dt, a.c_kv, cd, cs, box, CU_TENSOR_MAP_SWIZZLE_128B) &&
+         make_map_4d(&m->kz, dt, a.kz, zd, zs, box, CU_TENSOR_MAP_SWIZZLE_128B) &&
          make_map_3d(&m->ks, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.kscale, FKV, L, B, (uint64_t)a.s_st * 4, ssb, FKV,
                      TT, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
 }

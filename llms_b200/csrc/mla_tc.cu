@@ -5,9 +5,10 @@
 // mla.cuh) with three roles:
 //   warp 0      TMA producer: per unit, the latent rows c [64 tokens x 256]
 //               and the RoPE'd-key side-band z [64 x 8*32] as four 64-column
-//               boxes each, 128-byte swizzled, plus the k-RMS side-band s
-//               [64 x 8]; a ring of three stages guarded by full / empty
-//               mbarriers.
+//               boxes each (one 4-D TMA instruction per tensor: a TMA
+//               instruction costs ~130 ns to issue whatever its size),
+//               128-byte swizzled, plus the k-RMS side-band s [64 x 8]; a
+//               ring of three stages guarded by full / empty mbarriers.
 //   warps 1,6,7 one thread each issues tcgen05.mma (warp 1 also owns TMEM):
 //                 scores  S[64 x 32] (M = 64 tokens, N = 32 heads):
 //                           c-part  A = c box j, B = qt rows (K-major), 16
@@ -159,6 +160,7 @@ __global__ void __launch_bounds__(kThr, 1)
   TcSmem& S = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   volatile int* failed = &S.failed;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  MLA_SPAN(1, 0);
   const int cta = blockIdx.x;
   float* ws = static_cast<float*>(a.ws);
   int* err = reinterpret_cast<int*>(static_cast<unsigned char*>(a.ws) + w.off_err);
@@ -195,13 +197,30 @@ __global__ void __launch_bounds__(kThr, 1)
   tc_fence_after();
   const uint32_t tmem = S.tmem;
 
+  // one unit's cache rows: the four c boxes, the four z boxes (one 4-D TMA
+  // instruction each) and the k-RMS side-band
+  auto issue = [&](int j) {
+    const int st = j % NST, b = row_of(j), t0 = t0_of(j);
+    unsigned char* sb = S.stage[st];
+    TRACE(0, j);
+    mbar_expect_tx(&S.full[st], kStage);
+    tma_load_4d(sb, &map_c, 0, t0, 0, b, &S.full[st]);
+    tma_load_4d(sb + kZOff, &map_z, 0, t0, 0, b, &S.full[st]);
+    tma_load_3d(sb + kSOff, &map_s, 0, t0, b, &S.full[st]);
+  };
+  // The absorb kernel releases this one only after its own predecessor (the
+  // cache append) finished, so the cache may be fetched before the wait; the
+  // absorbed queries (workspace) are read after it.
+  const int pre = n < NST ? n : NST;
+  if (tid == 0)
+    for (int j = 0; j < pre; ++j) issue(j);
   pdl_trigger();
-  pdl_wait();  // the cache, side-bands and absorbed queries come from earlier kernels
+  pdl_wait();
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      int j = 0;
+      int j = pre;
       for (; j < n; ++j) {
         const int st = j % NST;
         if (j >= NST && !mbar_wait(&S.empty[st], (uint32_t)(((j - NST) / NST) & 1))) {
@@ -209,16 +228,7 @@ __global__ void __launch_bounds__(kThr, 1)
           break;
         }
         if (*failed) break;
-        const int b = row_of(j), t0 = t0_of(j);
-        unsigned char* sb = S.stage[st];
-        TRACE(0, j);
-        mbar_expect_tx(&S.full[st], kStage);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tma_load_3d(sb + c * kBox, &map_c, 64 * c, t0, b, &S.full[st]);
-          tma_load_3d(sb + kZOff + c * kBox, &map_z, 64 * c, t0, b, &S.full[st]);
-        }
-        tma_load_3d(sb + kSOff, &map_s, 0, t0, b, &S.full[st]);
+        issue(j);
       }
       S.issued = j;
     }
@@ -307,15 +317,22 @@ __global__ void __launch_bounds__(kThr, 1)
     auto load_q = [&](int b) {  // queries of batch row b, storage dtype, K-major swizzled
       const float* qt = ws + w.off_qt / 4 + (int64_t)b * FH * FR;
       const float* qr = ws + w.off_qr / 4 + (int64_t)b * FH * FDR;
-      for (int i = gt; i < FH * 32; i += 128) {  // qt: 32 rows x 32 chunks of 8
-        const int row = i >> 5, c8 = i & 31, k0 = 8 * c8;
-        const float4 v0 = *reinterpret_cast<const float4*>(qt + row * FR + k0);
-        const float4 v1 = *reinterpret_cast<const float4*>(qt + row * FR + k0 + 4);
+      constexpr int QI = FH * 32 / 128;  // qt: 32 rows x 32 chunks of 8, QI per thread, all loads first
+      float4 v[QI][2];
+#pragma unroll
+      for (int u = 0; u < QI; ++u) {
+        const int i = gt + 128 * u, row = i >> 5, k0 = 8 * (i & 31);
+        v[u][0] = *reinterpret_cast<const float4*>(qt + row * FR + k0);
+        v[u][1] = *reinterpret_cast<const float4*>(qt + row * FR + k0 + 4);
+      }
+#pragma unroll
+      for (int u = 0; u < QI; ++u) {
+        const int i = gt + 128 * u, row = i >> 5, c8 = i & 31;
         uint4 o;
-        o.x = pack2<T>(v0.x, v0.y);
-        o.y = pack2<T>(v0.z, v0.w);
-        o.z = pack2<T>(v1.x, v1.y);
-        o.w = pack2<T>(v1.z, v1.w);
+        o.x = pack2<T>(v[u][0].x, v[u][0].y);
+        o.y = pack2<T>(v[u][0].z, v[u][0].w);
+        o.z = pack2<T>(v[u][1].x, v[u][1].y);
+        o.w = pack2<T>(v[u][1].z, v[u][1].w);
         *reinterpret_cast<uint4*>(S.qt + (c8 >> 3) * (FH * 128) + sw_chunk(row, c8 & 7)) = o;
       }
       {  // qr block j, row i = head 8j+i; nonzero in its group's 32 columns of box j
@@ -481,6 +498,7 @@ __global__ void __launch_bounds__(kThr, 1)
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
+  MLA_SPAN(1, 1);
 }
 
 }  // namespace

@@ -24,6 +24,10 @@ bool make_map_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uin
                  uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1,
                  uint32_t b2, CUtensorMapSwizzle swz);
 
+// 4-D tiled map: dims[0] contiguous; strides in BYTES for dims 1..3.
+bool make_map_4d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, const uint64_t dims[4],
+                 const uint64_t strides_bytes[3], const uint32_t box[4], CUtensorMapSwizzle swz);
+
 bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1,
                  uint64_t stride1_bytes, uint32_t b0, uint32_t b1, CUtensorMapSwizzle swz);
 
@@ -87,6 +91,14 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
       "[%5];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int x, int y, int z, int w,
+                                            void* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+      "%5}], [%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
       : "memory");
 }
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, void* bar) {
