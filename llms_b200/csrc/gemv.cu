@@ -31,8 +31,17 @@ struct GemvParams {
   int M, N, K;
 };
 
+// Two CTAs per SM for M <= 4 (at most 128 registers).  Three per SM with
+// fewer loads in flight made a lone QKV launch faster, but in the decode step
+// the QKV and gate-up launches alternate and a register-full QKV grid keeps
+// the next gate-up grid from starting early, which cost more than it saved.
+template <int MR, bool GATE>
+constexpr int gemv_min_blocks() {
+  return MR <= 4 ? 2 : 1;
+}
+
 template <typename TX, typename TW, int MR, bool GATE, int NCH>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, gemv_min_blocks<MR, GATE>())
 gemv_kernel(const GemvParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   TX* xs = reinterpret_cast<TX*>(smem_raw);  // [MR][K] activation rows
