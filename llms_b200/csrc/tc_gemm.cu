@@ -3,18 +3,22 @@
 //   Y[M, N] = X[M, K] . W[N, K]^T            (fused QKV: W = [Wq; Wk; Wv])
 //   Y[M, N] = silu(X Wg^T) * (X Wu^T)        (fused gate-up-SiLU)
 //
-// One CTA per 128 x BN output tile (BN x 2 for gate-up), 6 warps:
+// Persistent: one CTA per SM walks 128 x BN output tiles (BN x 2 for
+// gate-up; m-tiles vary fastest), 6 warps:
 //   warp 0      TMA producer: X box [64 k x 128 rows], W box(es) [64 k x BN
 //               rows], 128-byte swizzle, into a STAGES-deep ring guarded by
-//               full/empty mbarriers;
+//               full/empty mbarriers, continuous across the CTA's tiles;
 //   warp 1      allocates TMEM, one thread issues tcgen05.mma (kind::f16,
 //               M = 128, N = BN, K = 16 per instruction, fp32 accumulator in
-//               TMEM) and frees each stage with tcgen05.commit;
+//               TMEM) and frees each stage with tcgen05.commit; tile j
+//               accumulates into buffer j & 1, so the epilogue of tile j
+//               overlaps the main loop of tile j + 1;
 //   warps 2-5   epilogue: tcgen05.ld of the accumulator (each warp reads its
 //               32-lane quadrant), SiLU * up in registers for gate-up, one
-//               rounding to the output dtype, 16-byte stores.
+//               rounding to the output dtype, 16-byte stores, then the buffer
+//               is handed back to the issuer.
 // Every mbarrier wait is bounded; a CTA whose wait expires stops issuing,
-// drains its own copies in flight, frees TMEM and writes NaN over its tile.
+// drains its own copies in flight, frees TMEM and writes NaN over its tiles.
 #include "dense.cuh"
 #include "tcgen05.cuh"
 
@@ -25,7 +29,7 @@ namespace {
 constexpr int BM = 128;  // tile rows (X rows) = MMA M = TMEM lanes
 constexpr int BK = 64;   // K per stage: 128 bytes of 16-bit elements (one swizzle span)
 constexpr int kThreads = 192;
-constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kTmemCols = 512;  // two accumulator buffers (one CTA per SM)
 
 template <bool GATE, int BN>
 struct Cfg {
@@ -67,21 +71,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap mx, const __grid_constant__ CUtensorMap mw0,
                    const __grid_constant__ CUtensorMap mw1, const TcParams p) {
   using C = Cfg<GATE, BN>;
+  constexpr uint32_t ACC = C::NB * BN;  // TMEM columns of one tile's accumulators
+  static_assert(2 * ACC <= kTmemCols, "two accumulator buffers must fit the TMEM allocation");
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                        ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + C::STAGES * C::STAGE_BYTES);
   uint64_t* empty = full + C::STAGES;
-  uint64_t* accum = empty + C::STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* acc_full = empty + C::STAGES;  // [2]: a tile's accumulators are complete
+  uint64_t* acc_empty = acc_full + 2;      // [2]: the epilogue has read them
+  uint64_t* mma_done = acc_empty + 2;      // every MMA of this CTA has completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* failed = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* issued = const_cast<int*>(failed) + 1;
   int* consumed = issued + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // m-tiles vary fastest: a wave covers all of X against a narrow band of W,
-  // so each weight row leaves HBM once and X stays in L2
-  const int tile_m = blockIdx.x, tile_n = blockIdx.y;
+  // Persistent: CTA c takes tiles c, c + G, ...; m-tiles vary fastest, so the
+  // tiles in flight at once cover all of X against a narrow band of W (each
+  // weight row leaves HBM once, X stays in L2).
+  const int mt = (p.M + BM - 1) / BM, ntl = (p.N + BN - 1) / BN, tiles = mt * ntl;
+  const int mine = blockIdx.x < tiles ? (tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
   const int nk = (p.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -89,7 +99,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    mbar_init(mma_done, 1);
     *failed = 0;
     *issued = 0;
     *consumed = 0;
@@ -98,9 +112,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_map(&mw0);
     if (GATE) prefetch_map(&mw1);
   }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
-  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -110,88 +122,121 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_wait();  // X may be the output of the previous kernel
 
   if (warp == 0) {
+    // ---------------- TMA producer: one ring across all of this CTA's tiles ----------------
     if (lane == 0) {
-      int kb = 0;
-      for (; kb < nk; ++kb) {
-        const int s = kb % C::STAGES, it = kb / C::STAGES;
-        if (kb >= C::STAGES && !mbar_wait(&empty[s], (uint32_t)((it - 1) & 1))) {
-          *failed = 1;
-          break;
+      int g = 0;
+      bool ok = true;
+      for (int j = 0; ok && j < mine; ++j) {
+        const int t = blockIdx.x + j * gridDim.x, tm = t % mt, tn = t / mt;
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % C::STAGES, it = g / C::STAGES;
+          if (g >= C::STAGES && !mbar_wait(&empty[s], (uint32_t)((it - 1) & 1))) ok = false;
+          if (!ok || *failed) {
+            ok = false;
+            break;
+          }
+          unsigned char* st = sm + s * C::STAGE_BYTES;
+          mbar_expect_tx(&full[s], C::STAGE_BYTES);
+          tma_load_2d(st, &mx, kb * BK, tm * BM, &full[s]);
+          tma_load_2d(st + C::A_BYTES, &mw0, kb * BK, tn * BN, &full[s]);
+          if (GATE) tma_load_2d(st + C::A_BYTES + C::B_BYTES, &mw1, kb * BK, tn * BN, &full[s]);
         }
-        if (*failed) break;
-        unsigned char* st = sm + s * C::STAGE_BYTES;
-        mbar_expect_tx(&full[s], C::STAGE_BYTES);
-        tma_load_2d(st, &mx, kb * BK, tile_m * BM, &full[s]);
-        tma_load_2d(st + C::A_BYTES, &mw0, kb * BK, tile_n * BN, &full[s]);
-        if (GATE) tma_load_2d(st + C::A_BYTES + C::B_BYTES, &mw1, kb * BK, tile_n * BN, &full[s]);
       }
-      *issued = kb;
+      if (!ok) *failed = 1;
+      *issued = g;
     }
   } else if (warp == 1) {
+    // ---------------- MMA issuer: tile j accumulates into buffer j & 1 ----------------
     if (lane == 0) {
       // gate-up: the Wg and Wu boxes are adjacent in shared memory, so one
       // N = 2*BN instruction reads A once and fills [gate | up] accumulators
       constexpr uint32_t ID = idesc<T, GATE ? 2 * BN : BN>();
-      int kb = 0;
-      for (; kb < nk; ++kb) {
-        const int s = kb % C::STAGES, it = kb / C::STAGES;
-        if (!mbar_wait(&full[s], (uint32_t)(it & 1))) {
-          *failed = 1;
+      int g = 0;
+      bool ok = true;
+      for (int j = 0; ok && j < mine; ++j) {
+        const int b = j & 1;
+        // the epilogue of tile j - 2 must have read this buffer
+        if (j >= 2 && !mbar_wait(&acc_empty[b], (uint32_t)(((j >> 1) - 1) & 1))) {
+          ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t st = smem_u32(sm + s * C::STAGE_BYTES);
-        const uint64_t a = sdesc(st), b = sdesc(st + C::A_BYTES);
+        const uint32_t d = tmem + b * ACC;
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % C::STAGES, it = g / C::STAGES;
+          if (!mbar_wait(&full[s], (uint32_t)(it & 1)) || *failed) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = smem_u32(sm + s * C::STAGE_BYTES);
+          const uint64_t a = sdesc(st), bd = sdesc(st + C::A_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk) {
-          // +32 bytes of K per instruction inside the 128-byte swizzle span
-          mma_f16(tmem, a + 2 * kk, b + 2 * kk, ID, (kb | kk) != 0);
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            // +32 bytes of K per instruction inside the 128-byte swizzle span
+            mma_f16(d, a + 2 * kk, bd + 2 * kk, ID, (kb | kk) != 0);
+          }
+          mma_commit(&empty[s]);
         }
-        mma_commit(&empty[s]);
+        if (ok) mma_commit(&acc_full[b]);  // fires once the tile's MMAs have completed
       }
-      *consumed = kb;
-      mma_commit(accum);  // fires once every MMA issued above has completed
+      if (!ok) *failed = 1;
+      *consumed = g;
+      // let every MMA issued above finish before TMEM can be freed (its own
+      // barrier: one more arrival on acc_full could run ahead of the epilogue)
+      mma_commit(mma_done);
     }
   } else {
-    // epilogue: warps 2..5 -> TMEM lane quadrant warp % 4
-    const bool ok = mbar_wait(accum, 0);
-    tc_fence_after();
-    const bool bad = !ok || *failed;
+    // ---------------- epilogue: warps 2..5 -> TMEM lane quadrant warp % 4 ----------------
     const int q = warp & 3;
-    const int row = tile_m * BM + 32 * q + lane;
     const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16);
-    T* yrow = static_cast<T*>(p.y) + (int64_t)row * p.ldy;
+    bool bad = false;
+    for (int j = 0; j < mine; ++j) {
+      const int t = blockIdx.x + j * gridDim.x, tm = t % mt, tn = t / mt;
+      const int b = j & 1;
+      if (!bad) {
+        bad = !mbar_wait(&acc_full[b], (uint32_t)((j >> 1) & 1)) || *failed;
+        tc_fence_after();
+      }
+      const int row = tm * BM + 32 * q + lane;
+      T* yrow = static_cast<T*>(p.y) + (int64_t)row * p.ldy;
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
-      float v[32];
-      tmem_ld32(tq + c, v);
-      if (GATE) {
-        float u[32];
-        tmem_ld32(tq + BN + c, u);
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        if (!bad) {
+          tmem_ld32(tq + b * ACC + c, v);
+          if (GATE) {
+            float u[32];
+            tmem_ld32(tq + b * ACC + BN + c, u);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = silu_mul(v[i], u[i]);
-      }
-      if (bad) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __int_as_float(0x7fc00000);
-      }
-      if (row < p.M) {
-        const int n0 = tile_n * BN + c;
-        if (n0 + 32 <= p.N) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint4 o;
-            o.x = pack_out<T>(v[8 * j + 0], v[8 * j + 1]);
-            o.y = pack_out<T>(v[8 * j + 2], v[8 * j + 3]);
-            o.z = pack_out<T>(v[8 * j + 4], v[8 * j + 5]);
-            o.w = pack_out<T>(v[8 * j + 6], v[8 * j + 7]);
-            *reinterpret_cast<uint4*>(yrow + n0 + 8 * j) = o;
+            for (int i = 0; i < 32; ++i) v[i] = silu_mul(v[i], u[i]);
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (n0 + i < p.N) yrow[n0 + i] = from_f<T>(v[i]);
+          for (int i = 0; i < 32; ++i) v[i] = __int_as_float(0x7fc00000);
         }
+        if (row < p.M) {
+          const int n0 = tn * BN + c;
+          if (n0 + 32 <= p.N) {
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+              uint4 o;
+              o.x = pack_out<T>(v[8 * jj + 0], v[8 * jj + 1]);
+              o.y = pack_out<T>(v[8 * jj + 2], v[8 * jj + 3]);
+              o.z = pack_out<T>(v[8 * jj + 4], v[8 * jj + 5]);
+              o.w = pack_out<T>(v[8 * jj + 6], v[8 * jj + 7]);
+              *reinterpret_cast<uint4*>(yrow + n0 + 8 * jj) = o;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (n0 + i < p.N) yrow[n0 + i] = from_f<T>(v[i]);
+          }
+        }
+      }
+      if (!bad) {
+        tc_fence_before();
+        mbar_arrive(&acc_empty[b]);  // buffer b may take tile j + 2
       }
     }
   }
@@ -200,9 +245,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (threadIdx.x == 0 && *failed) {
     // copies issued but never consumed still target this CTA's shared memory
-    for (int kb = *consumed; kb < *issued; ++kb)
-      mbar_wait(&full[kb % C::STAGES], (uint32_t)((kb / C::STAGES) & 1));
+    for (int g = *consumed; g < *issued; ++g) mbar_wait(&full[g % C::STAGES], (uint32_t)((g / C::STAGES) & 1));
   }
+  if (threadIdx.x == 32) mbar_wait(mma_done, 0);
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
@@ -244,8 +289,10 @@ int launch_bn(const DenseArgs& a) {
     configured[dev] = true;
   }
   TcParams p{a.M, a.N, a.K, a.y, a.ldy};
-  dim3 grid((a.M + BM - 1) / BM, (a.N + BN - 1) / BN);
-  if (grid.x > 2147483647u || grid.y > 65535u) return B200MM_ERR_SHAPE;
+  const long tiles = (long)((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
+  if (tiles > 2147483647L) return B200MM_ERR_SHAPE;
+  const int sms = num_sms(dev);
+  dim3 grid((unsigned)(tiles < sms ? tiles : sms));  // persistent: one CTA per SM
   return launch_pdl(kern, grid, dim3(kThreads), C::SMEM, a.stream, mx, mw0, mw1, p) == cudaSuccess
              ? B200MM_OK
              : B200MM_ERR_LAUNCH;
