@@ -298,18 +298,26 @@ int launch_bn(const DenseArgs& a) {
              : B200MM_ERR_LAUNCH;
 }
 
-// N tile: the widest whose grid still gives every SM a tile.
+// N tile: the one with the least streaming per SM.  A CTA's tile reads
+// BM x K of X and (2 x) BN x K of W, and the persistent grid takes
+// ceil(tiles / SMs) rounds, so cost(BN) = rounds x (BM + NB * BN) -- e.g. at
+// M = 128 gate-up, 76 tiles of BN = 128 in one round beat 152 tiles of
+// BN = 64 in two.
 template <typename T>
 int launch_t(const DenseArgs& a) {
-  const int sms = num_sms(current_device());
+  const long sms = num_sms(current_device());
   const long mt = (a.M + BM - 1) / BM;
-  auto tiles = [&](int bn) { return mt * ((a.N + bn - 1) / bn); };
+  auto cost = [&](int bn, int nb) {
+    const long tiles = mt * ((a.N + bn - 1) / bn);
+    return ((tiles + sms - 1) / sms) * (long)(BM + nb * bn);
+  };
   if (a.gate) {
-    if (tiles(128) >= sms) return launch_bn<T, true, 128>(a);
-    return launch_bn<T, true, 64>(a);
+    const long c128 = cost(128, 2), c64 = cost(64, 2);
+    return c128 <= c64 ? launch_bn<T, true, 128>(a) : launch_bn<T, true, 64>(a);
   }
-  if (tiles(256) >= sms) return launch_bn<T, false, 256>(a);
-  if (tiles(128) >= sms) return launch_bn<T, false, 128>(a);
+  const long c256 = cost(256, 1), c128 = cost(128, 1), c64 = cost(64, 1);
+  if (c256 <= c128 && c256 <= c64) return launch_bn<T, false, 256>(a);
+  if (c128 <= c64) return launch_bn<T, false, 128>(a);
   return launch_bn<T, false, 64>(a);
 }
 
