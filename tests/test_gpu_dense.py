@@ -305,3 +305,21 @@ def test_int8_prefill_m(M):
     q, k, v = int8_fused_qkv(x, to(lay["qkv_q"]), to(lay["qkv_s"]), n_q=768, n_k=128)
     e = lay["x"][rows].astype(np.float64) @ O.dequant(lay["qkv_q"][:1024], lay["qkv_s"][:1024]).T
     bf16_check(host(torch.cat([q, k, v], -1))[rows], e)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 96, 2560), (1, 768, 2560), (3, 1216, 4096), (2, 770, 2560), (1, 4000, 1024)])
+@pytest.mark.parametrize("gate", [False, True])
+def test_decode_column_shards(M, N, K, gate):
+    """Decode on a column shard (down to N/8 of a layer, odd N, odd M)."""
+    from llms_b200.kernels import triton_fused_gate_up_silu, triton_fused_qkv
+    rng = np.random.default_rng(N + K + M)
+    xd = dev(rng.standard_normal((M, K), dtype=np.float32))
+    w0d = dev(rng.standard_normal((N, K), dtype=np.float32) * 0.02)
+    if gate:
+        w1d = dev(rng.standard_normal((N, K), dtype=np.float32) * 0.02)
+        bf16_check(host(triton_fused_gate_up_silu(xd, w0d, w1d)), O.gate_up_silu(host(xd), host(w0d), host(w1d)))
+    else:
+        nk = N // 8
+        q, k, v = triton_fused_qkv(xd, w0d, n_q=N - 2 * nk, n_k=nk)
+        e = host(xd).astype(np.float64) @ host(w0d).astype(np.float64).T
+        bf16_check(host(torch.cat([q, k, v], -1)), e)
