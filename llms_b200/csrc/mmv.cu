@@ -75,7 +75,10 @@ __global__ void __launch_bounds__(kThreads) mmv_kernel(const MmvParams p) {
   constexpr int KC = W8 ? 64 : 32;       // K columns per warp-chunk (4 lanes x 16 bytes)
   constexpr int NM = GATE ? 2 : 1;
   constexpr int MP = 8 * MT;             // padded activation rows
-  constexpr int U = 2;                   // chunks in flight per warp
+  // chunks in flight per warp (measured): a 16-bit QKV chunk is only 1 KB per
+  // warp, so QKV keeps 8 (int8: 4 up to 16 rows); gate-up holds two matrices'
+  // chunks and loses occupancy beyond 2
+  constexpr int U = GATE ? 2 : (W8 ? (MT <= 2 ? 4 : 2) : 8);
   constexpr int RP = MP + 2;             // reduction row pitch: even, so float2 stores stay aligned
   extern __shared__ __align__(16) unsigned char smem_raw[];
   // row pitch (elements): a 16-byte load phase of 8 lanes covers 2 rows x 64
