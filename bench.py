@@ -20,6 +20,8 @@ e2e   : the same job through the public API (llms_b200.kernels functions,
         pinned host memory and all outputs copied back, inside the timed region.
 suite : (rank 0, N = 1) the other BASELINE sub-metrics measured in the same
         run: per-op GB/s at M = 1, TFLOP/s at M = 2048, MLA decode GB/s.
+mla_decode_b32_l32768_sharded : (N > 1) MLA decode at B = 32, L = 32768 split
+        by batch row across the ranks, whole-job GB/s (max-over-ranks time).
 """
 
 from __future__ import annotations
@@ -450,6 +452,54 @@ def suite(job):
     return out
 
 
+def mla_sharded(rank, world, steps=10):
+    """BASELINE configs[3] across GPUs: MLA decode at B = 32, L = 32768 split
+    by batch row (llms_b200.mla.batch_shard; no collective in the op), one
+    CUDA graph of one decode per rank, device time max over ranks; GB/s is
+    the whole job's algorithmic bytes over that time."""
+    from llms_b200 import mla
+
+    H, KV, D, DR, R, B, L = 32, 8, 128, 32, 256, 32, 32768
+    rows = mla.batch_shard(B, world, rank)
+    b = len(rows)
+    if b:
+        gg = torch.Generator(device="cuda").manual_seed(3 + 1000 * rank)
+        c = torch.randn(b, L, R, device="cuda", dtype=torch.bfloat16, generator=gg)
+        kr = torch.randn(b, L, KV, DR, device="cuda", dtype=torch.bfloat16, generator=gg)
+        wuk = torch.randn(KV, D - DR, R, device="cuda", dtype=torch.bfloat16, generator=gg) * 0.25
+        wuv = torch.randn(KV, D, R, device="cuda", dtype=torch.bfloat16, generator=gg) * 0.25
+        q = torch.randn(b, H, D, device="cuda", dtype=torch.bfloat16, generator=gg)
+        kw = torch.ones(D, device="cuda")
+        inv = mla.rope_inv_freq(D, DR, 1e6, "cuda")
+        ks, kz = mla.mla_sidebands(c, kr, wuk, kw, inv, B=b, L=L, num_kv_heads=KV, head_dim=D, eps=1e-6)
+        del kr
+        ws = torch.empty(mla.workspace_bytes(b, H, KV, D, DR, R, L, torch.bfloat16), dtype=torch.uint8,
+                         device="cuda")
+        o = torch.empty(b, H, D, device="cuda", dtype=torch.bfloat16)
+        fn = lambda: mla.mla_decode(q, c, kz, ks, wuk, wuv, kw, inv, L=L, scale=D ** -0.5, eps=1e-6, out=o,
+                                    workspace=ws)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        sec = time_graph(g, steps, 3, world)
+    else:  # more ranks than batch rows: this rank idles but joins the timing
+        class _Idle:
+            def replay(self):
+                pass
+        sec = time_graph(_Idle(), steps, 3, world)
+    per = sec / steps
+    alg = 1024 * B * L + 32 * B * L + 917504 + 512 * B
+    return {"GB/s": alg / per / 1e9, "us_per_step": per * 1e6, "B": B, "L": L,
+            "split": f"batch rows over {world} GPUs (no collective in the op)",
+            "bytes_note": "512*B*L latent + 512*B*L RoPE'd-key side-band + 32*B*L k-RMS side-band + weights + q/out"}
+
+
 def qwen3_8b_int8_decode(batches=(1, 16, 64), prompt=16):
     """a Qwen3-8B-shaped (36 layers, random init) decode
     step with int8 fused QKV / gate-up (per-row scales), bf16 elsewhere.
@@ -638,6 +688,8 @@ def main():
     extra = {}
     if rank == 0 and world == 1 and not args.no_suite:
         extra["suite"] = suite(job)
+    if world > 1:
+        extra["mla_decode_b32_l32768_sharded"] = mla_sharded(rank, world)
     cpu = None
     if rank == 0 and world == 1:
         from oracle import cpu_baseline as CB

@@ -54,6 +54,19 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+def batch_shard(B: int, world: int, rank: int) -> range:
+    """Batch rows of an MLA decode that GPU `rank` of `world` serves.
+
+    MLA decode shards by batch row with no collective: each GPU streams only
+    its own rows' latent cache (the rows are independent), and outputs are
+    gathered afterwards if the caller needs them on one GPU.  Rank r takes
+    rows [B*r/world, B*(r+1)/world); with B < world the surplus ranks get an
+    empty range and idle (their GB/s counts as zero in an aggregate)."""
+    if world < 1 or not 0 <= rank < world or B < 0:
+        raise ValueError(f"bad shard request: B={B} world={world} rank={rank}")
+    return range(B * rank // world, B * (rank + 1) // world)
+
+
 def workspace_bytes(B: int, H: int, KV: int, D: int, DR: int, R: int, L: int, dtype, eps: float = 1e-6) -> int:
     shp = _shape(B, H, KV, D, DR, R, dtype, eps)
     return int(_capi.lib.b200mm_mla_decode_workspace_size(ctypes.byref(shp), L))
