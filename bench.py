@@ -422,6 +422,39 @@ def suite(job):
             out[f"{name}_m{M}"] = {"us_per_launch": per * 1e6, "GB/s": b / per / 1e9}
             del g, x, y
     del w8
+    # o / down projections (b200mm_linear) at the Qwen3-4B shapes, against
+    # torch's F.linear (cuBLAS), which is what the reference engine runs for
+    # them; 8 weight copies rotate so the weights never sit in L2
+    gl = torch.Generator(device="cuda").manual_seed(6)
+    for name, K in (("o", NQ), ("down", INTER)):
+        wl = [torch.randn(HIDDEN, K, device="cuda", dtype=torch.bfloat16, generator=gl) * 0.02 for _ in range(8)]
+        for M in (1, 16, 128):
+            x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+            y = torch.empty(M, HIDDEN, device="cuda", dtype=torch.bfloat16)
+
+            def run_lin(x=x, y=y, K=K, M=M):
+                s = torch.cuda.current_stream().cuda_stream
+                for w in wl:
+                    st = _capi.lib.b200mm_linear(x.data_ptr(), K, w.data_ptr(), K, y.data_ptr(), HIDDEN,
+                                                 M, HIDDEN, K, 2, s)
+                    _capi.check(st, "b200mm_linear")
+
+            def run_cublas(x=x, y=y):
+                for w in wl:
+                    torch.matmul(x, w.t(), out=y)
+
+            b = op_bytes(HIDDEN, K, M, HIDDEN)
+            res = {}
+            for tag, fn in (("", run_lin), ("cublas_", run_cublas)):
+                g, _ = job.capture(fn)
+                sec = time_graph(g, 20, 2, 1)
+                per = sec / (20 * len(wl))
+                res[tag + "us_per_launch"] = per * 1e6
+                res[tag + "GB/s"] = b / per / 1e9
+                del g
+            out[f"{name}_m{M}"] = res
+            del x, y
+        del wl
     # MLA decode GB/s at L = 32k
     H, KV, D, DR, R = 32, 8, 128, 32, 256
     for B, L in ((32, 32768), (1, 32768)):
@@ -504,14 +537,17 @@ def qwen3_8b_int8_decode(batches=(1, 16, 64), prompt=16):
     """a Qwen3-8B-shaped (36 layers, random init) decode
     step with int8 fused QKV / gate-up (per-row scales), bf16 elsewhere.
     One step = the whole model for one new token per sequence, replayed as a
-    CUDA graph; tok/s = batch / step time.  Greedy agreement is checked
-    against the same model in fp32 with dequantised weights on rows whose
-    fp32 top-2 gap exceeds 4x the observed logit error."""
+    CUDA graph; tok/s = batch / step time.  Measured twice: with the bf16
+    ``o`` / ``down`` projections as torch ``nn.Linear`` (cuBLAS, as in the
+    reference engine) and routed through ``b200mm_linear``.  Greedy agreement
+    is checked against the same model in fp32 with dequantised weights on rows
+    whose fp32 top-2 gap exceeds 4x the observed logit error."""
+    from llms_b200.kernels import apply_linear_kernels
     from llms_b200.qwen3 import greedy, synthetic_int8_model
 
     model = synthetic_int8_model(seed=4)
-    res = {}
-    for B in batches:
+
+    def measure(B):
         g = torch.Generator(device="cuda").manual_seed(100 + B)
         ids = torch.randint(0, model.shape.vocab_size, (B, prompt), generator=g, device="cuda")
         nxt = torch.randint(0, model.shape.vocab_size, (B, 1), generator=g, device="cuda")
@@ -537,12 +573,22 @@ def qwen3_8b_int8_decode(batches=(1, 16, 64), prompt=16):
                 model(nxt, cache, start_pos=prompt)
             sec = time_graph(graph, 20, 3, 1)
             del graph, cache
-        res[f"qwen3_8b_int8_decode_b{B}"] = {
-            "ms_per_step": sec / 20 * 1e3, "tok/s": B * 20 / sec,
+        return sec, {
             "argmax_agree_decided": bool(agree[decided].all().item()),
             "decided_rows": int(decided.sum().item()), "rows": B,
             "argmax_agree_all": float(agree.float().mean().item()),
             "logits_rel_l2": float(((logits - ref).norm() / ref.norm()).item()),
+        }
+
+    cublas = {B: measure(B)[0] for B in batches}
+    apply_linear_kernels(model)
+    res = {}
+    for B in batches:
+        sec, chk = measure(B)
+        res[f"qwen3_8b_int8_decode_b{B}"] = {
+            "ms_per_step": sec / 20 * 1e3, "tok/s": B * 20 / sec,
+            "o_down": "b200mm_linear",
+            "tok/s_o_down_cublas": B * 20 / cublas[B], **chk,
         }
     del model
     torch.cuda.empty_cache()

@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define B200MM_ABI_VERSION 1
+#define B200MM_ABI_VERSION 2
 
 /* status codes */
 enum {
@@ -129,6 +129,27 @@ int b200mm_qkv_w8(const void* x, int64_t ldx,
                   void* y, int64_t ldy,
                   int64_t M, int64_t N, int64_t K,
                   int dtype, void* stream);
+
+/*
+ * Plain bias-free projection, y[m, n] = sum_k x[m,k] * w[n,k], on the same
+ * kernel families as b200mm_qkv (decode GEMV, small-batch tensor-core GEMV,
+ * tcgen05 GEMM).  Replaces the attention output projection `self.o(attn)`
+ * (src/engine/attention.py:163) and the FFN down projection
+ * `self.down(...)` (src/engine/model.py:37), both nn.Linear(bias=False).
+ *   x : [M, K], w : [N, K], y : [M, N]; all `dtype`.
+ */
+int b200mm_linear(const void* x, int64_t ldx,
+                  const void* w, int64_t ldw,
+                  void* y, int64_t ldy,
+                  int64_t M, int64_t N, int64_t K,
+                  int dtype, void* stream);
+
+/* Int8 weight-only b200mm_linear: y = (x . wq^T) * s (see the _w8 block above). */
+int b200mm_linear_w8(const void* x, int64_t ldx,
+                     const int8_t* w, const float* s, int64_t ldw,
+                     void* y, int64_t ldy,
+                     int64_t M, int64_t N, int64_t K,
+                     int dtype, void* stream);
 
 /*
  * MLA latent-cache shapes shared by the two MLA entry points.

@@ -59,6 +59,14 @@ SIGNATURES: dict[str, tuple] = {
         ctypes.c_int,
         [_c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int, _c_p],
     ),
+    "b200mm_linear": (
+        ctypes.c_int,
+        [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int, _c_p],
+    ),
+    "b200mm_linear_w8": (
+        ctypes.c_int,
+        [_c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int, _c_p],
+    ),
     "b200mm_mla_append": (
         ctypes.c_int,
         [ctypes.POINTER(MlaShape), _c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_p,

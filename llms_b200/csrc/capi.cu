@@ -64,12 +64,15 @@ int dense_dispatch(const DenseArgs& a) {
   }
 #endif
   // measured on B200 at the Qwen3 shapes: M <= 4 CUDA-core GEMV; small M the
-  // mma.sync GEMV (bf16 M <= 16, int8 M <= 32); then tcgen05 with the weights
-  // as the MMA's M side (bf16 up to M = 64, int8 any M); bf16 M >= 65 the
-  // tcgen05 GEMM tiled over X
+  // mma.sync GEMV (gate-up M <= 16, plain projections M <= 8, int8 M <= 32);
+  // then tcgen05 with the weights as the MMA's M side (16-bit up to M = 64,
+  // and up to 128 for narrow deep projections such as FFN down, whose few
+  // output tiles leave the GEMM tiled over X short of CTAs; int8 any M);
+  // otherwise the tcgen05 GEMM tiled over X
+  const bool narrow_deep = !a.gate && a.K >= 2 * a.N;
   if (a.M <= 4 && gemv_supported(a)) return gemv_launch(a);
-  if (a.M <= (a.w8 ? 32 : 16) && mmv_supported(a)) return mmv_launch(a);
-  if ((a.w8 || a.M <= 64) && swap_supported(a)) return swap_launch(a);
+  if (a.M <= (a.w8 ? 32 : a.gate ? 16 : 8) && mmv_supported(a)) return mmv_launch(a);
+  if ((a.w8 || a.M <= 64 || (narrow_deep && a.M <= 128)) && swap_supported(a)) return swap_launch(a);
   if (tc_supported(a)) return tc_launch(a);
   if (mmv_supported(a)) return mmv_launch(a);
   if (gemv_supported(a)) return gemv_launch(a);
@@ -167,6 +170,16 @@ int b200mm_qkv_w8(const void* x, int64_t ldx, const int8_t* w, const float* s, i
   a.dtype = dtype; a.w8 = true; a.gate = false;
   a.stream = static_cast<cudaStream_t>(stream);
   return run_dense(a, M, N, K);
+}
+
+int b200mm_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy,
+                  int64_t M, int64_t N, int64_t K, int dtype, void* stream) {
+  return b200mm_qkv(x, ldx, w, ldw, y, ldy, M, N, K, dtype, stream);
+}
+
+int b200mm_linear_w8(const void* x, int64_t ldx, const int8_t* w, const float* s, int64_t ldw,
+                     void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int dtype, void* stream) {
+  return b200mm_qkv_w8(x, ldx, w, s, ldw, y, ldy, M, N, K, dtype, stream);
 }
 
 int b200mm_mla_append(const b200mm_mla_shape* shape, const void* c_kv, int64_t c_sb, int64_t c_st,

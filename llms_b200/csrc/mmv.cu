@@ -15,13 +15,16 @@
 //     is spliced under the fp16 exponent of 1024 by one byte-permute and
 //     1152 is subtracted from the pair; x is then staged as fp16
 //     (satfinite conversion: |x| beyond 65504 saturates);
-//   * K is split over a cluster of 4 CTAs (each owns a quarter of K for the
-//     same 128 weight rows); the partial sums meet through distributed shared
-//     memory: CTA r receives the partials of rows [32r, 32r+32) from all four
-//     and finishes them (int8 scale, SiLU * up), so there is no workspace and
-//     no atomic;
+//   * K is split over a cluster of CS = 4 or 8 CTAs (each owns 1/CS of K for
+//     the same 128 weight rows); the partial sums meet through distributed
+//     shared memory: CTA r receives the partials of rows [r*128/CS, +128/CS)
+//     from all CS ranks and finishes them (int8 scale, SiLU * up), so there
+//     is no workspace and no atomic.  CS = 8 when four-way groups would not
+//     fill the SMs (narrow outputs such as the 2560-row o / down
+//     projections);
 //   * launched with programmatic dependent launch; a warp issues its first
 //     weight loads before griddepcontrol.wait.
+#include <cstdlib>
 #include <type_traits>
 
 #include "dense.cuh"
@@ -32,7 +35,6 @@ namespace {
 
 constexpr int kWarps = 8;            // 8 x 16 = 128 weight rows per CTA
 constexpr int kThreads = 32 * kWarps;
-constexpr int kCluster = 4;          // K split
 constexpr int kRows = 16 * kWarps;   // weight rows per CTA (per matrix)
 
 struct MmvParams {
@@ -69,7 +71,7 @@ template <> struct MmaOp<__half> {
 
 // TX: activation dtype in memory; TM: MMA input dtype (== TX, or fp16 for int8
 // weights); TW: weight dtype; MT: n-tiles of 8 activation rows.
-template <typename TX, typename TM, typename TW, int MT, bool GATE>
+template <typename TX, typename TM, typename TW, int MT, bool GATE, int CS>
 __global__ void __launch_bounds__(kThreads) mmv_kernel(const MmvParams p) {
   constexpr bool W8 = sizeof(TW) == 1;
   constexpr int KC = W8 ? 64 : 32;       // K columns per warp-chunk (4 lanes x 16 bytes)
@@ -85,11 +87,12 @@ __global__ void __launch_bounds__(kThreads) mmv_kernel(const MmvParams p) {
   // bytes (16-bit weights) or 4 rows x 32 bytes (int8); rows shift by 64 / 16 bytes
   const int xpitch = p.kslice + (W8 ? 8 : 32);
   TM* xs = reinterpret_cast<TM*>(smem_raw);                                            // [MP][xpitch]
-  float* red = reinterpret_cast<float*>(smem_raw + (size_t)MP * xpitch * sizeof(TM));  // [NM][4][32][RP]
+  constexpr int RPO = kRows / CS;       // rows finished per cluster rank
+  float* red = reinterpret_cast<float*>(smem_raw + (size_t)MP * xpitch * sizeof(TM));  // [NM][CS][RPO][RP]
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t rank = cluster_rank();
-  const int group = blockIdx.x / kCluster;
+  const int group = blockIdx.x / CS;
   const int row_base = group * kRows + 16 * warp;   // this warp's 16 weight rows
   const int k_begin = (int)rank * p.kslice;
   const int k_end = min(p.K, k_begin + p.kslice);
@@ -205,35 +208,35 @@ __global__ void __launch_bounds__(kThreads) mmv_kernel(const MmvParams p) {
     }
   }
 
-  // partials -> owner CTA (cluster rank = local row / 32) through distributed shared memory
+  // partials -> owner CTA (cluster rank = local row / RPO) through distributed shared memory
   {
-    const int owner = warp >> 1;
-    const int lrow = 16 * (warp & 1) + (lane >> 2);
+    const int owner = (16 * warp) / RPO;
+    const int lrow = (16 * warp) % RPO + (lane >> 2);
 #pragma unroll
     for (int mtx = 0; mtx < NM; ++mtx)
 #pragma unroll
       for (int t = 0; t < MT; ++t)
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
-          float* dst = red + ((int64_t)(mtx * kCluster + rank) * 32 + lrow + 8 * hf) * RP + 8 * t + 2 * (lane & 3);
+          float* dst = red + ((int64_t)(mtx * CS + rank) * RPO + lrow + 8 * hf) * RP + 8 * t + 2 * (lane & 3);
           st_cluster_f2(map_to_rank(dst, (uint32_t)owner), acc[mtx][t][2 * hf], acc[mtx][t][2 * hf + 1]);
         }
   }
   cluster_sync();
 
-  // finish rows [32*rank, +32) of this group: sum the four K-slices, epilogue, store
+  // finish rows [RPO*rank, +RPO) of this group: sum the CS K-slices, epilogue, store
   {
     TX* y = static_cast<TX*>(p.y);
-    for (int i = threadIdx.x; i < 32 * p.M; i += kThreads) {
-      const int m = i / 32, lr = i % 32;
-      const int n = group * kRows + 32 * (int)rank + lr;
+    for (int i = threadIdx.x; i < RPO * p.M; i += kThreads) {
+      const int m = i / RPO, lr = i % RPO;
+      const int n = group * kRows + RPO * (int)rank + lr;
       if (n >= p.N) continue;
       float v[NM];
 #pragma unroll
       for (int mtx = 0; mtx < NM; ++mtx) {
         float s = 0.f;
 #pragma unroll
-        for (int r = 0; r < kCluster; ++r) s += red[((int64_t)(mtx * kCluster + r) * 32 + lr) * RP + m];
+        for (int r = 0; r < CS; ++r) s += red[((int64_t)(mtx * CS + r) * RPO + lr) * RP + m];
         v[mtx] = s;
       }
       float out;
@@ -252,12 +255,12 @@ __global__ void __launch_bounds__(kThreads) mmv_kernel(const MmvParams p) {
 
 size_t smem_bytes(int MT, bool gate, bool w8, int kslice) {
   const int MP = 8 * MT;
-  return (size_t)MP * (kslice + (w8 ? 8 : 32)) * 2 + (size_t)(gate ? 2 : 1) * kCluster * 32 * (MP + 2) * sizeof(float);
+  return (size_t)MP * (kslice + (w8 ? 8 : 32)) * 2 + (size_t)(gate ? 2 : 1) * kRows * (MP + 2) * sizeof(float);
 }
 
-template <typename TX, typename TM, typename TW, int MT, bool GATE>
+template <typename TX, typename TM, typename TW, int MT, bool GATE, int CS>
 int launch_mmv(const DenseArgs& a, int kslice) {
-  auto kern = mmv_kernel<TX, TM, TW, MT, GATE>;
+  auto kern = mmv_kernel<TX, TM, TW, MT, GATE, CS>;
   const size_t smem = smem_bytes(MT, GATE, sizeof(TW) == 1, kslice);
   if (smem > 220 * 1024) return B200MM_ERR_SHAPE;
   static int configured[64] = {0};
@@ -270,29 +273,41 @@ int launch_mmv(const DenseArgs& a, int kslice) {
   }
   MmvParams p{a.x, a.ldx, a.w0, a.ldw0, a.w1, a.ldw1, a.s0, a.s1, a.y, a.ldy, a.M, a.N, a.K, kslice};
   const int groups = (a.N + kRows - 1) / kRows;
-  return launch_pdl_cluster(kern, dim3(groups * kCluster), dim3(kThreads), smem, a.stream, kCluster, p) == cudaSuccess
+  return launch_pdl_cluster(kern, dim3(groups * CS), dim3(kThreads), smem, a.stream, CS, p) == cudaSuccess
              ? B200MM_OK
              : B200MM_ERR_LAUNCH;
 }
 
-template <typename TX, typename TM, typename TW, bool GATE>
+template <typename TX, typename TM, typename TW, bool GATE, int CS>
 int launch_mt(const DenseArgs& a, int kslice) {
-  if (a.M <= 8) return launch_mmv<TX, TM, TW, 1, GATE>(a, kslice);
-  if (a.M <= 16) return launch_mmv<TX, TM, TW, 2, GATE>(a, kslice);
-  if (a.M <= 32) return launch_mmv<TX, TM, TW, 4, GATE>(a, kslice);
-  return launch_mmv<TX, TM, TW, 8, GATE>(a, kslice);
+  if (a.M <= 8) return launch_mmv<TX, TM, TW, 1, GATE, CS>(a, kslice);
+  if (a.M <= 16) return launch_mmv<TX, TM, TW, 2, GATE, CS>(a, kslice);
+  if (a.M <= 32) return launch_mmv<TX, TM, TW, 4, GATE, CS>(a, kslice);
+  return launch_mmv<TX, TM, TW, 8, GATE, CS>(a, kslice);
 }
 
 template <typename TX, typename TM, typename TW>
-int launch_g(const DenseArgs& a, int kslice) {
-  return a.gate ? launch_mt<TX, TM, TW, true>(a, kslice) : launch_mt<TX, TM, TW, false>(a, kslice);
+int launch_g(const DenseArgs& a, int cs, int kslice) {
+  if (cs == 8)
+    return a.gate ? launch_mt<TX, TM, TW, true, 8>(a, kslice) : launch_mt<TX, TM, TW, false, 8>(a, kslice);
+  return a.gate ? launch_mt<TX, TM, TW, true, 4>(a, kslice) : launch_mt<TX, TM, TW, false, 4>(a, kslice);
 }
 
 inline bool al16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
+// Cluster size: eight-way K split when four-way groups leave SMs idle.
+int cluster_of(const DenseArgs& a) {
+  const int groups = (a.N + kRows - 1) / kRows;
+  int cs = groups * 4 < num_sms(current_device()) ? 8 : 4;
+#ifdef SWAP_TRACE
+  if (const char* e = getenv("B200MM_MMV_CS")) cs = atoi(e) == 8 ? 8 : 4;
+#endif
+  return cs;
+}
+
 // K columns per cluster rank: a multiple of 64 (both chunk widths divide it)
-int kslice_of(const DenseArgs& a) {
-  const int per = (a.K + kCluster - 1) / kCluster;
+int kslice_of(const DenseArgs& a, int cs) {
+  const int per = (a.K + cs - 1) / cs;
   return (per + 63) / 64 * 64;
 }
 
@@ -306,17 +321,18 @@ bool mmv_supported(const DenseArgs& a) {
   if (!al16(a.w0) || (a.ldw0 * wsz) % 16) return false;
   if (a.gate && (!al16(a.w1) || (a.ldw1 * wsz) % 16)) return false;
   const int MT = a.M <= 8 ? 1 : a.M <= 16 ? 2 : a.M <= 32 ? 4 : 8;
-  return smem_bytes(MT, a.gate, a.w8, kslice_of(a)) <= 220 * 1024;
+  return smem_bytes(MT, a.gate, a.w8, kslice_of(a, cluster_of(a))) <= 220 * 1024;
 }
 
 int mmv_launch(const DenseArgs& a) {
-  const int ks = kslice_of(a);
+  const int cs = cluster_of(a);
+  const int ks = kslice_of(a, cs);
   if (a.w8) {
-    if (a.dtype == B200MM_BF16) return launch_g<__nv_bfloat16, __half, int8_t>(a, ks);
-    return launch_g<__half, __half, int8_t>(a, ks);
+    if (a.dtype == B200MM_BF16) return launch_g<__nv_bfloat16, __half, int8_t>(a, cs, ks);
+    return launch_g<__half, __half, int8_t>(a, cs, ks);
   }
-  if (a.dtype == B200MM_BF16) return launch_g<__nv_bfloat16, __nv_bfloat16, __nv_bfloat16>(a, ks);
-  return launch_g<__half, __half, __half>(a, ks);
+  if (a.dtype == B200MM_BF16) return launch_g<__nv_bfloat16, __nv_bfloat16, __nv_bfloat16>(a, cs, ks);
+  return launch_g<__half, __half, __half>(a, cs, ks);
 }
 
 }  // namespace b200mm

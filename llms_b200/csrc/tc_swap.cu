@@ -7,9 +7,11 @@
 // Decode and small-batch calls have few activation rows, so they go on the
 // MMA's N side (N = 16..64; int8 weights up to 256 per tile, any M) and the
 // weight rows fill the accumulator lanes.
-// One CTA owns 64 weight rows (MMA M = 64: an M = 64 instruction costs what an
-// M = 128 one does, and the smaller tile doubles the number of CTAs streaming
-// weights) and an N-tile of activation rows.
+// One CTA owns 128 weight rows (16-bit weights) or 64 (int8) and an N-tile of
+// activation rows.  The tensor core takes about 85 ns per small-N instruction
+// (measured, N = 16..64, whether one thread or four issue them), so at M = 64
+// it, not HBM, set the pace: 128-row tiles move twice the weight bytes per
+// instruction, and the K split below restores the CTA count.
 //
 // The kernel is a weight stream, so its speed is the bytes it keeps in flight:
 // at full load HBM answers in about 3 us, and 6 TB/s needs ~190 KB in flight
@@ -39,7 +41,6 @@ namespace b200mm {
 
 namespace {
 
-constexpr int FM = 64;     // weight rows per CTA = MMA M
 constexpr int BK = 64;     // K per chunk (128 bytes of 16-bit elements)
 constexpr int kThr = 192;  // warps: 0 TMA, 1 MMA issuer + TMEM owner, 2-5 converters + epilogue
 constexpr int kMaxNS = 16;  // ring stages (barrier arrays)
@@ -47,8 +48,13 @@ constexpr uint32_t kBudget1 = 200 * 1024, kBudget2 = 100 * 1024;  // ring bytes:
 
 template <int MN, bool GATE, bool W8>
 struct SwapCfg {
+  // weight rows per CTA = MMA M: 128 for 16-bit weights (a small-N MMA costs
+  // about the same at M = 64 and M = 128, and the tensor core, not HBM, set
+  // the pace of the M = 64 tiles); 64 for int8, whose converter hand-off is
+  // the limit and whose fp16 operand ring would not fit beside 128-row tiles
+  static constexpr int FM = W8 ? 64 : 128;
   static constexpr int NW = GATE ? 2 : 1;
-  static constexpr uint32_t W16 = FM * BK * 2;  // 16-bit weight chunk: 8 KB
+  static constexpr uint32_t W16 = FM * BK * 2;  // 16-bit weight chunk
   static constexpr uint32_t WB = W8 ? FM * BK : W16;  // staged weight chunk
   static constexpr uint32_t XB = MN * BK * 2;   // activation chunk
   static constexpr uint32_t CHUNK = NW * WB + XB;  // staged bytes per K-chunk
@@ -107,6 +113,7 @@ __global__ void __launch_bounds__(kThr, 2)
                    const __grid_constant__ CUtensorMap mw1, const SwapParams p) {
   using C = SwapCfg<MN, GATE, W8>;
   using TM = typename std::conditional<W8, __half, T>::type;  // MMA operand type
+  constexpr int FM = C::FM;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                        ~uintptr_t(1023));
@@ -322,14 +329,17 @@ __global__ void __launch_bounds__(kThr, 2)
   __syncthreads();
   bad = bad || *failed;
   const int q = warp & 3;
-  const int fl = 16 * q + lane;  // this lane's weight row in the M = 64 accumulator (lanes 0-15)
+  // this lane's weight row: M = 128 accumulators use every TMEM lane, M = 64
+  // ones lanes 0-15 of each 32-lane quadrant
+  constexpr bool kAllLanes = FM == 128;
+  const int fl = kAllLanes ? 32 * q + lane : 16 * q + lane;
   const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16);
   constexpr int CW = C::ACC >= 32 ? 32 : 16;  // columns per TMEM load
   float* red = reinterpret_cast<float*>(sm);  // the ring is idle now: rank 0 collects partials here
   if (p.cs > 1) {
     cluster_sync();  // every rank's ring is idle
     if (rank != 0 && epi) {
-      // the loads are warp-collective; lanes 16-31 hold nothing and store nothing
+      // the loads are warp-collective; at M = 64 lanes 16-31 hold nothing and store nothing
       float* dst = red + ((int64_t)(rank - 1) * FM + fl) * C::RP;
 #pragma unroll 1
       for (int c = 0; c < C::ACC; c += CW) {
@@ -341,7 +351,7 @@ __global__ void __launch_bounds__(kThr, 2)
 #pragma unroll
           for (int e = 0; e < CW; ++e) v[e] += v1[e];
         }
-        if (lane < 16) {
+        if (kAllLanes || lane < 16) {
 #pragma unroll
           for (int e = 0; e < CW; e += 4)
             st_cluster_f4(map_to_rank(dst + c + e, 0), v[e], v[e + 1], v[e + 2], v[e + 3]);
@@ -357,7 +367,7 @@ __global__ void __launch_bounds__(kThr, 2)
   if (rank == 0 && epi) {
     bad = bad || *reinterpret_cast<volatile int*>(peer_failed);
     const int f = f0 + fl;
-    const bool live = lane < 16 && f < p.N;
+    const bool live = (kAllLanes || lane < 16) && f < p.N;
     const float sc0 = (live && p.s0) ? p.s0[f] : 1.f;
     const float sc1 = (live && GATE && p.s1) ? p.s1[f] : 1.f;
     T* ycol = static_cast<T*>(p.y) + f;
@@ -473,6 +483,7 @@ bool operand_map(CUtensorMap* m, CUtensorMapDataType dt, uint32_t esz, const voi
 template <typename T, int MN, bool GATE, bool W8>
 int launch_cfg(const DenseArgs& a) {
   using C = SwapCfg<MN, GATE, W8>;
+  constexpr int FM = C::FM;
   const int kchunks = (a.K + BK - 1) / BK;
   const bool map3d = a.K % BK == 0;
   const int tf = (a.N + FM - 1) / FM, tm = (a.M + MN - 1) / MN;
@@ -483,6 +494,9 @@ int launch_cfg(const DenseArgs& a) {
   // ring: one CTA per SM when the tiles fit in one wave that way, else two;
   // two K-chunks per stage when that still leaves three stages
   int budget_idx = base <= sms ? 0 : 1;
+#ifdef SWAP_TRACE
+  if (const char* e = getenv("B200MM_SWAP_BUDGET")) budget_idx = atoi(e) ? 1 : 0;
+#endif
   if (budget_idx == 1 && kBudget2 < C::OPS * C::OPST + 2 * C::CHUNK) budget_idx = 0;  // big int8 tiles
   const uint32_t budget = (budget_idx == 0 ? kBudget1 : kBudget2) - C::OPS * C::OPST;
   // K-chunks per stage: as many as leave three stages (a stage costs one
@@ -528,8 +542,11 @@ int launch_cfg(const DenseArgs& a) {
   // K split over a cluster while every tile's cluster is resident at once,
   // each rank keeps two stages or more, and rank 0's ring holds the partials
   const long slots = (long)sms * (budget_idx == 0 ? 1 : 2);
-  int cs = 1;
-  for (int c = 2; c <= 8 && c <= nstages / 2 && base * c <= slots && (uint32_t)(c - 1) * C::RED <= ns * stage;
+  int cs = 1, cs_cap = 8;
+#ifdef SWAP_TRACE
+  if (const char* e = getenv("B200MM_SWAP_CS")) cs_cap = atoi(e);
+#endif
+  for (int c = 2; c <= cs_cap && c <= nstages / 2 && base * c <= slots && (uint32_t)(c - 1) * C::RED <= ns * stage;
        ++c) {
     if (base > max_clusters(kern, c, smem, budget_idx)) break;
     cs = c;
@@ -557,11 +574,8 @@ int launch_mn(const DenseArgs& a) {
   if (a.M <= 16) return launch_cfg<T, 16, GATE, W8>(a);
   if (a.M <= 32) return launch_cfg<T, 32, GATE, W8>(a);
   if (a.M <= 64) return launch_cfg<T, 64, GATE, W8>(a);
-  if constexpr (W8) {  // 16-bit weights beyond M = 64 go to the GEMM tiled over X
-    if (a.M <= 128) return launch_cfg<T, 128, GATE, W8>(a);
-    return launch_cfg<T, 256, GATE, W8>(a);
-  }
-  return B200MM_ERR_SHAPE;
+  if (a.M <= 128) return launch_cfg<T, 128, GATE, W8>(a);
+  return launch_cfg<T, 256, GATE, W8>(a);
 }
 
 template <typename T>
@@ -583,7 +597,7 @@ extern "C" int b200mm_debug_trace(void* host, size_t bytes) {
 
 bool swap_supported(const DenseArgs& a) {
   if (a.dtype != B200MM_BF16 && a.dtype != B200MM_F16) return false;
-  if (a.M < 5 || (!a.w8 && a.M > 64)) return false;
+  if (a.M < 5) return false;
   const int wsz = a.w8 ? 1 : 2;
   if (!al16(a.x) || !al16(a.w0) || (a.gate && !al16(a.w1))) return false;
   if ((a.ldx * 2) % 16 || (a.ldw0 * wsz) % 16 || (a.gate && (a.ldw1 * wsz) % 16)) return false;

@@ -13,6 +13,7 @@ from torch import nn
 
 from .fused_ffn import TritonFFN
 from .fused_qkv import TritonAttention, triton_fused_qkv
+from .linear import B200Linear, Int8Linear
 from .quant import Int8Attention, Int8FFN, int8_fused_qkv
 
 
@@ -37,6 +38,21 @@ def apply_int8_kernels(model: nn.Module, *, ffn: bool = True, qkv: bool = True) 
             hasattr(block.attn, "v") or hasattr(block.attn, "W_qkv")
         ):
             block.attn = Int8Attention.from_eager(block.attn)
+    return model
+
+
+def apply_linear_kernels(model: nn.Module, *, int8: bool = False, o: bool = True, down: bool = True) -> nn.Module:
+    """Route each layer's attention output projection ``attn.o`` and FFN
+    ``ffn.down`` through the B200 projection kernels (:class:`B200Linear`,
+    sharing the weight; or :class:`Int8Linear` with ``int8=True``).  Works on
+    the engine modules and on the fused-kernel modules alike, since both call
+    ``self.o(...)`` / ``self.down(...)``.  Idempotent; returns ``model``."""
+    cls = Int8Linear if int8 else B200Linear
+    for block in model.layers:
+        if o and isinstance(block.attn.o, nn.Linear):
+            block.attn.o = cls.from_linear(block.attn.o)
+        if down and isinstance(block.ffn.down, nn.Linear):
+            block.ffn.down = cls.from_linear(block.ffn.down)
     return model
 
 

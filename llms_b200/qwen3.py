@@ -41,6 +41,7 @@ class Qwen3Shape:
 
 
 QWEN3_8B = Qwen3Shape()
+QWEN3_4B = Qwen3Shape(hidden_size=2560, intermediate_size=9728)
 
 
 class RMSNorm(nn.Module):

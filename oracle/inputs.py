@@ -52,6 +52,16 @@ def cfg3(M: int, seed: int = 2, K: int = 2560, N: int = 9728):
     return x, w[:N], w[N:]
 
 
+def o_down(M: int, which: str, seed: int = 6, hidden: int = 2560, n_q: int = 4096, inter: int = 9728):
+    """Qwen3-4B output projection (``which="o"``: W [hidden, n_q]) or down
+    projection (``"down"``: W [hidden, inter]), bf16 -> (x, W)."""
+    K = n_q if which == "o" else inter
+    rng = np.random.default_rng(seed + (0 if which == "o" else 1))
+    x = round_bf16(_normal(rng, (M, K)))
+    w = round_bf16(_normal(rng, (hidden, K), 0.02))
+    return x, w
+
+
 def cfg4(B: int, L: int, seed: int = 3, H=32, KV=8, D=128, DR=32, R=256):
     """MLA latent decode, bf16: c_kv [B,L,R], kr [B,L,KV,DR], W_UK [KV,D-DR,R],
     W_UV [KV,D,R] (std 1/4, i.e. variance 1/16), q [B,H,D]; k_norm weight ones."""

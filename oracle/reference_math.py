@@ -30,6 +30,13 @@ def qkv(x: np.ndarray, w_qkv: np.ndarray, n_q: int, n_k: int):
     return y[..., :n_q], y[..., n_q:n_q + n_k], y[..., n_q + n_k:]
 
 
+def linear(x: np.ndarray, w: np.ndarray) -> np.ndarray:
+    """Bias-free ``nn.Linear``: the attention output projection
+    ``self.o(attn)`` (engine/attention.py:163) and the FFN down projection
+    ``self.down(...)`` (engine/model.py:37).  x: (..., K); W: (N, K)."""
+    return np.asarray(x, np.float64) @ np.asarray(w, np.float64).T
+
+
 def dequant(q: np.ndarray, s: np.ndarray) -> np.ndarray:
     """int8 weight-only storage: W[n, k] = q[n, k] * s[n] (new path; the
     oracle is dequantise-then-reference)."""

@@ -28,7 +28,7 @@ def test_library_exports_header_symbols():
 
 def test_status_strings_and_version():
     from llms_b200 import _capi
-    assert _capi.lib.b200mm_abi_version() == 1
+    assert _capi.lib.b200mm_abi_version() == 2
     assert _capi.lib.b200mm_status_string(0) == b"ok"
     for code in range(1, 9):
         assert _capi.lib.b200mm_status_string(code) not in (b"ok", b"unknown status")

@@ -31,6 +31,40 @@ def test_apply_triton_kernels_swaps_and_is_idempotent():
     assert all(a is b.ffn for a, b in zip(first, m.layers))
 
 
+def test_apply_linear_kernels_swaps_o_and_down():
+    from llms_b200.kernels import (B200Linear, Int8Linear, apply_linear_kernels, apply_triton_kernels,
+                                   dequantize_per_row)
+    m = tiny()
+    o0, d0 = m.layers[0].attn.o.weight, m.layers[1].ffn.down.weight
+    apply_triton_kernels(m)
+    apply_linear_kernels(m)
+    assert all(isinstance(b.attn.o, B200Linear) and isinstance(b.ffn.down, B200Linear) for b in m.layers)
+    assert m.layers[0].attn.o.weight is o0 and m.layers[1].ffn.down.weight is d0
+    first = [b.attn.o for b in m.layers]
+    apply_linear_kernels(m)  # idempotent
+    assert all(a is b.attn.o for a, b in zip(first, m.layers))
+    sd = m.state_dict()
+    assert "layers.0.attn.o.weight" in sd and "layers.1.ffn.down.weight" in sd
+
+    m8 = tiny()
+    d = m8.layers[0].ffn.down.weight.detach().clone()
+    apply_linear_kernels(m8, int8=True, o=False)
+    assert isinstance(m8.layers[0].ffn.down, Int8Linear) and isinstance(m8.layers[0].attn.o, torch.nn.Linear)
+    lin = m8.layers[0].ffn.down
+    assert lin.qweight.dtype == torch.int8 and lin.scale.shape == (d.shape[0],)
+    err = (dequantize_per_row(lin.qweight, lin.scale) - d).abs()
+    assert (err <= lin.scale[:, None] / 2 + 1e-7).all()
+
+
+def test_linear_module_rejects_bias():
+    import pytest
+    from llms_b200.kernels import B200Linear, Int8Linear
+    with pytest.raises(ValueError):
+        B200Linear.from_linear(torch.nn.Linear(4, 4, bias=True))
+    with pytest.raises(ValueError):
+        Int8Linear.from_linear(torch.nn.Linear(4, 4, bias=True))
+
+
 def test_apply_triton_kernels_flags():
     from llms_b200.kernels import TritonAttention, TritonFFN, apply_triton_kernels
     m = tiny()
