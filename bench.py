@@ -480,6 +480,40 @@ def suite(job):
                                  "bytes_note": "512*B*L latent + 512*B*L RoPE'd-key side-band + 32*B*L k-RMS "
                                                "side-band + weights + q/out"}
         del g, c, kz, ks, ws
+    # MLA decode step, fused "Q + latent" projection: q [4096], latent c_kv
+    # [256] and pre-RoPE key [256] rows of one [4608, 2560] weight in one
+    # b200mm_linear launch, against the reference's three Linears (cuBLAS);
+    # 8 layers' weights rotate so they never sit in L2
+    gq = torch.Generator(device="cuda").manual_seed(7)
+    wparts = [[torch.randn(n, HIDDEN, device="cuda", dtype=torch.bfloat16, generator=gq) * 0.02
+               for n in (NQ, 256, 256)] for _ in range(8)]
+    wcat = [torch.cat(w) for w in wparts]
+    for B in (1, 32):
+        x = torch.randn(B, HIDDEN, device="cuda", dtype=torch.bfloat16)
+        y = torch.empty(B, NQ + 512, device="cuda", dtype=torch.bfloat16)
+        ys = [torch.empty(B, n, device="cuda", dtype=torch.bfloat16) for n in (NQ, 256, 256)]
+
+        def fused(x=x, y=y, B=B):
+            s = torch.cuda.current_stream().cuda_stream
+            for w in wcat:
+                _capi.check(_capi.lib.b200mm_linear(x.data_ptr(), HIDDEN, w.data_ptr(), HIDDEN, y.data_ptr(),
+                                                    NQ + 512, B, NQ + 512, HIDDEN, 2, s), "b200mm_linear")
+
+        def three_cublas(x=x, ys=ys):
+            for ws in wparts:
+                for w, yy in zip(ws, ys):
+                    torch.matmul(x, w.t(), out=yy)
+
+        res = {}
+        for tag, fn in (("", fused), ("three_linear_cublas_", three_cublas)):
+            g, _ = job.capture(fn)
+            sec = time_graph(g, 20, 2, 1)
+            res[tag + "us_per_layer"] = sec / (20 * len(wcat)) * 1e6
+            del g
+        res["GB/s"] = op_bytes(NQ + 512, HIDDEN, B, NQ + 512) / (res["us_per_layer"] * 1e-6) / 1e9
+        out[f"mla_q_latent_proj_b{B}"] = res
+        del x, y, ys
+    del wparts, wcat
     torch.cuda.empty_cache()
     out.update(qwen3_8b_int8_decode())
     return out

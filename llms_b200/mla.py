@@ -37,6 +37,7 @@ from torch import nn
 
 from . import _capi
 from .kernels._eager import rotate_half
+from .kernels.linear import b200_linear
 
 
 def rope_inv_freq(head_dim: int, d_rope: int, theta: float, device=None) -> torch.Tensor:
@@ -265,6 +266,36 @@ class B200MLAttention(nn.Module):
             self._b200_consts = cache
         return cache[1], cache[2]
 
+    def _q_latent_weight(self, x: torch.Tensor) -> torch.Tensor | None:
+        """``[q; dkv; kr]`` row-stacked in one buffer (the fused "Q + latent"
+        projection of the decode step, replacing the three Linears at
+        engine/mla.py:195-205).  Built once: the three weights are rebound as
+        views of the buffer, so no weight is stored twice and state dicts
+        keep their keys.  Rebuilt if a weight was replaced since (``.to()``,
+        a new Parameter); None when the weights cannot serve ``x``."""
+        lins = [self.q, self.dkv] + ([self.kr] if self.kr is not None else [])
+        if any(lin.bias is not None or lin.weight.dtype != x.dtype or lin.weight.device != x.device
+               for lin in lins):
+            return None
+        W = getattr(self, "_b200_qlat", None)
+        if W is not None and W.dtype == x.dtype and W.device == x.device:
+            off, ok = 0, True
+            for lin in lins:
+                w = lin.weight
+                ok = ok and w.data_ptr() == W[off:].data_ptr() and w.shape[0] + off <= W.shape[0] and w.is_contiguous()
+                off += w.shape[0]
+            if ok and off == W.shape[0]:
+                return W
+        with torch.no_grad():
+            W = torch.cat([lin.weight.detach() for lin in lins], 0).contiguous()
+            off = 0
+            for lin in lins:
+                n = lin.weight.shape[0]
+                lin.weight = nn.Parameter(W[off:off + n], requires_grad=lin.weight.requires_grad)
+                off += n
+        self._b200_qlat = W
+        return W
+
     def supports_fast_decode(self, x: torch.Tensor) -> bool:
         return x.is_cuda and x.shape[1] == 1 and x.dtype in _capi.DTYPE_CODES
 
@@ -285,8 +316,17 @@ class B200MLAttention(nn.Module):
         B = x.shape[0]
         H, KV, D, DR, DN = self.num_heads, self.num_kv_heads, self.head_dim, self.d_rope, self.d_nope
         end = start_pos + 1
-        q = self.q_norm(self.q(x).view(B, 1, H, D))
-        self._write_cache(x, kv_cache, layer_idx, start_pos, end)
+        W = self._q_latent_weight(x)
+        if W is not None:  # one launch for q, the latent c_kv and the pre-RoPE key
+            y = b200_linear(x, W)
+            q, c_new, k_new = y.split([H * D, self.rank, KV * DR], dim=-1)
+            kv_cache.c_kv[layer_idx][:B, start_pos:end, :] = c_new
+            if DR > 0:
+                kv_cache.k_rope_pre[layer_idx][:B, start_pos:end] = k_new.view(B, 1, KV, DR)
+            q = self.q_norm(q.reshape(B, 1, H, D))
+        else:
+            q = self.q_norm(self.q(x).view(B, 1, H, D))
+            self._write_cache(x, kv_cache, layer_idx, start_pos, end)
         c = kv_cache.c_kv[layer_idx]
         kr = kv_cache.k_rope_pre[layer_idx] if DR > 0 else None
         w_uk = self.uk_nope.weight.view(KV, DN, self.rank) if DN > 0 else None

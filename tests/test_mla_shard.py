@@ -1,6 +1,7 @@
 """MLA decode across GPUs: batch-row shards with no collective in the op
 (`llms_b200.mla.batch_shard`), outputs gathered afterwards -- checked on CPU
-with two gloo ranks against the unsharded oracle."""
+with two gloo ranks against the unsharded oracle -- and the host side of the
+decode step's fused Q + latent projection weight."""
 
 import multiprocessing as mp
 import os
@@ -60,3 +61,28 @@ def test_batch_sharded_decode_gathers_to_full_output_gloo():
         p.join(timeout=60)
         assert p.exitcode == 0
     assert err < 1e-9
+
+
+def test_q_latent_weight_is_one_buffer_of_views():
+    """The decode step's fused Q + latent projection: q, dkv and kr weights
+    become row views of one stacked buffer (no second copy), state dicts keep
+    their keys, and the buffer follows in-place loads."""
+    import torch
+    from llms_b200.mla import B200MLAttention
+    torch.manual_seed(0)
+    m = B200MLAttention(hidden_size=64, num_heads=4, num_kv_heads=2, head_dim=16, rms_eps=1e-6, rank=32,
+                        d_rope=8, max_position_embeddings=16, rope_theta=1e4)
+    x = torch.zeros(1, 1, 64)
+    ref = torch.cat([m.q.weight, m.dkv.weight, m.kr.weight]).detach().clone()
+    W = m._q_latent_weight(x)
+    assert W.shape == (64 + 32 + 16, 64) and torch.equal(W, ref)
+    assert m.q.weight.data_ptr() == W.data_ptr()
+    assert m.dkv.weight.data_ptr() == W[64:].data_ptr() and m.kr.weight.data_ptr() == W[96:].data_ptr()
+    assert m._q_latent_weight(x) is W
+    sd = {k: torch.randn_like(v) for k, v in m.state_dict().items()}
+    m.load_state_dict(sd)
+    assert torch.equal(W[:64], sd["q.weight"]) and torch.equal(W[96:], sd["kr.weight"])
+    m.double()  # replaces the parameters' storage: rebuilt for float64 inputs
+    assert m._q_latent_weight(x) is None
+    W2 = m._q_latent_weight(x.double())
+    assert W2.dtype == torch.float64 and m.dkv.weight.data_ptr() == W2[64:].data_ptr()
