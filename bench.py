@@ -480,6 +480,33 @@ def suite(job):
                                  "bytes_note": "512*B*L latent + 512*B*L RoPE'd-key side-band + 32*B*L k-RMS "
                                                "side-band + weights + q/out"}
         del g, c, kz, ks, ws
+    # GQA decode attention (the engine's decode_attn_op seam) at Qwen3 shapes:
+    # GB/s of the K/V cache read once per step, against the reference's own
+    # single-query path (repeat_interleave + SDPA) and torch's GQA SDPA
+    import torch.nn.functional as F
+    from llms_b200.kernels import b200_decode_attn
+    for B, L in ((32, 32768), (1, 32768)):
+        gg = torch.Generator(device="cuda").manual_seed(8)
+        q = torch.randn(B, 32, 1, HEAD, device="cuda", generator=gg).bfloat16()
+        kc = torch.randn(B, 8, L, HEAD, device="cuda", generator=gg).bfloat16()
+        vc = torch.randn(B, 8, L, HEAD, device="cuda", generator=gg).bfloat16()
+        res = {}
+        for tag, fn, reps in (
+                ("", lambda: b200_decode_attn(q, kc, vc, scale=HEAD ** -0.5), 10),
+                ("reference_repeat_sdpa_", lambda: F.scaled_dot_product_attention(
+                    q, kc.repeat_interleave(4, 1), vc.repeat_interleave(4, 1)), 2),
+                ("torch_sdpa_gqa_", lambda: F.scaled_dot_product_attention(q, kc, vc, enable_gqa=True), 10)):
+            g, launches = job.capture(fn)
+            sec = time_graph(g, reps, 2, 1)
+            res[tag + "us_per_step"] = sec / reps * 1e6
+            if not tag:
+                res["launches"] = launches
+            del g
+        alg = 2 * B * 8 * L * HEAD * 2 + 4 * B * 32 * HEAD
+        res["GB/s"] = alg / (res["us_per_step"] * 1e-6) / 1e9
+        out[f"gqa_decode_b{B}_l{L}"] = res
+        del q, kc, vc
+        torch.cuda.empty_cache()
     # MLA decode step, fused "Q + latent" projection: q [4096], latent c_kv
     # [256] and pre-RoPE key [256] rows of one [4608, 2560] weight in one
     # b200mm_linear launch, against the reference's three Linears (cuBLAS);

@@ -152,6 +152,36 @@ int b200mm_linear_w8(const void* x, int64_t ldx,
                      int dtype, void* stream);
 
 /*
+ * GQA single-query decode attention over the engine's KV cache:
+ *   out[b, h, :] = softmax_t(q[b, h, :] . k[b, h / g, t, :] * scale) v[b, h / g, t, :]
+ * for t < L, g = H / KV.  This is what the engine's swappable decode op
+ * computes (`Attention.decode_attn_op`, src/engine/attention.py:101-105 and
+ * :138-145, which hands it the pre-expansion K/V views), and what its default
+ * path (repeat_interleave + scaled_dot_product_attention,
+ * src/engine/attention.py:147-150) computes for T == 1.
+ *   q   : [B, H, D]  strides (q_sb, q_sh, 1)          `dtype`
+ *   k, v: [B, KV, L, D] strides (sb, sh, st, 1)         `dtype`
+ *   out : [B, H, D]  strides (o_sb, o_sh, 1)          `dtype`
+ * Strides are in elements.  fp32 softmax and accumulation; one rounding on
+ * store.  16-bit caches with D = 64 or 128, g <= 16 and contiguous token
+ * rows (st == D) take the split-context kernel; everything else a generic
+ * kernel.
+ *   workspace: >= b200mm_gqa_decode_workspace_size(B, H, KV, D, L) bytes,
+ *              256-byte aligned, owned by the stream until the call completes,
+ *              ZERO-FILLED before its first use; every call leaves the few
+ *              words it needs zeroed for the next call (no per-call memset).
+ */
+size_t b200mm_gqa_decode_workspace_size(int64_t B, int64_t H, int64_t KV, int64_t D, int64_t L);
+
+int b200mm_gqa_decode(const void* q, int64_t q_sb, int64_t q_sh,
+                      const void* k, int64_t k_sb, int64_t k_sh, int64_t k_st,
+                      const void* v, int64_t v_sb, int64_t v_sh, int64_t v_st,
+                      void* out, int64_t o_sb, int64_t o_sh,
+                      int64_t B, int64_t H, int64_t KV, int64_t D, int64_t L,
+                      float scale, int dtype,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * MLA latent-cache shapes shared by the two MLA entry points.
  *   B      batch rows served by this call (rows 0..B-1 of the cache)
  *   H      query heads, KV key/value groups (H % KV == 0)

@@ -67,6 +67,12 @@ SIGNATURES: dict[str, tuple] = {
         ctypes.c_int,
         [_c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int, _c_p],
     ),
+    "b200mm_gqa_decode_workspace_size": (ctypes.c_size_t, [_c_i64] * 5),
+    "b200mm_gqa_decode": (
+        ctypes.c_int,
+        [_c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_i64,
+         _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_float, ctypes.c_int, _c_p, ctypes.c_size_t, _c_p],
+    ),
     "b200mm_mla_append": (
         ctypes.c_int,
         [ctypes.POINTER(MlaShape), _c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_p,

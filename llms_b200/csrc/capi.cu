@@ -182,6 +182,39 @@ int b200mm_linear_w8(const void* x, int64_t ldx, const int8_t* w, const float* s
   return b200mm_qkv_w8(x, ldx, w, s, ldw, y, ldy, M, N, K, dtype, stream);
 }
 
+namespace {
+bool gqa_shape_ok(int64_t B, int64_t H, int64_t KV, int64_t D, int64_t L) {
+  return B >= 0 && B <= 65535 && KV >= 1 && H >= KV && H <= 65535 && H % KV == 0 && D >= 2 && D <= 1024 &&
+         D % 2 == 0 && L >= 1 && L < (int64_t(1) << 31);
+}
+}  // namespace
+
+size_t b200mm_gqa_decode_workspace_size(int64_t B, int64_t H, int64_t KV, int64_t D, int64_t L) {
+  if (!gqa_shape_ok(B, H, KV, D, L)) return 0;
+  return gqa_workspace_bytes((int)(B > 0 ? B : 1), (int)H, (int)KV, (int)D, L);
+}
+
+int b200mm_gqa_decode(const void* q, int64_t q_sb, int64_t q_sh, const void* k, int64_t k_sb, int64_t k_sh,
+                      int64_t k_st, const void* v, int64_t v_sb, int64_t v_sh, int64_t v_st, void* out,
+                      int64_t o_sb, int64_t o_sh, int64_t B, int64_t H, int64_t KV, int64_t D, int64_t L,
+                      float scale, int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  if (dtype != B200MM_F32 && dtype != B200MM_F16 && dtype != B200MM_BF16) return B200MM_ERR_DTYPE;
+  if (!gqa_shape_ok(B, H, KV, D, L)) return B200MM_ERR_SHAPE;
+  if (!q || !k || !v || !out || !(scale > 0.f)) return B200MM_ERR_ARG;
+  if (q_sb < 0 || q_sh < 0 || k_sb < 0 || k_sh < 0 || k_st < D || v_sb < 0 || v_sh < 0 || v_st < D || o_sb < 0 ||
+      o_sh < 0)
+    return B200MM_ERR_SHAPE;
+  if (B == 0) return B200MM_OK;
+  const size_t need = gqa_workspace_bytes((int)B, (int)H, (int)KV, (int)D, L);
+  if (!workspace || workspace_bytes < need || ((uintptr_t)workspace & 255u)) return B200MM_ERR_WORKSPACE;
+  int st = check_device();
+  if (st != B200MM_OK) return st;
+  st = gqa_decode(q, q_sb, q_sh, k, k_sb, k_sh, k_st, v, v_sb, v_sh, v_st, out, o_sb, o_sh, (int)B, (int)H,
+                  (int)KV, (int)D, L, scale, dtype, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+  if (st != B200MM_OK) return st;
+  return launch_status();
+}
+
 int b200mm_mla_append(const b200mm_mla_shape* shape, const void* c_kv, int64_t c_sb, int64_t c_st,
                       const void* k_rope_pre, int64_t r_sb, int64_t r_st, const void* w_uk, const float* k_norm_w,
                       const float* rope_inv_freq, float* kscale, int64_t s_sb, int64_t s_st, void* kz,

@@ -35,4 +35,11 @@ int swap_launch(const DenseArgs& a);
 bool tc_supported(const DenseArgs& a);
 int tc_launch(const DenseArgs& a);
 
+// GQA single-query decode attention (gqa.cu); shapes validated by the caller.
+size_t gqa_workspace_bytes(int B, int H, int KV, int D, int64_t L);
+int gqa_decode(const void* q, int64_t q_sb, int64_t q_sh, const void* k, int64_t k_sb, int64_t k_sh, int64_t k_st,
+               const void* v, int64_t v_sb, int64_t v_sh, int64_t v_st, void* out, int64_t o_sb, int64_t o_sh,
+               int B, int H, int KV, int D, int64_t L, float scale, int dtype, void* ws, size_t ws_bytes,
+               cudaStream_t stream);
+
 }  // namespace b200mm

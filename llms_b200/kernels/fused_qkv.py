@@ -109,6 +109,8 @@ class TritonAttention(nn.Module):
         self.o = nn.Linear(num_heads * head_dim, hidden_size, bias=False)
         self.q_norm = _RMSNorm(head_dim, eps=rms_eps)
         self.k_norm = _RMSNorm(head_dim, eps=rms_eps)
+        # the engine Attention's swappable single-query op (engine/attention.py:101-105)
+        self.decode_attn_op = None
 
     @classmethod
     def from_eager(cls, eager: nn.Module) -> "TritonAttention":
@@ -127,6 +129,7 @@ class TritonAttention(nn.Module):
         out.o = eager.o
         out.q_norm = eager.q_norm
         out.k_norm = eager.k_norm
+        out.decode_attn_op = getattr(eager, "decode_attn_op", None)
         return out
 
     def project_qkv(self, x: torch.Tensor):
@@ -146,6 +149,10 @@ class TritonAttention(nn.Module):
         kv_cache.v[layer_idx][:B, :, start_pos:end, :] = v
         full_k = kv_cache.k[layer_idx][:B, :, :end, :]
         full_v = kv_cache.v[layer_idx][:B, :, :end, :]
+        op = getattr(self, "decode_attn_op", None)
+        if T == 1 and op is not None:  # the engine's decode seam (engine/attention.py:138-145)
+            attn = op(q, full_k, full_v, scale=self.head_dim ** -0.5, layer_idx=layer_idx)
+            return self.o(attn.transpose(1, 2).reshape(B, T, self.num_heads * self.head_dim))
         rep = self.num_heads // self.num_kv_heads
         if rep > 1:
             full_k = full_k.repeat_interleave(rep, dim=1)

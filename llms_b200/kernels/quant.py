@@ -158,6 +158,7 @@ class Int8Attention(TritonAttention):
         out.o = eager.o
         out.q_norm = eager.q_norm
         out.k_norm = eager.k_norm
+        out.decode_attn_op = getattr(eager, "decode_attn_op", None)
         return out
 
     def project_qkv(self, x: torch.Tensor):

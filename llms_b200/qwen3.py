@@ -81,14 +81,17 @@ def rope_tables(head_dim: int, max_pos: int, theta: float, device=None):
     return emb.cos().to(device), emb.sin().to(device)
 
 
-def attention_core(q, k, v, kv_cache, layer_idx, start_pos, n_rep):
-    """Cache write + GQA SDPA of engine/attention.py:122-149 (q, k, v: B, H, T, D)."""
+def attention_core(q, k, v, kv_cache, layer_idx, start_pos, n_rep, decode_op=None):
+    """Cache write + GQA SDPA of engine/attention.py:122-149 (q, k, v: B, H, T, D);
+    a single-query step goes to ``decode_op`` when one is set (:138-145)."""
     B, _, T, _ = q.shape
     end = start_pos + T
     kv_cache.k[layer_idx][:B, :, start_pos:end] = k
     kv_cache.v[layer_idx][:B, :, start_pos:end] = v
     fk = kv_cache.k[layer_idx][:B, :, :end]
     fv = kv_cache.v[layer_idx][:B, :, :end]
+    if T == 1 and decode_op is not None:
+        return decode_op(q, fk, fv, scale=q.shape[-1] ** -0.5, layer_idx=layer_idx)
     if n_rep > 1:
         fk = fk.repeat_interleave(n_rep, dim=1)
         fv = fv.repeat_interleave(n_rep, dim=1)
@@ -112,6 +115,7 @@ class Attention(nn.Module):
         self.o = nn.Linear(H * D, C, bias=False)
         self.q_norm = RMSNorm(D, shape.rms_norm_eps)
         self.k_norm = RMSNorm(D, shape.rms_norm_eps)
+        self.decode_attn_op = None  # engine/attention.py:101-105
 
     def forward(self, x, *, kv_cache, layer_idx, cos, sin, start_pos):
         B, T, _ = x.shape
@@ -119,7 +123,8 @@ class Attention(nn.Module):
         k = self.k_norm(self.k(x).view(B, T, self.num_kv_heads, self.head_dim)).transpose(1, 2)
         v = self.v(x).view(B, T, self.num_kv_heads, self.head_dim).transpose(1, 2)
         q, k = rope(q, cos, sin), rope(k, cos, sin)
-        a = attention_core(q, k, v, kv_cache, layer_idx, start_pos, self.num_heads // self.num_kv_heads)
+        a = attention_core(q, k, v, kv_cache, layer_idx, start_pos, self.num_heads // self.num_kv_heads,
+                           self.decode_attn_op)
         return self.o(a.transpose(1, 2).reshape(B, T, self.num_heads * self.head_dim))
 
 

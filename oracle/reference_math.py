@@ -138,3 +138,23 @@ def mla_rope_keys(k_rope_pre, k_norm_w, inv_freq, t0=0):
     cos, sin = rope_cos_sin(np.arange(t0, t0 + kr.shape[1]), inv_freq)
     z = kr * w
     return z * cos[None, :, None, :] + rotate_half(z) * sin[None, :, None, :]
+
+
+def gqa_decode(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float) -> np.ndarray:
+    """Single-query GQA attention as the engine's decode step computes it:
+    K/V expanded over the g = H / KV heads of each group (repeat_interleave)
+    and ``scaled_dot_product_attention`` with no mask (engine/attention.py:
+    147-150; the decode seam at :138-145 receives the unexpanded K/V).
+    q: [B, H, D]; k, v: [B, KV, L, D] -> [B, H, D]."""
+    q = np.asarray(q, np.float64)
+    k = np.asarray(k, np.float64)
+    v = np.asarray(v, np.float64)
+    B, H, D = q.shape
+    g = H // k.shape[1]
+    out = np.empty((B, H, D))
+    for b in range(B):
+        for h in range(H):
+            s = k[b, h // g] @ q[b, h] * scale
+            p = np.exp(s - s.max())
+            out[b, h] = (p / p.sum()) @ v[b, h // g]
+    return out

@@ -15,7 +15,11 @@ against.  Values are captured with forward hooks on the reference modules:
   * QKV: the outputs of ``Attention.q/k/v`` inside ``Attention.forward``
     (engine/attention.py:119-121);
   * MLA decode: the output of ``q_norm`` and the input of ``o`` inside
-    ``MLAttention.forward`` (engine/mla.py:195-265), T == 1.
+    ``MLAttention.forward`` (engine/mla.py:195-265), T == 1;
+  * GQA decode: the input of ``o`` of ``Attention.forward`` on its default
+    single-query path (repeat_interleave + SDPA, engine/attention.py:147-150),
+    and the q / K / V that path sees, captured through the module's own decode
+    seam (``decode_attn_op``, :138-145) in a second, identical forward.
 """
 
 from __future__ import annotations
@@ -33,7 +37,7 @@ sys.path.insert(0, str(REPO))
 REF = Path(os.environ.get("LLMS_REF", "/root/reference"))
 sys.path.insert(0, str(REF / "src"))
 
-from engine.attention import Attention, RMSNorm  # noqa: E402
+from engine.attention import Attention, RMSNorm, build_rope_tables  # noqa: E402
 from engine.kv_cache import KVCache  # noqa: E402
 from engine.mla import MLAKVCache, MLAttention  # noqa: E402
 from engine.model import FFN  # noqa: E402
@@ -134,6 +138,37 @@ def ref_mla_decode(d, L, *, H, KV, D, DR, R, theta, eps, seed, knorm_noise):
     return out
 
 
+def ref_gqa_decode(*, B, H, KV, D, n_prefill, seed, hidden=64):
+    """One decode step (T == 1) of the reference ``Attention`` after a prefill
+    of ``n_prefill`` tokens; returns q [B, H, D], K / V [B, KV, L, D] (L =
+    n_prefill + 1, the whole cache), the softmax scale and the attention
+    output [B, H, D] of the default path."""
+    torch.manual_seed(seed)
+    attn = Attention(hidden_size=hidden, num_heads=H, num_kv_heads=KV, head_dim=D, rms_eps=1e-6)
+    L = n_prefill + 1
+    cache = KVCache.alloc(num_layers=1, max_batch=B, num_kv_heads=KV, max_seq_len=L, head_dim=D,
+                          dtype=torch.float32, device="cpu")
+    cos, sin = build_rope_tables(D, L, base=1e6, dtype=torch.float32)
+    x0 = torch.randn(B, n_prefill, hidden)
+    x1 = torch.randn(B, 1, hidden)
+    with torch.no_grad():
+        attn(x0, kv_cache=cache, layer_idx=0, cos=cos[:n_prefill], sin=sin[:n_prefill], start_pos=0)
+        box, h = capture_input(attn.o)
+        attn(x1, kv_cache=cache, layer_idx=0, cos=cos[n_prefill:L], sin=sin[n_prefill:L], start_pos=n_prefill)
+        h.remove()
+        grab = {}
+
+        def spy(q, full_k, full_v, *, scale, layer_idx):
+            grab.update(q=q.clone(), k=full_k.clone(), v=full_v.clone(), scale=scale)
+            return torch.zeros_like(q)
+
+        attn.decode_attn_op = spy
+        attn(x1, kv_cache=cache, layer_idx=0, cos=cos[n_prefill:L], sin=sin[n_prefill:L], start_pos=n_prefill)
+    return dict(q=grab["q"][:, :, 0].numpy().copy(), k=grab["k"].numpy().copy(), v=grab["v"].numpy().copy(),
+                scale=np.array([grab["scale"]], np.float32),
+                out=box["v"].view(B, H, D).numpy().copy())
+
+
 def main() -> None:
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     out = {}
@@ -170,6 +205,16 @@ def main() -> None:
         d = I.cfg4(B, L, **dims)
         r = ref_mla_decode(d, L, theta=1e6, eps=1e-6, seed=5, knorm_noise=noise, **dims)
         for k_, v_ in r.items():
+            out[f"{name}__{k_}"] = v_
+
+    gqa_cases = {
+        # name: (B, H, KV, D, prefill tokens)
+        "gqa_b2_h8_kv2_d128_l38": (2, 8, 2, 128, 37),
+        "gqa_b3_h12_kv4_d64_l70": (3, 12, 4, 64, 69),
+        "gqa_b1_h4_kv4_d32_l5": (1, 4, 4, 32, 4),
+    }
+    for name, (B, H, KV, D, n) in gqa_cases.items():
+        for k_, v_ in ref_gqa_decode(B=B, H=H, KV=KV, D=D, n_prefill=n, seed=11).items():
             out[f"{name}__{k_}"] = v_
 
     np.savez_compressed(HERE / "golden.npz", **{k: np.asarray(v, np.float32) for k, v in out.items()})

@@ -78,3 +78,11 @@ def test_mla_rope_tables(golden, name):
     cos, sin = O.rope_cos_sin(np.arange(L), O.mla_inv_freq(dims["D"], dims["DR"], 1e6))
     _close(cos, golden[f"{name}__rope_cos"], 0, 2e-6)
     _close(sin, golden[f"{name}__rope_sin"], 0, 2e-6)
+
+
+@pytest.mark.parametrize("name", ["gqa_b2_h8_kv2_d128_l38", "gqa_b3_h12_kv4_d64_l70", "gqa_b1_h4_kv4_d32_l5"])
+def test_gqa_decode(golden, name):
+    """The GQA decode oracle vs the reference Attention's default single-query
+    path, on the q / K / V that path saw."""
+    g = lambda k: golden[f"{name}__{k}"]
+    _close(O.gqa_decode(g("q"), g("k"), g("v"), float(g("scale")[0])), g("out"), 1e-5, 1e-6)
