@@ -19,7 +19,13 @@ e2e   : the same job through the public API (llms_b200.kernels functions,
         captured in a CUDA graph) with the step's activations copied from
         pinned host memory and all outputs copied back, inside the timed region.
 suite : (rank 0, N = 1) the other BASELINE sub-metrics measured in the same
-        run: per-op GB/s at M = 1, TFLOP/s at M = 2048, MLA decode GB/s.
+        run: per-op GB/s at M = 1, TFLOP/s at M = 2048, MLA decode GB/s; and
+        the parts next to the path: o / down projections against cuBLAS
+        (o_m*, down_m*), GQA decode attention against the reference's
+        repeat_interleave + SDPA (gqa_decode_*), the MLA fused Q + latent
+        projection against three cuBLAS Linears (mla_q_latent_proj_*), and
+        the Qwen3-8B int8 decode step with o / down on this library or on
+        cuBLAS (qwen3_8b_int8_decode_*).
 mla_decode_b32_l32768_sharded : (N > 1) MLA decode at B = 32, L = 32768 split
         by batch row across the ranks, whole-job GB/s (max-over-ranks time).
 """
