@@ -62,11 +62,11 @@ def parse_args():
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--no-suite", action="store_true", help="skip the per-op sub-metrics")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
-    p.add_argument("--profile-op", choices=["qkv", "gate_up", "qkv_w8", "gate_up_w8", "mla"],
+    p.add_argument("--profile-op", choices=["qkv", "gate_up", "qkv_w8", "gate_up_w8", "mla", "gqa", "down"],
                    help="run one op 3 times and exit (a small driver for ncu captures)")
     p.add_argument("--M", type=int, default=1, help="--profile-op: rows of x")
-    p.add_argument("--B", type=int, default=32, help="--profile-op mla: batch")
-    p.add_argument("--L", type=int, default=4096, help="--profile-op mla: context")
+    p.add_argument("--B", type=int, default=32, help="--profile-op mla / gqa: batch")
+    p.add_argument("--L", type=int, default=4096, help="--profile-op mla / gqa: context")
     return p.parse_args()
 
 
@@ -74,7 +74,8 @@ def profile_op(args):
     """Three calls of one hot-path op at a BASELINE shape, for ncu: the first
     two warm, the third is the one to capture (-s 2 -c 1)."""
     from llms_b200 import mla
-    from llms_b200.kernels import int8_fused_gate_up_silu, int8_fused_qkv, triton_fused_gate_up_silu, triton_fused_qkv
+    from llms_b200.kernels import (b200_decode_attn, b200_linear, int8_fused_gate_up_silu, int8_fused_qkv,
+                                   triton_fused_gate_up_silu, triton_fused_qkv)
 
     torch.cuda.set_device(0)
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -89,6 +90,15 @@ def profile_op(args):
         kw, inv = torch.ones(D, device="cuda"), mla.rope_inv_freq(D, DR, 1e6, "cuda")
         ks, kz = mla.mla_sidebands(c, kr, wuk, kw, inv, B=B, L=L, num_kv_heads=KV, head_dim=D, eps=1e-6)
         fn = lambda: mla.mla_decode(q, c, kz, ks, wuk, wuv, kw, inv, L=L, scale=D ** -0.5, eps=1e-6)
+    elif args.profile_op == "gqa":  # GQA decode attention, Qwen3 heads (32 q / 8 kv, D 128)
+        q = torch.randn(args.B, 32, 1, HEAD, **bf)
+        kc = torch.randn(args.B, 8, args.L, HEAD, **bf)
+        vc = torch.randn(args.B, 8, args.L, HEAD, **bf)
+        fn = lambda: b200_decode_attn(q, kc, vc, scale=HEAD ** -0.5)
+    elif args.profile_op == "down":  # Qwen3-4B FFN down projection [2560, 9728]
+        x = torch.randn(args.M, INTER, **bf)
+        w = torch.randn(HIDDEN, INTER, **bf) * 0.02
+        fn = lambda: b200_linear(x, w)
     else:
         M = args.M
         w8 = args.profile_op.endswith("_w8")
