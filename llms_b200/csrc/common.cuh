@@ -109,6 +109,9 @@ __device__ __forceinline__ uint32_t i8x2_to_h2(uint32_t wflip, int j) {
       __hsub2(*reinterpret_cast<const __half2*>(&h), __half2(__float2half(1152.f), __float2half(1152.f)));
   return *reinterpret_cast<const uint32_t*>(&v);
 }
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
