@@ -28,6 +28,11 @@ suite : (rank 0, N = 1) the other BASELINE sub-metrics measured in the same
         cuBLAS (qwen3_8b_int8_decode_*).
 mla_decode_b32_l32768_sharded : (N > 1) MLA decode at B = 32, L = 32768 split
         by batch row across the ranks, whole-job GB/s (max-over-ranks time).
+qwen3_8b_int8_decode_b*_sharded : (N > 1) the Qwen3-8B int8 decode step with
+        every projection column-sharded and all-gathered (llms_b200.shard),
+        tok/s at batch 1 / 16 / 64, plus its logit difference to the
+        unsharded step (the prefill's K split follows the shard width, so
+        the difference is not zero).
 """
 
 from __future__ import annotations
@@ -562,6 +567,64 @@ def suite(job):
     return out
 
 
+def qwen3_8b_int8_decode_sharded(rank, world, batches=(1, 16, 64), prompt=16, steps=20):
+    """BASELINE config 5 across GPUs (llms_b200.shard): every projection of
+    each layer column-sharded (QKV head-aligned, gate-up by intermediate
+    columns, o / down by hidden columns) and followed by one NCCL all-gather;
+    attention, norms, embedding and LM head replicated.  Each rank builds the
+    same seeded model; before sharding it runs one unsharded decode step,
+    after sharding the same step, and the largest logit difference over
+    ranks is reported.  Timing: one decode step per CUDA graph (the
+    all-gathers captured inside), max over ranks; tok/s = batch / step."""
+    from llms_b200.kernels import apply_linear_kernels
+    from llms_b200.qwen3 import greedy, synthetic_int8_model
+    from llms_b200.shard import shard_decode_model
+
+    model = synthetic_int8_model(seed=4)
+    apply_linear_kernels(model)
+    inputs = {}
+    for B in batches:
+        g = torch.Generator(device="cuda").manual_seed(100 + B)
+        inputs[B] = (torch.randint(0, model.shape.vocab_size, (B, prompt), generator=g, device="cuda"),
+                     torch.randint(0, model.shape.vocab_size, (B, 1), generator=g, device="cuda"))
+    with torch.inference_mode():
+        ids, nxt = inputs[batches[0]]
+        cache = model.alloc_cache(prompt + 8, max_batch=ids.shape[0])
+        model(ids, cache, start_pos=0)
+        ref = model(nxt, cache, start_pos=prompt)[:, -1].float()
+        del cache
+    shard_decode_model(model, rank, world)
+    torch.cuda.empty_cache()
+    res = {}
+    with torch.inference_mode():
+        for B in batches:
+            ids, nxt = inputs[B]
+            cache = model.alloc_cache(prompt + 8, max_batch=B)
+            model(ids, cache, start_pos=0)
+            logits = model(nxt, cache, start_pos=prompt)[:, -1].float()
+            entry = {}
+            if B == batches[0]:
+                diff = (logits - ref).abs().max().item()
+                entry["max_abs_logit_diff_vs_unsharded"] = max_over_ranks(diff, world)
+                entry["argmax_agree_vs_unsharded"] = bool((greedy(logits) == greedy(ref)).all().item())
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                model(nxt, cache, start_pos=prompt)
+            torch.cuda.current_stream().wait_stream(s)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                model(nxt, cache, start_pos=prompt)
+            sec = time_graph(graph, steps, 3, world)
+            del graph, cache
+            res[f"qwen3_8b_int8_decode_b{B}_sharded"] = {
+                "ms_per_step": sec / steps * 1e3, "tok/s": B * steps / sec,
+                "split": f"column shards over {world} GPUs, NCCL all-gather after each projection", **entry}
+    del model
+    torch.cuda.empty_cache()
+    return res
+
+
 def mla_sharded(rank, world, steps=10):
     """BASELINE configs[3] across GPUs: MLA decode at B = 32, L = 32768 split
     by batch row (llms_b200.mla.batch_shard; no collective in the op), one
@@ -813,6 +876,7 @@ def main():
         extra["suite"] = suite(job)
     if world > 1:
         extra["mla_decode_b32_l32768_sharded"] = mla_sharded(rank, world)
+        extra.update(qwen3_8b_int8_decode_sharded(rank, world))
     cpu = None
     if rank == 0 and world == 1:
         from oracle import cpu_baseline as CB

@@ -1,0 +1,151 @@
+"""Column-sharded decode step across GPUs (one process per GPU).
+
+The multi-GPU form of the Qwen3-8B-shaped int8 decode step: every
+projection of a layer is split by output columns across the ranks and
+followed by one NCCL all-gather, the only collective the path uses:
+
+* fused QKV, head-aligned: rank r holds q heads [r H / N, (r + 1) H / N)
+  and the same share of the k and v heads (rows of the stacked [Wq; Wk; Wv]),
+  so every rank's block is whole heads;
+* gate-up-SiLU by intermediate columns (the gate and up rows of the same
+  columns stay together, so SiLU * up is local);
+* ``o`` and ``down`` by hidden columns.
+
+The attention core (QK-norm, RoPE, the KV cache, softmax), the norms, the
+embedding and the LM head run replicated on every rank, on the gathered
+activations, so each rank holds the whole KV cache and produces the whole
+logits.  Row-parallel projections with an all-reduce are not used (the path
+allows gathers only).  Every projection is one of this package's kernels on
+the local shard: ``int8_linear`` / ``int8_fused_gate_up_silu`` for the int8
+projections and ``b200_linear`` for ``o`` / ``down``.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+from torch import nn
+
+from .kernels.linear import b200_linear, int8_linear
+from .kernels.quant import Int8Attention, Int8FFN, int8_fused_gate_up_silu
+
+
+def even_range(n: int, rank: int, world: int) -> range:
+    """Rank ``rank``'s block of ``n`` columns; ``n`` must split evenly (the
+    all-gather moves equal blocks)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} not in [0, {world})")
+    if n % world:
+        raise ValueError(f"{n} columns do not split evenly over {world} ranks")
+    per = n // world
+    return range(rank * per, (rank + 1) * per)
+
+
+def qkv_rows(n_q: int, n_k: int, rank: int, world: int) -> list[int]:
+    """Rows of the stacked [Wq; Wk; Wv] that rank ``rank`` holds, head-aligned
+    when the head counts split evenly (callers check that)."""
+    q = even_range(n_q, rank, world)
+    k = even_range(n_k, rank, world)
+    return list(q) + [n_q + i for i in k] + [n_q + n_k + i for i in k]
+
+
+def gather_cols(y: torch.Tensor, world: int, group=None) -> torch.Tensor:
+    """All-gather each rank's column block of ``y`` (..., c) into (..., world c),
+    blocks in rank order."""
+    if world == 1:
+        return y
+    lead, c = y.shape[:-1], y.shape[-1]
+    y2 = y.reshape(-1, c).contiguous()
+    out = torch.empty((world * y2.shape[0], c), dtype=y.dtype, device=y.device)
+    dist.all_gather_into_tensor(out, y2, group=group)
+    return out.view(world, y2.shape[0], c).permute(1, 0, 2).reshape(*lead, world * c)
+
+
+def gather_qkv(y: torch.Tensor, cq: int, ck: int, world: int, group=None):
+    """All-gather per-rank [q_r | k_r | v_r] blocks (widths cq, ck, ck) into the
+    full q (world cq), k and v (world ck), each in head order."""
+    lead = y.shape[:-1]
+    if world == 1:
+        return y.split([cq, ck, ck], dim=-1)
+    y2 = y.reshape(-1, cq + 2 * ck).contiguous()
+    out = torch.empty((world * y2.shape[0], cq + 2 * ck), dtype=y.dtype, device=y.device)
+    dist.all_gather_into_tensor(out, y2, group=group)
+    parts = out.view(world, y2.shape[0], cq + 2 * ck).split([cq, ck, ck], dim=-1)
+    return tuple(p.permute(1, 0, 2).reshape(*lead, world * p.shape[-1]) for p in parts)
+
+
+class ShardedLinear(nn.Module):
+    """Bias-free projection holding this rank's block of output rows of the
+    full weight; the output is gathered back to the full width."""
+
+    def __init__(self, weight: torch.Tensor, world: int, group=None) -> None:
+        super().__init__()
+        self.weight = nn.Parameter(weight, requires_grad=False)
+        self.world, self.group = world, group
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return gather_cols(b200_linear(x, self.weight), self.world, self.group)
+
+
+class ShardedInt8Attention(Int8Attention):
+    """``Int8Attention`` whose QKV and ``o`` projections run on this rank's
+    rows; the attention core in between is the inherited, replicated one."""
+
+    @classmethod
+    def from_module(cls, att: Int8Attention, rank: int, world: int, group=None) -> "ShardedInt8Attention":
+        if att.num_heads % world or att.num_kv_heads % world:
+            raise ValueError(f"{att.num_heads} q / {att.num_kv_heads} kv heads do not split over {world} ranks")
+        out = cls.__new__(cls)
+        nn.Module.__init__(out)
+        for name in ("hidden_size", "num_heads", "num_kv_heads", "head_dim", "n_q", "n_k"):
+            setattr(out, name, getattr(att, name))
+        rows = torch.tensor(qkv_rows(att.n_q, att.n_k, rank, world), device=att.q_qkv.device)
+        out.register_buffer("q_qkv", att.q_qkv.index_select(0, rows).contiguous())
+        out.register_buffer("s_qkv", att.s_qkv.index_select(0, rows).contiguous())
+        hid = even_range(att.o.weight.shape[0], rank, world)
+        out.o = ShardedLinear(att.o.weight.detach()[hid.start:hid.stop].contiguous(), world, group)
+        out.q_norm, out.k_norm = att.q_norm, att.k_norm
+        out.decode_attn_op = getattr(att, "decode_attn_op", None)
+        out.world, out.group = world, group
+        return out
+
+    def project_qkv(self, x: torch.Tensor):
+        y = int8_linear(x, self.q_qkv, self.s_qkv)
+        return gather_qkv(y, self.n_q // self.world, self.n_k // self.world, self.world, self.group)
+
+
+class ShardedInt8FFN(Int8FFN):
+    """``Int8FFN`` with this rank's intermediate columns of gate / up and its
+    hidden columns of ``down``."""
+
+    @classmethod
+    def from_module(cls, ffn: Int8FFN, rank: int, world: int, group=None) -> "ShardedInt8FFN":
+        out = cls.__new__(cls)
+        nn.Module.__init__(out)
+        cols = even_range(ffn.qg.shape[0], rank, world)
+        sl = slice(cols.start, cols.stop)
+        for name in ("qg", "sg", "qu", "su"):
+            out.register_buffer(name, getattr(ffn, name)[sl].contiguous())
+        w = ffn.down.weight.detach()
+        hid = even_range(w.shape[0], rank, world)
+        out.down = ShardedLinear(w[hid.start:hid.stop].contiguous(), world, group)
+        out.world, out.group = world, group
+        return out
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        h = int8_fused_gate_up_silu(x, self.qg, self.sg, self.qu, self.su)
+        return self.down(gather_cols(h, self.world, self.group))
+
+
+def shard_decode_model(model: nn.Module, rank: int, world: int, group=None) -> nn.Module:
+    """Replace every layer's int8 attention / FFN with its column-sharded
+    form (in place; the full projection weights are dropped).  Returns
+    ``model``."""
+    for block in model.layers:
+        block.attn = ShardedInt8Attention.from_module(block.attn, rank, world, group)
+        block.ffn = ShardedInt8FFN.from_module(block.ffn, rank, world, group)
+    return model
+
+
+__all__ = ["ShardedInt8Attention", "ShardedInt8FFN", "ShardedLinear", "even_range", "gather_cols",
+           "gather_qkv", "qkv_rows", "shard_decode_model"]
