@@ -491,20 +491,23 @@ int launch_cfg(const DenseArgs& a) {
   const int dev = current_device();
   if (dev < 0 || dev >= 64) return B200MM_ERR_DEVICE;
   const int sms = num_sms(dev);
-  // ring: one CTA per SM when the tiles fit in one wave that way, else two;
-  // two K-chunks per stage when that still leaves three stages
+  // ring: one CTA per SM when the tiles fit in one wave that way, else two
   int budget_idx = base <= sms ? 0 : 1;
 #ifdef SWAP_TRACE
   if (const char* e = getenv("B200MM_SWAP_BUDGET")) budget_idx = atoi(e) ? 1 : 0;
 #endif
   if (budget_idx == 1 && kBudget2 < C::OPS * C::OPST + 2 * C::CHUNK) budget_idx = 0;  // big int8 tiles
   const uint32_t budget = (budget_idx == 0 ? kBudget1 : kBudget2) - C::OPS * C::OPST;
-  // K-chunks per stage: as many as leave three stages (a stage costs one
-  // tcgen05.commit, which stalls the issuer), up to 8
+  // K-chunks per stage (a stage costs one tcgen05.commit, which stalls the
+  // issuer): int8, as many as leave three stages, up to 8 (the converter
+  // ring sits between the stages and the MMAs); 16-bit, as many as leave two
+  // stages, up to 4 (measured: 4 chunks in 2 stages beat 2 chunks in 5 by
+  // 4-9 % at M = 16..64, and gate-up 2 chunks in 2 stages beat 1 in 5 by 15 %)
   int kc = 1;
+  constexpr int kMaxKc = W8 ? 8 : 4, kMinStages = W8 ? 3 : 2;
   if (map3d)
-    for (int c = 8; c >= 2; c >>= 1)
-      if (kchunks >= c && budget / (c * C::CHUNK) >= 3) {
+    for (int c = kMaxKc; c >= 2; c >>= 1)
+      if (kchunks >= c && budget / (c * C::CHUNK) >= (uint32_t)kMinStages) {
         kc = c;
         break;
       }
