@@ -791,14 +791,12 @@ def main():
     if args.profile_op:
         profile_op(args)
         return
-    rank, world, local = dist_setup()
     if args.impl == "reference":
-        run_reference(args, rank, world)
-        if world > 1:
-            import torch.distributed as dist
-
-            dist.destroy_process_group()
+        # the reference arm runs on host cores only: no device, no process
+        # group; under torchrun rank 0 runs and prints, the other ranks exit 0
+        run_reference(args, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")))
         return
+    rank, world, local = dist_setup()
 
     from llms_b200 import _capi
     from llms_b200.kernels import triton_fused_gate_up_silu, triton_fused_qkv

@@ -1,0 +1,34 @@
+"""The bench's reference arm (`bench.py --impl reference`) runs on host cores
+only: it must print one JSON line with the contract's keys on rank 0 and exit
+0 without work on the other ranks -- on a machine with no GPU too."""
+
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _run(env_extra):
+    env = dict(os.environ, **env_extra)
+    return subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "2",
+                           "--warmup", "1"], capture_output=True, text=True, env=env, timeout=600)
+
+
+def test_reference_arm_prints_contract_line():
+    r = _run({"WORLD_SIZE": "1", "RANK": "0"})
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    for key in ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "scaling", "dtype", "config", "cpu_baseline", "e2e"):
+        assert key in line, key
+    assert line["impl"] == "reference" and line["value"] > 0
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["value"] == line["value"]
+
+
+def test_reference_arm_other_ranks_exit_quietly():
+    r = _run({"WORLD_SIZE": "2", "RANK": "1"})
+    assert r.returncode == 0 and r.stdout.strip() == "", (r.stdout, r.stderr[-2000:])
