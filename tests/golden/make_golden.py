@@ -34,7 +34,9 @@ import torch
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
 sys.path.insert(0, str(REPO))
-REF = Path(os.environ.get("LLMS_REF", "/root/reference"))
+if "LLMS_REF" not in os.environ:
+    sys.exit("set LLMS_REF to the reference checkout (the directory holding src/engine)")
+REF = Path(os.environ["LLMS_REF"])
 sys.path.insert(0, str(REF / "src"))
 
 from engine.attention import Attention, RMSNorm, build_rope_tables  # noqa: E402
