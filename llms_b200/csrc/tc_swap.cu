@@ -61,8 +61,15 @@ struct SwapCfg {
   static constexpr uint32_t OPST = W8 ? NW * W16 + XB : 0;  // converted operands of one chunk
   static constexpr int OPS = W8 ? 2 : 0;
   static constexpr int ACC = NW * MN;           // accumulator columns
-  static constexpr int RP = ACC + 4;            // reduction row pitch (floats)
-  static constexpr uint32_t RED = FM * RP * 4;  // one rank's partial
+  static constexpr int CW = ACC >= 32 ? 32 : 16;  // accumulator columns per TMEM load
+  static constexpr int SPAN = MN < CW ? MN : CW;  // activation columns per epilogue block
+  static constexpr int NB = MN / SPAN;            // epilogue blocks; block j belongs to cluster rank j % cs
+  // floats per partial row at an owner rank: its blocks only, gate and up
+  __host__ __device__ static constexpr int rpo(int cs) { return (NB + cs - 1) / cs * SPAN * NW + 4; }
+  // bytes an owner rank receives from the other cs - 1 ranks
+  __host__ __device__ static constexpr uint32_t red_bytes(int cs) {
+    return (uint32_t)(cs - 1) * FM * rpo(cs) * 4;
+  }
   static constexpr uint32_t EXTRA = 1024 /*align*/ + 512 /*barriers, flags*/;
   static_assert(WB % 1024 == 0 && XB % 1024 == 0 && OPST % 1024 == 0, "chunks must keep the 1024-byte alignment");
 };
@@ -334,73 +341,84 @@ __global__ void __launch_bounds__(kThr, 2)
   constexpr bool kAllLanes = FM == 128;
   const int fl = kAllLanes ? 32 * q + lane : 16 * q + lane;
   const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16);
-  constexpr int CW = C::ACC >= 32 ? 32 : 16;  // columns per TMEM load
-  float* red = reinterpret_cast<float*>(sm);  // the ring is idle now: rank 0 collects partials here
-  if (p.cs > 1) {
+  constexpr int CW = C::CW, SPAN = C::SPAN, NB = C::NB;
+  const int cs = p.cs;
+  const int rpo = C::rpo(cs);
+  // The K split's partials meet at their owners: epilogue block j (activation
+  // columns [j SPAN, (j + 1) SPAN)) belongs to rank j % cs, which receives
+  // that block from the other ranks into its idle ring and finishes it.  Every
+  // owner's buffer then holds only its own blocks, and every rank stores.
+  float* red = reinterpret_cast<float*>(sm);
+  auto load_block = [&](int c, float* g, float* u) {  // sum of the accumulator sets, columns [c, c + SPAN)
+    for (int jj = 0; jj < p.na; ++jj) {
+      const uint32_t tj = tq + jj * C::ACC;
+      float g1[CW], u1[CW];
+      if (GATE && MN < CW) {  // MN = 16: one 32-column load holds [gate | up]
+        tmem_ld<CW>(tj, g1);
+#pragma unroll
+        for (int e = 0; e < MN; ++e) u1[e] = g1[MN + e];
+      } else {
+        tmem_ld<CW>(tj + c, g1);
+        if (GATE) tmem_ld<CW>(tj + MN + c, u1);
+      }
+#pragma unroll
+      for (int e = 0; e < CW; ++e) {
+        g[e] = jj ? g[e] + g1[e] : g1[e];
+        if (GATE) u[e] = jj ? u[e] + u1[e] : u1[e];
+      }
+    }
+  };
+  if (cs > 1) {
     cluster_sync();  // every rank's ring is idle
-    if (rank != 0 && epi) {
+    if (epi) {
       // the loads are warp-collective; at M = 64 lanes 16-31 hold nothing and store nothing
-      float* dst = red + ((int64_t)(rank - 1) * FM + fl) * C::RP;
 #pragma unroll 1
-      for (int c = 0; c < C::ACC; c += CW) {
-        float v[CW];
-        tmem_ld<CW>(tq + c, v);
-        for (int jj = 1; jj < p.na; ++jj) {
-          float v1[CW];
-          tmem_ld<CW>(tq + jj * C::ACC + c, v1);
-#pragma unroll
-          for (int e = 0; e < CW; ++e) v[e] += v1[e];
-        }
+      for (int j = 0; j < NB; ++j) {
+        const int o = j % cs;
+        if (o == rank) continue;
+        float g[CW], u[CW];
+        load_block(j * SPAN, g, u);
         if (kAllLanes || lane < 16) {
+          const int slot = rank < o ? rank : rank - 1;
+          float* dst = red + ((int64_t)slot * FM + fl) * rpo + (j / cs) * SPAN * C::NW;
 #pragma unroll
-          for (int e = 0; e < CW; e += 4)
-            st_cluster_f4(map_to_rank(dst + c + e, 0), v[e], v[e + 1], v[e + 2], v[e + 3]);
+          for (int e = 0; e < SPAN; e += 4) {
+            st_cluster_f4(map_to_rank(dst + e, (uint32_t)o), g[e], g[e + 1], g[e + 2], g[e + 3]);
+            if (GATE) st_cluster_f4(map_to_rank(dst + SPAN + e, (uint32_t)o), u[e], u[e + 1], u[e + 2], u[e + 3]);
+          }
         }
       }
       if (bad && threadIdx.x == 64) {
         const int one = 1;
-        asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(map_to_rank(peer_failed, 0)), "r"(one) : "memory");
+        for (int o = 0; o < cs; ++o)
+          if (o != rank)
+            asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(map_to_rank(peer_failed, (uint32_t)o)), "r"(one)
+                         : "memory");
       }
     }
     cluster_sync();  // partials landed
   }
-  if (rank == 0 && epi) {
+  if (epi) {
     bad = bad || *reinterpret_cast<volatile int*>(peer_failed);
     const int f = f0 + fl;
     const bool live = (kAllLanes || lane < 16) && f < p.N;
     const float sc0 = (live && p.s0) ? p.s0[f] : 1.f;
     const float sc1 = (live && GATE && p.s1) ? p.s1[f] : 1.f;
     T* ycol = static_cast<T*>(p.y) + f;
-    constexpr int SPAN = MN < CW ? MN : CW;  // output columns handled per step
 #pragma unroll 1
-    for (int c = 0; c < MN; c += SPAN) {
+    for (int j = rank; j < NB; j += cs) {  // the blocks this rank owns (all of them without a cluster)
+      const int c = j * SPAN;
       float g[CW], u[CW];
-      for (int jj = 0; jj < p.na; ++jj) {  // sum the accumulator sets
-        const uint32_t tj = tq + jj * C::ACC;
-        float g1[CW], u1[CW];
-        if (GATE && MN < CW) {  // MN = 16: one 32-column load holds [gate | up]
-          tmem_ld<CW>(tj, g1);
-#pragma unroll
-          for (int e = 0; e < MN; ++e) u1[e] = g1[MN + e];
-        } else {
-          tmem_ld<CW>(tj + c, g1);
-          if (GATE) tmem_ld<CW>(tj + MN + c, u1);
-        }
-#pragma unroll
-        for (int e = 0; e < CW; ++e) {
-          g[e] = jj ? g[e] + g1[e] : g1[e];
-          if (GATE) u[e] = jj ? u[e] + u1[e] : u1[e];
-        }
-      }
+      load_block(c, g, u);
       if (live) {
-        for (int r = 0; r + 1 < p.cs; ++r) {
-          const float* src = red + ((int64_t)r * FM + fl) * C::RP;
+        for (int r = 0; r + 1 < cs; ++r) {
+          const float* src = red + ((int64_t)r * FM + fl) * rpo + (j / cs) * SPAN * C::NW;
 #pragma unroll
           for (int e = 0; e < SPAN; e += 4) {
-            const float4 a = *reinterpret_cast<const float4*>(src + c + e);
+            const float4 a = *reinterpret_cast<const float4*>(src + e);
             g[e] += a.x; g[e + 1] += a.y; g[e + 2] += a.z; g[e + 3] += a.w;
             if (GATE) {
-              const float4 b = *reinterpret_cast<const float4*>(src + MN + c + e);
+              const float4 b = *reinterpret_cast<const float4*>(src + SPAN + e);
               u[e] += b.x; u[e + 1] += b.y; u[e + 2] += b.z; u[e + 3] += b.w;
             }
           }
@@ -549,7 +567,7 @@ int launch_cfg(const DenseArgs& a) {
 #ifdef SWAP_TRACE
   if (const char* e = getenv("B200MM_SWAP_CS")) cs_cap = atoi(e);
 #endif
-  for (int c = 2; c <= cs_cap && c <= nstages / 2 && base * c <= slots && (uint32_t)(c - 1) * C::RED <= ns * stage;
+  for (int c = 2; c <= cs_cap && c <= nstages / 2 && base * c <= slots && C::red_bytes(c) <= ns * stage;
        ++c) {
     if (base > max_clusters(kern, c, smem, budget_idx)) break;
     cs = c;
