@@ -91,3 +91,44 @@ def test_cpu_tensors_fail_loudly():
         triton_fused_gate_up_silu(x, W, W)
     with pytest.raises(RuntimeError, match="no CPU path"):
         triton_fused_qkv(x, W, n_q=64, n_k=16)
+
+
+def test_linear_and_gqa_entry_points_validate_before_launch():
+    """b200mm_linear(_w8) and b200mm_gqa_decode reject invalid calls with the
+    documented status codes before touching a device (no GPU here: a valid
+    call reaches the device check and returns B200MM_ERR_DEVICE)."""
+    from llms_b200 import _capi
+    L = _capi.lib
+    before = L.b200mm_launch_count()
+    fake = ctypes.c_void_p(256)
+    OK, SHAPE, DTYPE, ARG, WS, DEV = 0, 1, 3, 5, 6, 7
+    # plain projection: same checks as the QKV entry point
+    assert L.b200mm_linear(None, 64, fake, 64, fake, 32, 1, 32, 64, 2, None) == ARG
+    assert L.b200mm_linear(fake, 64, fake, 64, fake, 32, 1, 32, 0, 2, None) == SHAPE
+    assert L.b200mm_linear(fake, 64, fake, 64, fake, 32, 1, 32, 64, 9, None) == DTYPE
+    assert L.b200mm_linear(fake, 64, fake, 64, fake, 32, 0, 32, 64, 2, None) == OK
+    assert L.b200mm_linear_w8(fake, 64, fake, None, 64, fake, 32, 1, 32, 64, 2, None) == ARG
+    # GQA decode: workspace size, then argument checks in order
+    ws = L.b200mm_gqa_decode_workspace_size(2, 32, 8, 128, 1000)
+    assert ws > 0 and ws % 256 == 0
+    assert L.b200mm_gqa_decode_workspace_size(2, 32, 7, 128, 1000) == 0   # H % KV != 0
+    assert L.b200mm_gqa_decode_workspace_size(2, 32, 8, 128, 0) == 0      # no tokens
+    assert L.b200mm_gqa_decode_workspace_size(2, 32, 8, 127, 10) == 0     # odd head dim
+    good = dict(q_sb=32 * 128, q_sh=128, k_sb=8 * 1024 * 128, k_sh=1024 * 128, k_st=128)
+
+    def call(q=fake, k=fake, v=fake, out=fake, B=2, H=32, KV=8, D=128, Lc=1000, scale=0.088, dtype=2,
+             wsp=ctypes.c_void_p(4096), wsb=ws, k_st=128):
+        return L.b200mm_gqa_decode(q, good["q_sb"], good["q_sh"], k, good["k_sb"], good["k_sh"], k_st,
+                                   v, good["k_sb"], good["k_sh"], k_st, out, good["q_sb"], good["q_sh"],
+                                   B, H, KV, D, Lc, scale, dtype, wsp, wsb, None)
+
+    assert call(dtype=5) == DTYPE
+    assert call(KV=7) == SHAPE
+    assert call(q=None) == ARG
+    assert call(scale=0.0) == ARG
+    assert call(k_st=64) == SHAPE                    # token stride shorter than a row
+    assert call(B=0) == OK                           # empty batch: no-op
+    assert call(wsb=ws - 1) == WS                    # workspace too small
+    assert call(wsp=ctypes.c_void_p(4096 + 16)) == WS  # workspace not 256-byte aligned
+    assert call() == DEV                             # valid: stops at the device check here
+    assert L.b200mm_launch_count() == before
