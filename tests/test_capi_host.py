@@ -132,3 +132,31 @@ def test_linear_and_gqa_entry_points_validate_before_launch():
     assert call(wsp=ctypes.c_void_p(4096 + 16)) == WS  # workspace not 256-byte aligned
     assert call() == DEV                             # valid: stops at the device check here
     assert L.b200mm_launch_count() == before
+
+
+def test_new_ops_check_arguments_on_the_host():
+    """b200_linear / int8_linear / b200_decode_attn validate shapes and dtypes
+    before any device work, and refuse CPU tensors (no CPU path)."""
+    from llms_b200.kernels import b200_decode_attn, b200_linear, int8_linear
+    x = torch.zeros(2, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="W must be 2D"):
+        b200_linear(x, torch.zeros(64, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="x last dim"):
+        b200_linear(x, torch.zeros(8, 32, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="share a dtype"):
+        b200_linear(x, torch.zeros(8, 64, dtype=torch.float16))
+    with pytest.raises(RuntimeError, match="no CPU path"):
+        b200_linear(x, torch.zeros(8, 64, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="int8"):
+        int8_linear(x, torch.zeros(8, 64, dtype=torch.bfloat16), torch.ones(8))
+    with pytest.raises(ValueError, match="float32 of shape"):
+        int8_linear(x, torch.zeros(8, 64, dtype=torch.int8), torch.ones(7))
+    q = torch.zeros(2, 8, 1, 64, dtype=torch.bfloat16)
+    k = torch.zeros(2, 2, 10, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match=r"\(B, H, 1, D\)"):
+        b200_decode_attn(q[:, :, 0], k, k, scale=0.1)
+    with pytest.raises(ValueError, match="does not match"):
+        b200_decode_attn(q, torch.zeros(2, 3, 10, 64, dtype=torch.bfloat16),
+                         torch.zeros(2, 3, 10, 64, dtype=torch.bfloat16), scale=0.1)
+    with pytest.raises(RuntimeError, match="no CPU path"):
+        b200_decode_attn(q, k, k, scale=0.1)
