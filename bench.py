@@ -144,8 +144,12 @@ def dist_setup():
     if world > 1:
         import torch.distributed as dist
 
+        from datetime import timedelta
+
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        # a finite timeout: a rank that fails alone must not leave the others
+        # waiting in a collective for the default ten minutes
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=timedelta(seconds=300))
     else:
         torch.cuda.set_device(0)
     return rank, world, local
@@ -873,8 +877,15 @@ def main():
     if rank == 0 and world == 1 and not args.no_suite:
         extra["suite"] = suite(job)
     if world > 1:
-        extra["mla_decode_b32_l32768_sharded"] = mla_sharded(rank, world)
-        extra.update(qwen3_8b_int8_decode_sharded(rank, world))
+        # the sub-metrics next to the headline: a failure costs its own key only
+        for key, fn in (("mla_decode_b32_l32768_sharded", lambda: {"mla_decode_b32_l32768_sharded":
+                                                                    mla_sharded(rank, world)}),
+                        ("qwen3_8b_int8_decode_sharded", lambda: qwen3_8b_int8_decode_sharded(rank, world))):
+            try:
+                extra.update(fn())
+            except Exception as e:  # noqa: BLE001 -- reported in the JSON line
+                extra[key + "_error"] = f"{type(e).__name__}: {e}"[:300]
+                torch.cuda.synchronize()
     cpu = None
     if rank == 0 and world == 1:
         from oracle import cpu_baseline as CB
