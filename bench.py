@@ -875,7 +875,10 @@ def main():
 
     extra = {}
     if rank == 0 and world == 1 and not args.no_suite:
-        extra["suite"] = suite(job)
+        try:
+            extra["suite"] = suite(job)
+        except Exception as e:  # noqa: BLE001 -- the headline line still prints
+            extra["suite_error"] = f"{type(e).__name__}: {e}"[:300]
     if world > 1:
         # the sub-metrics next to the headline: a failure costs its own key only
         for key, fn in (("mla_decode_b32_l32768_sharded", lambda: {"mla_decode_b32_l32768_sharded":
@@ -885,7 +888,6 @@ def main():
                 extra.update(fn())
             except Exception as e:  # noqa: BLE001 -- reported in the JSON line
                 extra[key + "_error"] = f"{type(e).__name__}: {e}"[:300]
-                torch.cuda.synchronize()
     cpu = None
     if rank == 0 and world == 1:
         from oracle import cpu_baseline as CB
