@@ -16,7 +16,9 @@ against.  Values are captured with forward hooks on the reference modules:
     (engine/attention.py:119-121);
   * MLA decode: the output of ``q_norm`` and the input of ``o`` inside
     ``MLAttention.forward`` (engine/mla.py:195-265), T == 1;
-  * GQA decode: the input of ``o`` of ``Attention.forward`` on its default
+  * ``down``: the input and output of ``FFN.down`` inside ``FFN.forward``
+    (engine/model.py:37);
+  * GQA decode: the input and output of ``o`` of ``Attention.forward`` on its default
     single-query path (repeat_interleave + SDPA, engine/attention.py:147-150),
     and the q / K / V that path sees, captured through the module's own decode
     seam (``decode_attn_op``, :138-145) in a second, identical forward.
@@ -70,6 +72,20 @@ def ref_gate_up(x, wg, wu):
         ffn(torch.from_numpy(x))
     h.remove()
     return box["v"].numpy()
+
+
+def ref_down(x, seed=12, hidden=256, inter=768):
+    """The reference FFN (engine/model.py:27-37) on x [M, hidden]: the input
+    and output of its ``down`` projection, and the down weight."""
+    torch.manual_seed(seed)
+    ffn = FFN(hidden, inter)
+    bi, h1 = capture_input(ffn.down)
+    bo, h2 = capture_output(ffn.down)
+    with torch.no_grad():
+        ffn(torch.from_numpy(x))
+    h1.remove()
+    h2.remove()
+    return dict(h=bi["v"].numpy(), w=ffn.down.weight.detach().numpy().copy(), y=bo["v"].numpy())
 
 
 def ref_qkv(x, w, n_q, n_k, head_dim=128):
@@ -156,8 +172,10 @@ def ref_gqa_decode(*, B, H, KV, D, n_prefill, seed, hidden=64):
     with torch.no_grad():
         attn(x0, kv_cache=cache, layer_idx=0, cos=cos[:n_prefill], sin=sin[:n_prefill], start_pos=0)
         box, h = capture_input(attn.o)
+        bo, h2 = capture_output(attn.o)
         attn(x1, kv_cache=cache, layer_idx=0, cos=cos[n_prefill:L], sin=sin[n_prefill:L], start_pos=n_prefill)
         h.remove()
+        h2.remove()
         grab = {}
 
         def spy(q, full_k, full_v, *, scale, layer_idx):
@@ -168,7 +186,8 @@ def ref_gqa_decode(*, B, H, KV, D, n_prefill, seed, hidden=64):
         attn(x1, kv_cache=cache, layer_idx=0, cos=cos[n_prefill:L], sin=sin[n_prefill:L], start_pos=n_prefill)
     return dict(q=grab["q"][:, :, 0].numpy().copy(), k=grab["k"].numpy().copy(), v=grab["v"].numpy().copy(),
                 scale=np.array([grab["scale"]], np.float32),
-                out=box["v"].view(B, H, D).numpy().copy())
+                out=box["v"].view(B, H, D).numpy().copy(),
+                o_w=attn.o.weight.detach().numpy().copy(), o_y=bo["v"].numpy().copy())
 
 
 def main() -> None:
@@ -208,6 +227,12 @@ def main() -> None:
         r = ref_mla_decode(d, L, theta=1e6, eps=1e-6, seed=5, knorm_noise=noise, **dims)
         for k_, v_ in r.items():
             out[f"{name}__{k_}"] = v_
+
+    # the bias-free projections behind o / down (engine/attention.py:163,
+    # engine/model.py:37): the reference FFN's own down input and output
+    rng = np.random.default_rng(12)
+    for k_, v_ in ref_down(rng.standard_normal((3, 256), dtype=np.float32)).items():
+        out[f"down_m3__{k_}"] = v_
 
     gqa_cases = {
         # name: (B, H, KV, D, prefill tokens)

@@ -86,3 +86,14 @@ def test_gqa_decode(golden, name):
     path, on the q / K / V that path saw."""
     g = lambda k: golden[f"{name}__{k}"]
     _close(O.gqa_decode(g("q"), g("k"), g("v"), float(g("scale")[0])), g("out"), 1e-5, 1e-6)
+
+
+def test_linear_down_and_o(golden):
+    """The bias-free projection oracle vs the reference's own ``FFN.down``
+    (engine/model.py:37) and ``Attention.o`` (engine/attention.py:163)
+    inputs and outputs."""
+    _close(O.linear(golden["down_m3__h"], golden["down_m3__w"]), golden["down_m3__y"], 1e-5, 1e-6)
+    for name in ("gqa_b2_h8_kv2_d128_l38", "gqa_b3_h12_kv4_d64_l70", "gqa_b1_h4_kv4_d32_l5"):
+        out = golden[f"{name}__out"]
+        B, H, D = out.shape
+        _close(O.linear(out.reshape(B, 1, H * D), golden[f"{name}__o_w"]), golden[f"{name}__o_y"], 1e-5, 1e-6)
