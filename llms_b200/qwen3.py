@@ -102,6 +102,37 @@ def attention_core(q, k, v, kv_cache, layer_idx, start_pos, n_rep, decode_op=Non
     return F.scaled_dot_product_attention(q, fk, fv, attn_mask=qp >= kp)
 
 
+def _project_qkv(attn, x):
+    """q, k, v of any attention module here (the engine's q/k/v Linears, or the
+    fused / int8 / sharded modules' ``project_qkv``)."""
+    if hasattr(attn, "project_qkv"):
+        return attn.project_qkv(x)
+    return attn.q(x), attn.k(x), attn.v(x)
+
+
+def static_decode_attention(attn, x, kv_cache, layer_idx, cos, sin, pos):
+    """One decode token (x: B, 1, C) through ``attn`` with its position ``pos``
+    a device tensor: the cache row is written with ``index_copy_`` and the
+    softmax runs over the whole static cache with a mask computed on the
+    device, so nothing in it depends on a host-side position (what a CUDA graph
+    replayed at every position needs).  Same result as the engine's T == 1
+    path (engine/attention.py:119-163)."""
+    B = x.shape[0]
+    H, KV, D = attn.num_heads, attn.num_kv_heads, attn.head_dim
+    qf, kf, vf = _project_qkv(attn, x)
+    q = attn.q_norm(qf.reshape(B, 1, H, D)).transpose(1, 2)
+    k = attn.k_norm(kf.reshape(B, 1, KV, D)).transpose(1, 2)
+    v = vf.reshape(B, 1, KV, D).transpose(1, 2)
+    q, k = rope(q, cos, sin), rope(k, cos, sin)
+    kc, vc = kv_cache.k[layer_idx][:B], kv_cache.v[layer_idx][:B]
+    kc.index_copy_(2, pos, k.to(kc.dtype))
+    vc.index_copy_(2, pos, v.to(vc.dtype))
+    S = kc.shape[2]
+    mask = (torch.arange(S, device=x.device) <= pos).view(1, 1, 1, S)
+    a = F.scaled_dot_product_attention(q, kc, vc, attn_mask=mask, enable_gqa=H != KV)
+    return attn.o(a.transpose(1, 2).reshape(B, 1, H * D))
+
+
 class Attention(nn.Module):
     """Eager GQA attention with QK-norm and RoPE (engine/attention.py:79-163)."""
 
@@ -184,6 +215,20 @@ class Qwen3Model(nn.Module):
         kv_cache.cur_len = start_pos + T
         return logits
 
+    def forward_static(self, input_ids: torch.Tensor, kv_cache: KVCache, pos: torch.Tensor) -> torch.Tensor:
+        """One decode step (input_ids: B, 1) at the position held in the device
+        tensor ``pos`` (shape (1,), int64): the same blocks as ``forward``, with
+        the RoPE rows picked and the cache written on the device
+        (``static_decode_attention``), so one captured CUDA graph serves every
+        position.  Does not touch ``kv_cache.cur_len``."""
+        h = self.embed(input_ids)
+        cos = self.rope_cos.index_select(0, pos).to(h.dtype)
+        sin = self.rope_sin.index_select(0, pos).to(h.dtype)
+        for i, blk in enumerate(self.layers):
+            h = h + static_decode_attention(blk.attn, blk.norm1(h), kv_cache, i, cos, sin, pos)
+            h = h + blk.ffn(blk.norm2(h))
+        return self.lm_head(self.final_norm(h))
+
     def alloc_cache(self, max_seq_len, *, max_batch=1, dtype=None, device=None) -> KVCache:
         p = self.lm_head.weight
         return KVCache.alloc(num_layers=len(self.layers), max_batch=max_batch,
@@ -227,6 +272,44 @@ class Qwen3Model(nn.Module):
             return self.final_norm(h) @ self.lm_head.weight.float().T
         finally:
             torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+class GraphedDecodeStep:
+    """A whole decode step of ``model`` (every layer, the LM head) captured once
+    as a CUDA graph and replayed at every position: the token ids and the
+    position are copied into static device buffers, then one graph launch
+    replaces the step's hundreds of kernel launches from Python (the dispatch
+    overhead the engine's own profiling names as the end-to-end blocker,
+    bench/profile.py:412-420).
+
+    ``step = GraphedDecodeStep(model, cache, batch)`` after the prefill;
+    ``logits = step(ids, pos)`` for each new token (ids: (batch, 1) on the
+    device).  The returned logits live in a static buffer overwritten by the
+    next call.  Building the graph runs the step once at ``cache.cur_len``,
+    the row the first real step writes anyway."""
+
+    def __init__(self, model: Qwen3Model, kv_cache: KVCache, batch: int) -> None:
+        dev = model.lm_head.weight.device
+        self.model, self.cache = model, kv_cache
+        self.ids = torch.zeros(batch, 1, dtype=torch.long, device=dev)
+        self.pos = torch.full((1,), kv_cache.cur_len, dtype=torch.long, device=dev)
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s), torch.inference_mode():  # first-call set-up outside the capture
+            model.forward_static(self.ids, kv_cache, self.pos)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph), torch.inference_mode():
+            self.logits = model.forward_static(self.ids, kv_cache, self.pos)
+
+    def __call__(self, ids: torch.Tensor, pos: int) -> torch.Tensor:
+        if pos >= self.cache.k[0].shape[2]:
+            raise ValueError(f"position {pos} is past the cache ({self.cache.k[0].shape[2]} rows)")
+        self.ids.copy_(ids)
+        self.pos.fill_(pos)
+        self.graph.replay()
+        self.cache.cur_len = pos + 1
+        return self.logits
 
 
 def greedy(logits: torch.Tensor) -> torch.Tensor:

@@ -74,3 +74,31 @@ def test_swap_kernels_on_eager_model():
         q = m(ids, m.alloc_cache(16, max_batch=2), start_pos=0).float()
     assert ((q - r).norm() / r.norm()).item() < 2e-2
     assert ((q - eager).norm() / eager.norm()).item() < 0.2  # int8 rounding of the weights
+
+
+def test_graphed_decode_step_matches_eager():
+    """GraphedDecodeStep: one CUDA graph of the whole decode step, replayed at
+    successive positions, against eager decode steps on a separate cache."""
+    import dataclasses
+    from llms_b200.kernels import apply_linear_kernels, apply_triton_kernels
+    from llms_b200.qwen3 import QWEN3_4B, GraphedDecodeStep, Qwen3Model
+    from tests.conftest import bf16_check
+    shape = dataclasses.replace(QWEN3_4B, num_hidden_layers=2, vocab_size=512)
+    torch.manual_seed(0)
+    m = Qwen3Model(shape).to("cuda", torch.bfloat16).eval()
+    for p in m.parameters():
+        torch.nn.init.normal_(p, std=0.02)
+    apply_triton_kernels(m)
+    apply_linear_kernels(m)
+    ids = torch.randint(0, 512, (2, 20), device="cuda")
+    nxt = torch.randint(0, 512, (3, 2, 1), device="cuda")
+    with torch.inference_mode():
+        ca, cb = m.alloc_cache(64, max_batch=2), m.alloc_cache(64, max_batch=2)
+        m(ids, ca, start_pos=0)
+        m(ids, cb, start_pos=0)
+        step = GraphedDecodeStep(m, cb, batch=2)
+        for i in range(3):
+            ref = m(nxt[i], ca, start_pos=20 + i).float()
+            got = step(nxt[i], 20 + i).float()
+            bf16_check(got.cpu().numpy(), ref.cpu().numpy(), max_abs=5e-2, rel_l2=2e-2)
+    assert cb.cur_len == 23

@@ -143,3 +143,22 @@ def test_column_shards_gather_to_full_output_gloo():
         p.join(timeout=60)
         assert p.exitcode == 0
     assert err < 1e-4
+
+
+def test_forward_static_matches_forward_on_cpu():
+    """The device-position decode step (what a CUDA graph replays at every
+    position) gives the engine's decode result, step after step."""
+    m = tiny().eval()
+    for p in m.parameters():
+        torch.nn.init.normal_(p, std=0.2)
+    ids = torch.randint(0, 64, (2, 6))
+    with torch.no_grad():
+        ca, cb = m.alloc_cache(12, max_batch=2), m.alloc_cache(12, max_batch=2)
+        m(ids, ca, start_pos=0)
+        m(ids, cb, start_pos=0)
+        for step in range(4):
+            nxt = torch.randint(0, 64, (2, 1))
+            ref = m(nxt, ca, start_pos=6 + step)
+            got = m.forward_static(nxt, cb, torch.tensor([6 + step]))
+            torch.testing.assert_close(got, ref, rtol=1e-5, atol=1e-5)
+        torch.testing.assert_close(cb.k[1][:, :, :10], ca.k[1][:, :, :10])
