@@ -25,7 +25,9 @@ suite : (rank 0, N = 1) the other BASELINE sub-metrics measured in the same
         repeat_interleave + SDPA (gqa_decode_*), the MLA fused Q + latent
         projection against three cuBLAS Linears (mla_q_latent_proj_*), and
         the Qwen3-8B int8 decode step with o / down on this library or on
-        cuBLAS (qwen3_8b_int8_decode_*).
+        cuBLAS (qwen3_8b_int8_decode_*), and a real decode loop at batch 1
+        (positions advancing) dispatched eagerly or as one CUDA graph per
+        step (qwen3_8b_int8_decode_loop_b1).
 mla_decode_b32_l32768_sharded : (N > 1) MLA decode at B = 32, L = 32768 split
         by batch row across the ranks, whole-job GB/s (max-over-ranks time).
 qwen3_8b_int8_decode_b*_sharded : (N > 1) the Qwen3-8B int8 decode step with
@@ -677,6 +679,44 @@ def mla_sharded(rank, world, steps=10):
             "bytes_note": "512*B*L latent + 512*B*L RoPE'd-key side-band + 32*B*L k-RMS side-band + weights + q/out"}
 
 
+def decode_loop(model, prompt, steps=32):
+    """A real decode loop at batch 1 (positions advancing, one cache row per
+    token) two ways: each step dispatched eagerly from Python, and each step one
+    replay of a GraphedDecodeStep (the whole step as one CUDA graph).  Wall
+    time per token over `steps` tokens after a warm-up, host-synchronised once
+    at the end; both loops feed back the greedy token on the device."""
+    from llms_b200.qwen3 import GraphedDecodeStep, greedy
+
+    g = torch.Generator(device="cuda").manual_seed(7)
+    ids = torch.randint(0, model.shape.vocab_size, (1, prompt), generator=g, device="cuda")
+    out = {}
+    with torch.inference_mode():
+        for mode in ("eager", "graph"):
+            cache = model.alloc_cache(prompt + 2 * steps + 8, max_batch=1)
+            logits = model(ids, cache, start_pos=0)[:, -1:]
+            tok = greedy(logits)
+            step = GraphedDecodeStep(model, cache, batch=1) if mode == "graph" else None
+            pos = prompt
+            for _ in range(4):  # warm-up tokens
+                logits = step(tok, pos) if step else model(tok, cache, start_pos=pos)
+                tok = greedy(logits[:, -1:] if logits.dim() == 3 else logits)
+                pos += 1
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(steps):
+                logits = step(tok, pos) if step else model(tok, cache, start_pos=pos)
+                tok = greedy(logits[:, -1:] if logits.dim() == 3 else logits)
+                pos += 1
+            torch.cuda.synchronize()
+            out[f"{mode}_ms_per_token"] = (time.perf_counter() - t0) / steps * 1e3
+            out[f"{mode}_last_token"] = int(tok.reshape(-1)[0].item())
+            del step, cache
+    out["tok/s_eager"] = 1e3 / out["eager_ms_per_token"]
+    out["tok/s_graph"] = 1e3 / out["graph_ms_per_token"]
+    out["same_tokens"] = out["eager_last_token"] == out["graph_last_token"]
+    return out
+
+
 def qwen3_8b_int8_decode(batches=(1, 16, 64), prompt=16):
     """a Qwen3-8B-shaped (36 layers, random init) decode
     step with int8 fused QKV / gate-up (per-row scales), bf16 elsewhere.
@@ -727,6 +767,10 @@ def qwen3_8b_int8_decode(batches=(1, 16, 64), prompt=16):
     cublas = {B: measure(B)[0] for B in batches}
     apply_linear_kernels(model)
     res = {}
+    try:
+        res["qwen3_8b_int8_decode_loop_b1"] = decode_loop(model, prompt)
+    except Exception as e:  # noqa: BLE001 -- reported, the other keys stay
+        res["qwen3_8b_int8_decode_loop_b1_error"] = f"{type(e).__name__}: {e}"[:300]
     for B in batches:
         sec, chk = measure(B)
         res[f"qwen3_8b_int8_decode_b{B}"] = {
