@@ -273,7 +273,10 @@ int b200mm_mla_decode(const b200mm_mla_shape* shape,
  *     and launches nothing (b200mm_mla_decode_workspace_size gives the need).
  *   - The first call on a device looks up the array's device address on that
  *     device (cudaGetSymbolAddress, the device current at the call); make that
- *     first call before any stream capture.
+ *     first call before any stream capture.  The looked-up address is kept
+ *     for the life of the process: after cudaDeviceReset (or anything else
+ *     that tears down the device's primary context) it is stale, so do not
+ *     call this entry point on a device after resetting it.
  *   - The array is shared by every call and keeps the last call's contents:
  *     two calls that can overlap on the GPU (different streams, or different
  *     host threads without ordering) race on it.  Calls on one stream are

@@ -10,12 +10,26 @@ and then multiplies by the weight (engine/attention.py:20-33); RoPE uses the
 from __future__ import annotations
 
 import torch
+from torch import nn
 
 
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     xf = x.float()
     xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
     return weight * xf.to(x.dtype)
+
+
+class RMSNorm(nn.Module):
+    """Parameter-compatible with the engine's RMSNorm (``weight``, ``eps``;
+    engine/attention.py:20-33); forward is :func:`rms_norm`."""
+
+    def __init__(self, dim: int, eps: float = 1e-6) -> None:
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(dim))
+        self.eps = eps
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return rms_norm(x, self.weight, self.eps)
 
 
 def rotate_half(x: torch.Tensor) -> torch.Tensor:

@@ -14,7 +14,7 @@ import torch.nn.functional as F
 from torch import nn
 
 from .. import _capi
-from ._eager import rope
+from ._eager import RMSNorm, rope
 
 
 def _check_qkv_args(x: torch.Tensor, W_qkv: torch.Tensor, n_q: int, n_k: int) -> None:
@@ -74,20 +74,6 @@ def triton_fused_qkv(
     return q, k, v
 
 
-class _RMSNorm(nn.Module):
-    """Parameter-compatible stand-in for the engine's RMSNorm (``weight``, ``eps``)."""
-
-    def __init__(self, dim: int, eps: float = 1e-6) -> None:
-        super().__init__()
-        self.weight = nn.Parameter(torch.ones(dim))
-        self.eps = eps
-
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
-        xf = x.float()
-        xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
-        return self.weight * xf.to(x.dtype)
-
-
 class TritonAttention(nn.Module):
     """Drop-in for the engine's GQA ``Attention`` whose q/k/v projections run
     as one fused B200 launch against a pre-concatenated ``W_qkv``.
@@ -107,8 +93,8 @@ class TritonAttention(nn.Module):
         self.n_k = num_kv_heads * head_dim
         self.W_qkv = nn.Parameter(torch.empty(self.n_q + 2 * self.n_k, hidden_size), requires_grad=False)
         self.o = nn.Linear(num_heads * head_dim, hidden_size, bias=False)
-        self.q_norm = _RMSNorm(head_dim, eps=rms_eps)
-        self.k_norm = _RMSNorm(head_dim, eps=rms_eps)
+        self.q_norm = RMSNorm(head_dim, eps=rms_eps)
+        self.k_norm = RMSNorm(head_dim, eps=rms_eps)
         # the engine Attention's swappable single-query op (engine/attention.py:101-105)
         self.decode_attn_op = None
 

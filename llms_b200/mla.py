@@ -36,7 +36,7 @@ import torch.nn.functional as F
 from torch import nn
 
 from . import _capi
-from .kernels._eager import rotate_half
+from .kernels._eager import RMSNorm, rotate_half
 from .kernels.linear import b200_linear
 
 
@@ -162,18 +162,6 @@ def mla_decode(q: torch.Tensor, c_kv: torch.Tensor, kz: torch.Tensor | None, ksc
 # ---------------------------------------------------------------------------
 # drop-in module
 # ---------------------------------------------------------------------------
-class _RMSNorm(nn.Module):
-    def __init__(self, dim: int, eps: float) -> None:
-        super().__init__()
-        self.weight = nn.Parameter(torch.ones(dim))
-        self.eps = eps
-
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
-        xf = x.float()
-        xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
-        return self.weight * xf.to(x.dtype)
-
-
 def _sideband(kv_cache, layer_idx: int, KV: int, DR: int):
     """The side-bands of ``layer_idx`` (allocated on first use): fp32 ``kscale``
     [max_batch, S, KV], ``kz`` [max_batch, S, KV, DR] in the cache dtype (None
@@ -221,8 +209,8 @@ class B200MLAttention(nn.Module):
         self.uv = nn.Linear(rank, num_kv_heads * head_dim, bias=False)
         self.kr = nn.Linear(hidden_size, num_kv_heads * d_rope, bias=False) if d_rope > 0 else None
         self.o = nn.Linear(num_heads * head_dim, hidden_size, bias=False)
-        self.q_norm = _RMSNorm(head_dim, rms_eps)
-        self.k_norm = _RMSNorm(head_dim, rms_eps)
+        self.q_norm = RMSNorm(head_dim, rms_eps)
+        self.k_norm = RMSNorm(head_dim, rms_eps)
         if d_rope > 0:
             inv = rope_inv_freq(head_dim, d_rope, rope_theta)
             ang = torch.outer(torch.arange(max_position_embeddings, dtype=torch.float32), inv)
@@ -252,6 +240,9 @@ class B200MLAttention(nn.Module):
             setattr(out, name, getattr(eager, name))
         out.rope_cos = eager.rope_cos
         out.rope_sin = eager.rope_sin
+        # the wrapped module serves the prefill; kept outside the module tree
+        # (its parameters are already registered here under the same names)
+        out.__dict__["_b200_reference"] = eager
         return out
 
     # -- helpers ------------------------------------------------------------
@@ -301,9 +292,29 @@ class B200MLAttention(nn.Module):
 
     def forward(self, x: torch.Tensor, *, kv_cache, layer_idx: int, start_pos: int,
                 cos: torch.Tensor | None = None, sin: torch.Tensor | None = None) -> torch.Tensor:
+        """T == 1 (decode): the absorbed B200 kernels.  T > 1 (prefill): the
+        reference's reconstruct-then-SDPA math, on purpose -- the north-star
+        path is the decode step; a prefill writes the cache once and its
+        side-bands are filled lazily by the next decode.  When this module
+        wraps a reference ``MLAttention`` (``from_eager``), the prefill is
+        that module's own ``forward``.  There is no CPU path: CPU tensors and
+        dtypes the kernels do not take raise."""
         del cos, sin  # accepted for signature compatibility, as in the reference
-        if self.supports_fast_decode(x):
+        _capi.require_cuda(x)
+        if x.dtype not in _capi.DTYPE_CODES:
+            raise ValueError(f"B200MLAttention takes float32 / float16 / bfloat16 inputs, got {x.dtype}")
+        if x.shape[1] == 1:
             return self._decode(x, kv_cache=kv_cache, layer_idx=layer_idx, start_pos=start_pos)
+        return self._prefill(x, kv_cache=kv_cache, layer_idx=layer_idx, start_pos=start_pos)
+
+    def _prefill(self, x, *, kv_cache, layer_idx, start_pos):
+        # tokens rewritten here invalidate their side-band entries
+        lens = getattr(kv_cache, "_b200_kscale_len", None)
+        if lens is not None and layer_idx in lens:
+            lens[layer_idx] = min(lens[layer_idx], start_pos)
+        ref = self.__dict__.get("_b200_reference")
+        if ref is not None:
+            return ref(x, kv_cache=kv_cache, layer_idx=layer_idx, start_pos=start_pos)
         return self._eager(x, kv_cache=kv_cache, layer_idx=layer_idx, start_pos=start_pos)
 
     def _write_cache(self, x, kv_cache, layer_idx, start_pos, end):
@@ -348,10 +359,6 @@ class B200MLAttention(nn.Module):
         end = start_pos + T
         q = self.q_norm(self.q(x).view(B, T, H, D)).transpose(1, 2)
         self._write_cache(x, kv_cache, layer_idx, start_pos, end)
-        # tokens rewritten here invalidate their side-band entries
-        lens = getattr(kv_cache, "_b200_kscale_len", None)
-        if lens is not None and layer_idx in lens:
-            lens[layer_idx] = min(lens[layer_idx], start_pos)
         c = kv_cache.c_kv[layer_idx][:B, :end]
         v = self.uv(c).view(B, end, KV, D)
         parts = []

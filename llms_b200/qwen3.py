@@ -22,7 +22,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
-from .kernels._eager import rope
+from .kernels._eager import RMSNorm, rope
 from .kernels.quant import Int8Attention, Int8FFN, dequantize_per_row
 
 
@@ -42,20 +42,6 @@ class Qwen3Shape:
 
 QWEN3_8B = Qwen3Shape()
 QWEN3_4B = Qwen3Shape(hidden_size=2560, intermediate_size=9728)
-
-
-class RMSNorm(nn.Module):
-    """fp32 normalise, cast back, multiply by the weight (engine/attention.py:20-33)."""
-
-    def __init__(self, dim: int, eps: float) -> None:
-        super().__init__()
-        self.weight = nn.Parameter(torch.ones(dim))
-        self.eps = eps
-
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
-        xf = x.float()
-        xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
-        return self.weight * xf.to(x.dtype)
 
 
 @dataclass
@@ -116,7 +102,13 @@ def static_decode_attention(attn, x, kv_cache, layer_idx, cos, sin, pos):
     softmax runs over the whole static cache with a mask computed on the
     device, so nothing in it depends on a host-side position (what a CUDA graph
     replayed at every position needs).  Same result as the engine's T == 1
-    path (engine/attention.py:119-163)."""
+    path (engine/attention.py:119-163).
+
+    Two limits of this static form: the softmax reads the cache's whole
+    capacity (``max_seq_len`` rows, masked) at every position, so a step
+    costs time for the capacity, not the current length; and
+    ``attn.decode_attn_op`` is not used here (the GQA decode kernel takes the
+    length on the host), so a captured step runs torch's SDPA."""
     B = x.shape[0]
     H, KV, D = attn.num_heads, attn.num_kv_heads, attn.head_dim
     qf, kf, vf = _project_qkv(attn, x)
@@ -303,8 +295,11 @@ class GraphedDecodeStep:
             self.logits = model.forward_static(self.ids, kv_cache, self.pos)
 
     def __call__(self, ids: torch.Tensor, pos: int) -> torch.Tensor:
-        if pos >= self.cache.k[0].shape[2]:
-            raise ValueError(f"position {pos} is past the cache ({self.cache.k[0].shape[2]} rows)")
+        S = self.cache.k[0].shape[2]
+        if not 0 <= pos < S:
+            raise ValueError(f"position {pos} is outside the cache (rows 0..{S - 1})")
+        if tuple(ids.shape) != tuple(self.ids.shape):
+            raise ValueError(f"ids shape {tuple(ids.shape)} != the captured step's {tuple(self.ids.shape)}")
         self.ids.copy_(ids)
         self.pos.fill_(pos)
         self.graph.replay()
@@ -317,6 +312,97 @@ def greedy(logits: torch.Tensor) -> torch.Tensor:
     return logits.argmax(dim=-1)
 
 
+def _int8_block(shape: Qwen3Shape, device, dtype):
+    """An empty decoder block of int8 fused QKV / gate-up modules (buffers
+    ``q_qkv, s_qkv`` and ``qg, sg, qu, su``) with bf16 ``o`` / ``down``."""
+    C, I = shape.hidden_size, shape.intermediate_size
+    H, KV, D = shape.num_attention_heads, shape.num_key_value_heads, shape.head_dim
+    att = Int8Attention.__new__(Int8Attention)
+    nn.Module.__init__(att)
+    att.hidden_size, att.num_heads, att.num_kv_heads, att.head_dim = C, H, KV, D
+    att.n_q, att.n_k = H * D, KV * D
+    att.register_buffer("q_qkv", torch.empty(H * D + 2 * KV * D, C, device=device, dtype=torch.int8))
+    att.register_buffer("s_qkv", torch.empty(H * D + 2 * KV * D, device=device))
+    att.o = nn.Linear(H * D, C, bias=False, device=device, dtype=dtype)
+    att.q_norm = RMSNorm(D, shape.rms_norm_eps).to(device=device, dtype=dtype)
+    att.k_norm = RMSNorm(D, shape.rms_norm_eps).to(device=device, dtype=dtype)
+    att.decode_attn_op = None
+    ffn = Int8FFN.__new__(Int8FFN)
+    nn.Module.__init__(ffn)
+    for name in ("g", "u"):
+        ffn.register_buffer("q" + name, torch.empty(I, C, device=device, dtype=torch.int8))
+        ffn.register_buffer("s" + name, torch.empty(I, device=device))
+    ffn.down = nn.Linear(I, C, bias=False, device=device, dtype=dtype)
+    return att, ffn
+
+
+def _int8_skeleton(shape: Qwen3Shape, device, dtype) -> Qwen3Model:
+    m = Qwen3Model(shape, build_projections=False)
+    m.to(device=device, dtype=dtype)
+    for blk in m.layers:
+        blk.attn, blk.ffn = _int8_block(shape, device, dtype)
+    return m
+
+
+@torch.no_grad()
+def int8_model_from_state(state: dict, shape: Qwen3Shape, *, device="cuda", dtype=torch.bfloat16) -> Qwen3Model:
+    """A model of int8 fused QKV / gate-up blocks loaded from ``state``
+    (tensors or numpy arrays named as ``oracle.inputs.cfg5_model`` writes
+    them: ``layers.i.attn.q_qkv`` / ``s_qkv``, ``layers.i.ffn.qg`` / ``sg`` /
+    ``qu`` / ``su``, the dense ``embed``, ``attn.o``, ``ffn.down`` and
+    ``lm_head`` weights, optional norm weights).  Every parameter and buffer
+    of the model must be covered, except norm weights (default one)."""
+    m = _int8_skeleton(shape, device, dtype)
+    own = dict(m.named_parameters())
+    own.update(dict(m.named_buffers()))
+    own = {k: v for k, v in own.items() if not k.startswith("rope_")}
+    missing = [k for k in own if k not in state and "norm" not in k]
+    unknown = [k for k in state if k not in own]
+    if missing or unknown:
+        raise ValueError(f"state mismatch: missing={missing[:8]}, unexpected={unknown[:8]}")
+    for k, v in state.items():
+        t = torch.as_tensor(v)
+        own[k].copy_(t.to(own[k].dtype) if t.dtype != own[k].dtype else t)
+    return m.eval()
+
+
+@torch.no_grad()
+def dequantized_dense_model(model: Qwen3Model) -> Qwen3Model:
+    """The reference engine's arithmetic for an int8 model: every int8 fused
+    projection dequantised (``W = q * s``), rounded to the model dtype and
+    split back into the engine's q / k / v and gate / up ``nn.Linear``s
+    (engine/attention.py:95-98, engine/model.py:30-32); ``o``, ``down``,
+    norms, embedding and LM head shared with ``model``."""
+    shape, p = model.shape, model.lm_head.weight
+    out = Qwen3Model(shape, build_projections=False)
+    out.to(device=p.device, dtype=p.dtype)
+    out.embed, out.lm_head, out.final_norm = model.embed, model.lm_head, model.final_norm
+    nq = shape.num_attention_heads * shape.head_dim
+    nk = shape.num_key_value_heads * shape.head_dim
+    for src, dst in zip(model.layers, out.layers):
+        a, f = src.attn, src.ffn
+        att = Attention.__new__(Attention)
+        nn.Module.__init__(att)
+        att.num_heads, att.num_kv_heads, att.head_dim = a.num_heads, a.num_kv_heads, a.head_dim
+        W = dequantize_per_row(a.q_qkv, a.s_qkv).to(p.dtype)
+        for name, w in zip(("q", "k", "v"), W.split([nq, nk, nk])):
+            setattr(att, name, nn.Linear(w.shape[1], w.shape[0], bias=False, device=p.device, dtype=p.dtype))
+            getattr(att, name).weight.copy_(w)
+        del W
+        att.o, att.q_norm, att.k_norm, att.decode_attn_op = a.o, a.q_norm, a.k_norm, None
+        ffn = FFN.__new__(FFN)
+        nn.Module.__init__(ffn)
+        for name, (q, s) in (("gate", (f.qg, f.sg)), ("up", (f.qu, f.su))):
+            w = dequantize_per_row(q, s).to(p.dtype)
+            setattr(ffn, name, nn.Linear(w.shape[1], w.shape[0], bias=False, device=p.device, dtype=p.dtype))
+            getattr(ffn, name).weight.copy_(w)
+            del w
+        ffn.down = f.down
+        dst.norm1, dst.norm2 = src.norm1, src.norm2
+        dst.attn, dst.ffn = att, ffn
+    return out.eval()
+
+
 @torch.no_grad()
 def synthetic_int8_model(shape: Qwen3Shape = QWEN3_8B, *, seed: int = 4, device="cuda",
                          dtype=torch.bfloat16) -> Qwen3Model:
@@ -324,39 +410,22 @@ def synthetic_int8_model(shape: Qwen3Shape = QWEN3_8B, *, seed: int = 4, device=
     with per-output-row scales ~ U(1e-4, 1e-3); everything else (embedding,
     o, down, LM head) bf16 ~ N(0, 0.02), norms 1.  Seeded on `device`."""
     g = torch.Generator(device=device).manual_seed(seed)
-    m = Qwen3Model(shape, build_projections=False)
-    m.to(device=device, dtype=dtype)
-    C, I = shape.hidden_size, shape.intermediate_size
-    H, KV, D = shape.num_attention_heads, shape.num_key_value_heads, shape.head_dim
+    m = _int8_skeleton(shape, device, dtype)
 
     def normal_(t):
         t.copy_(torch.randn(t.shape, generator=g, device=device, dtype=torch.float32) * 0.02)
 
-    def int8(n, k):
-        q = torch.randint(-127, 128, (n, k), generator=g, device=device, dtype=torch.int8)
-        s = torch.rand(n, generator=g, device=device) * 9e-4 + 1e-4
-        return q, s
+    def int8_(q, s):
+        q.copy_(torch.randint(-127, 128, q.shape, generator=g, device=device, dtype=torch.int8))
+        s.copy_(torch.rand(s.shape, generator=g, device=device) * 9e-4 + 1e-4)
 
     normal_(m.embed.weight)
     normal_(m.lm_head.weight)
     for blk in m.layers:
-        att = Int8Attention.__new__(Int8Attention)
-        nn.Module.__init__(att)
-        att.hidden_size, att.num_heads, att.num_kv_heads, att.head_dim = C, H, KV, D
-        att.n_q, att.n_k = H * D, KV * D
-        q, s = int8(H * D + 2 * KV * D, C)
-        att.register_buffer("q_qkv", q)
-        att.register_buffer("s_qkv", s)
-        att.o = nn.Linear(H * D, C, bias=False).to(device=device, dtype=dtype)
+        att, ffn = blk.attn, blk.ffn
+        int8_(att.q_qkv, att.s_qkv)
         normal_(att.o.weight)
-        att.q_norm = RMSNorm(D, shape.rms_norm_eps).to(device=device, dtype=dtype)
-        att.k_norm = RMSNorm(D, shape.rms_norm_eps).to(device=device, dtype=dtype)
-        ffn = Int8FFN.__new__(Int8FFN)
-        nn.Module.__init__(ffn)
-        for name, (qq, ss) in (("g", int8(I, C)), ("u", int8(I, C))):
-            ffn.register_buffer("q" + name, qq)
-            ffn.register_buffer("s" + name, ss)
-        ffn.down = nn.Linear(I, C, bias=False).to(device=device, dtype=dtype)
+        int8_(ffn.qg, ffn.sg)
+        int8_(ffn.qu, ffn.su)
         normal_(ffn.down.weight)
-        blk.attn, blk.ffn = att, ffn
     return m.eval()

@@ -42,13 +42,19 @@ def cpu_model() -> str:
 class DecodeProjections:
     """Weights of ``n_layers`` synthetic Qwen3-4B layers (bf16, N(0, 0.02))."""
 
-    def __init__(self, n_layers: int = 2, M: int = 1, seed: int = 0, dtype=torch.bfloat16):
+    def __init__(self, n_layers: int = 2, M: int = 1, seed: int = 0, dtype=torch.bfloat16, n_random: int = 2):
+        """Layers past the first ``n_random`` are clones of those (distinct
+        memory, same values): the weight stream, not the values, sets the time,
+        and drawing 4.7 GB of normals would take longer than timing them."""
         g = torch.Generator().manual_seed(seed)
         H, nq, nk, N = QWEN3_4B["hidden"], QWEN3_4B["n_q"], QWEN3_4B["n_k"], QWEN3_4B["inter"]
         self.layers = []
-        for _ in range(n_layers):
-            mk = lambda r: (torch.randn(r, H, generator=g) * 0.02).to(dtype)
-            self.layers.append(dict(wq=mk(nq), wk=mk(nk), wv=mk(nk), wg=mk(N), wu=mk(N)))
+        for i in range(n_layers):
+            if i < n_random:
+                mk = lambda r: (torch.randn(r, H, generator=g) * 0.02).to(dtype)
+                self.layers.append(dict(wq=mk(nq), wk=mk(nk), wv=mk(nk), wg=mk(N), wu=mk(N)))
+            else:
+                self.layers.append({k: v.clone() for k, v in self.layers[i % n_random].items()})
         self.x = torch.randn(M, H, generator=g).to(dtype)
         self.M = M
 
@@ -65,6 +71,11 @@ class DecodeProjections:
         q, k, v = F.linear(x, w["wq"]), F.linear(x, w["wk"]), F.linear(x, w["wv"])
         y = F.silu(F.linear(x, w["wg"])) * F.linear(x, w["wu"])
         return q, k, v, y
+
+    def run_step(self):
+        """One decode pass: every layer's QKV and gate-up projections."""
+        for i in range(len(self.layers)):
+            self.run_layer(i)
 
 
 def time_decode_projections(seconds: float = 10.0, M: int = 1, n_layers: int = 2, threads: int | None = None):

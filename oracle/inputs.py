@@ -90,3 +90,54 @@ def cfg5_layer(seed: int = 4, M: int = 1, K: int = 4096, n_q=4096, n_k=1024, int
     gu_q, gu_s = int8_weight(rng, 2 * inter, K)
     return dict(x=x, qkv_q=qkv_q, qkv_s=qkv_s, gate_q=gu_q[:inter], gate_s=gu_s[:inter],
                 up_q=gu_q[inter:], up_s=gu_s[inter:])
+
+
+def cfg5_model(layers: int = 2, vocab: int = 4096, seed: int = 4, hidden: int = 4096, n_q: int = 4096,
+               n_k: int = 1024, inter: int = 12288):
+    """Weights of a Qwen3-8B-shaped model (config 5) with ``layers`` decoder
+    blocks and a ``vocab``-row embedding / LM head, as a state dict of numpy
+    arrays named like the engine's modules (engine/model.py:40-106): int8
+    fused QKV ``layers.i.attn.q_qkv`` [n_q + 2 n_k, hidden] and gate / up
+    ``layers.i.ffn.qg`` / ``qu`` [inter, hidden] with fp32 per-row scales
+    (``s_qkv``, ``sg``, ``su``); bf16-representable N(0, 0.02) ``embed``,
+    ``attn.o``, ``ffn.down`` and ``lm_head``; RMSNorm weights one."""
+    rng = np.random.default_rng(seed)
+    st = {"embed.weight": round_bf16(_normal(rng, (vocab, hidden), 0.02))}
+    for i in range(layers):
+        p = f"layers.{i}."
+        st[p + "attn.q_qkv"], st[p + "attn.s_qkv"] = int8_weight(rng, n_q + 2 * n_k, hidden)
+        st[p + "attn.o.weight"] = round_bf16(_normal(rng, (hidden, n_q), 0.02))
+        st[p + "ffn.qg"], st[p + "ffn.sg"] = int8_weight(rng, inter, hidden)
+        st[p + "ffn.qu"], st[p + "ffn.su"] = int8_weight(rng, inter, hidden)
+        st[p + "ffn.down.weight"] = round_bf16(_normal(rng, (hidden, inter), 0.02))
+    st["lm_head.weight"] = round_bf16(_normal(rng, (vocab, hidden), 0.02))
+    return st
+
+
+def cfg5_tokens(batch: int, prompt: int, vocab: int, seed: int = 104):
+    """Prompt ids [batch, prompt] and the next token ids [batch, 1]."""
+    rng = np.random.default_rng(seed)
+    ids = rng.integers(0, vocab, size=(batch, prompt + 1), dtype=np.int64)
+    return ids[:, :prompt], ids[:, prompt:]
+
+
+def mla_module(hidden: int = 2560, seed: int = 9, H=32, KV=8, D=128, DR=32, R=256):
+    """Weights of one latent-attention layer at the Qwen3-4B MLA point, named
+    as the reference ``MLAttention``'s state dict (engine/mla.py:134-150):
+    projections N(0, 0.02) except ``uk_nope`` / ``uv`` N(0, 1/16) (std 1/4),
+    ``q_norm`` one, ``k_norm`` 1 + N(0, 0.1); bf16-representable."""
+    rng = np.random.default_rng(seed)
+    w = lambda n, k, std: round_bf16(_normal(rng, (n, k), std))
+    st = {"q.weight": w(H * D, hidden, 0.02), "dkv.weight": w(R, hidden, 0.02),
+          "uk_nope.weight": w(KV * (D - DR), R, 0.25), "uv.weight": w(KV * D, R, 0.25),
+          "kr.weight": w(KV * DR, hidden, 0.02), "o.weight": w(hidden, H * D, 0.02),
+          "q_norm.weight": np.ones(D, np.float32),
+          "k_norm.weight": round_bf16(1.0 + _normal(rng, (D,), 0.1))}
+    return st
+
+
+def mla_steps(B: int = 2, prefill: int = 20, decode: int = 3, hidden: int = 2560, seed: int = 10):
+    """Layer inputs: a prefill block [B, prefill, hidden] then ``decode``
+    single-token inputs [decode, B, 1, hidden], N(0, 1), bf16-representable."""
+    rng = np.random.default_rng(seed)
+    return round_bf16(_normal(rng, (B, prefill, hidden))), round_bf16(_normal(rng, (decode, B, 1, hidden)))

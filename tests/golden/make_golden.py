@@ -18,6 +18,17 @@ against.  Values are captured with forward hooks on the reference modules:
     ``MLAttention.forward`` (engine/mla.py:195-265), T == 1;
   * ``down``: the input and output of ``FFN.down`` inside ``FFN.forward``
     (engine/model.py:37);
+  * Qwen3-8B int8 decode step: the logits and ``greedy`` argmax
+    (engine/sampler.py:17-19) of the reference ``Qwen3Model``
+    (engine/model.py:76-150), built from a synthetic ``PretrainedConfig``
+    (pattern tests/_tiny.py:35-49) at the 8B widths with 2 layers and a
+    4096-row vocabulary, its int8 projections dequantised (W = q * s), after a
+    prefill; the weights are ``oracle.inputs.cfg5_model`` (regenerated, not
+    stored);
+  * MLA module steps: the outputs of the reference ``MLAttention``
+    (engine/mla.py:173-265) at the Qwen3-4B MLA point over a 20-token prefill
+    and three decode steps on the same cache (weights and inputs from
+    ``oracle.inputs.mla_module`` / ``mla_steps``);
   * GQA decode: the input and output of ``o`` of ``Attention.forward`` on its default
     single-query path (repeat_interleave + SDPA, engine/attention.py:147-150),
     and the q / K / V that path sees, captured through the module's own decode
@@ -44,7 +55,8 @@ sys.path.insert(0, str(REF / "src"))
 from engine.attention import Attention, RMSNorm, build_rope_tables  # noqa: E402
 from engine.kv_cache import KVCache  # noqa: E402
 from engine.mla import MLAKVCache, MLAttention  # noqa: E402
-from engine.model import FFN  # noqa: E402
+from engine.model import FFN, Qwen3Model  # noqa: E402
+from engine.sampler import greedy  # noqa: E402
 
 from oracle import inputs as I  # noqa: E402
 
@@ -190,6 +202,66 @@ def ref_gqa_decode(*, B, H, KV, D, n_prefill, seed, hidden=64):
                 o_w=attn.o.weight.detach().numpy().copy(), o_y=bo["v"].numpy().copy())
 
 
+def ref_qwen3_int8_step(*, layers=2, vocab=4096, batch=16, prompt=6):
+    """The reference engine's decode step on the dequantised config-5 model:
+    prefill ``prompt`` tokens, then one new token per row; returns the decode
+    step's logits [batch, vocab], their greedy argmax and the prefill's last
+    logits."""
+    from transformers import PretrainedConfig
+
+    cfg = PretrainedConfig(vocab_size=vocab, hidden_size=4096, num_hidden_layers=layers, num_attention_heads=32,
+                           num_key_value_heads=8, head_dim=128, intermediate_size=12288,
+                           max_position_embeddings=64, rms_norm_eps=1e-6, tie_word_embeddings=False,
+                           rope_theta=1e6, attention_bias=False)
+    st = I.cfg5_model(layers=layers, vocab=vocab)
+    deq = lambda q, s: torch.from_numpy(q.astype(np.float32) * st[s][:, None])
+    sd = {"embed.weight": torch.from_numpy(st["embed.weight"]),
+          "lm_head.weight": torch.from_numpy(st["lm_head.weight"]),
+          "final_norm.weight": torch.ones(4096)}
+    for i in range(layers):
+        p = f"layers.{i}."
+        w = deq(st[p + "attn.q_qkv"], p + "attn.s_qkv")
+        sd[p + "attn.q.weight"], sd[p + "attn.k.weight"], sd[p + "attn.v.weight"] = w.split([4096, 1024, 1024])
+        sd[p + "attn.o.weight"] = torch.from_numpy(st[p + "attn.o.weight"])
+        sd[p + "ffn.gate.weight"] = deq(st[p + "ffn.qg"], p + "ffn.sg")
+        sd[p + "ffn.up.weight"] = deq(st[p + "ffn.qu"], p + "ffn.su")
+        sd[p + "ffn.down.weight"] = torch.from_numpy(st[p + "ffn.down.weight"])
+        for n in ("norm1.weight", "norm2.weight"):
+            sd[p + n] = torch.ones(4096)
+        for n in ("attn.q_norm.weight", "attn.k_norm.weight"):
+            sd[p + n] = torch.ones(128)
+    model = Qwen3Model(cfg)
+    missing, unexpected = model.load_state_dict(sd, strict=False)
+    assert not unexpected and all("rope" in k for k in missing), (missing, unexpected)
+    model.eval()
+    ids, nxt = I.cfg5_tokens(batch, prompt, vocab)
+    cache = model.alloc_cache(prompt + 2, max_batch=batch, dtype=torch.float32, device="cpu")
+    with torch.no_grad():
+        pre = model(torch.from_numpy(ids), cache, start_pos=0)[:, -1]
+        logits = model(torch.from_numpy(nxt), cache, start_pos=prompt)[:, -1]
+    return dict(logits=logits.numpy().copy(), argmax=greedy(logits).numpy().astype(np.float32),
+                prefill_logits=pre.numpy().copy())
+
+
+def ref_mla_prefill_decode(*, B=2, prefill=20, decode=3, hidden=2560):
+    """The reference ``MLAttention`` (engine/mla.py:173-265) at the Qwen3-4B
+    MLA point (H 32, KV 8, D 128, d_rope 32, rank 256, theta 1e6) with the
+    weights of ``oracle.inputs.mla_module``: a prefill of ``prefill`` tokens,
+    then ``decode`` single-token steps on the same cache.  Returns the last
+    two prefill output rows and every decode step's output."""
+    mla = MLAttention(hidden_size=hidden, num_heads=32, num_kv_heads=8, head_dim=128, rms_eps=1e-6, rank=256,
+                      d_rope=32, max_position_embeddings=64, rope_theta=1e6, qk_norm_mode="single")
+    mla.load_state_dict({k: torch.from_numpy(v) for k, v in I.mla_module(hidden).items()})
+    x0, xs = I.mla_steps(B, prefill, decode, hidden)
+    cache = MLAKVCache.alloc(num_layers=1, max_batch=B, num_kv_heads=8, max_seq_len=prefill + decode + 1, rank=256,
+                             d_rope=32, dtype=torch.float32, device="cpu")
+    with torch.no_grad():
+        pre = mla(torch.from_numpy(x0), kv_cache=cache, layer_idx=0, start_pos=0)
+        outs = [mla(torch.from_numpy(xs[i]), kv_cache=cache, layer_idx=0, start_pos=prefill + i)
+                for i in range(decode)]
+    return dict(prefill_tail=pre[:, -2:].numpy().copy(), decode=torch.stack(outs).numpy().copy())
+
+
 def main() -> None:
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     out = {}
@@ -243,6 +315,12 @@ def main() -> None:
     for name, (B, H, KV, D, n) in gqa_cases.items():
         for k_, v_ in ref_gqa_decode(B=B, H=H, KV=KV, D=D, n_prefill=n, seed=11).items():
             out[f"{name}__{k_}"] = v_
+
+    for k_, v_ in ref_mla_prefill_decode().items():
+        out[f"mla_4b_module_steps__{k_}"] = v_
+
+    for k_, v_ in ref_qwen3_int8_step().items():
+        out[f"qwen3_8b_int8_l2__{k_}"] = v_
 
     np.savez_compressed(HERE / "golden.npz", **{k: np.asarray(v, np.float32) for k, v in out.items()})
     print(f"wrote {HERE / 'golden.npz'} with {len(out)} arrays")

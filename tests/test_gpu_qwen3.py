@@ -102,3 +102,51 @@ def test_graphed_decode_step_matches_eager():
             got = step(nxt[i], 20 + i).float()
             bf16_check(got.cpu().numpy(), ref.cpu().numpy(), max_abs=5e-2, rel_l2=2e-2)
     assert cb.cur_len == 23
+
+
+@pytest.fixture(scope="module")
+def golden_model():
+    """Config 5 at 2 layers / 4096 vocabulary on the device: the weights the
+    reference engine ran in tests/golden/make_golden.py."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from llms_b200.qwen3 import QWEN3_8B, dequantized_dense_model, int8_model_from_state
+    from oracle import inputs as I
+    shape = dataclasses.replace(QWEN3_8B, num_hidden_layers=2, vocab_size=4096, max_position_embeddings=64)
+    m = int8_model_from_state(I.cfg5_model(layers=2, vocab=4096), shape)
+    return m, dequantized_dense_model(m)
+
+
+def _decode_logits(model, ids, nxt):
+    with torch.inference_mode():
+        cache = model.alloc_cache(ids.shape[1] + 2, max_batch=ids.shape[0])
+        model(ids, cache, start_pos=0)
+        return model(nxt, cache, start_pos=ids.shape[1])[:, -1].float().cpu()
+
+
+def test_int8_step_matches_reference_engine(golden, golden_model):
+    """The int8 decode step (b200mm int8 QKV / gate-up, b200mm_linear o / down)
+    against the reference engine's fp32 logits (golden), next to the reference
+    engine's own bf16 arithmetic on the same weights (dequantised bf16
+    nn.Linear, torch kernels).  Bars: logits rel-L2 <= 1.25x the reference
+    bf16 path's; greedy argmax equal on every row whose fp32 top-2 gap exceeds
+    the reference bf16 path's largest logit error on that row, and at least
+    half the rows decided."""
+    import numpy as np
+    from llms_b200.kernels import apply_linear_kernels
+    from llms_b200.qwen3 import greedy
+    from oracle import inputs as I
+    m, dense = golden_model
+    ids, nxt = (torch.from_numpy(a).cuda() for a in I.cfg5_tokens(16, 6, 4096))
+    ref = torch.from_numpy(golden["qwen3_8b_int8_l2__logits"])
+    base = _decode_logits(dense, ids, nxt)
+    apply_linear_kernels(m)
+    ours = _decode_logits(m, ids, nxt)
+    rel = lambda a: ((a - ref).norm() / ref.norm()).item()
+    assert rel(ours) <= 1.25 * rel(base) + 1e-4, f"rel-L2 ours {rel(ours):.3e}, reference bf16 path {rel(base):.3e}"
+    top2 = ref.topk(2, dim=-1).values
+    decided = (top2[:, 0] - top2[:, 1]) > (base - ref).abs().amax(-1)
+    assert decided.sum().item() >= ref.shape[0] // 2, f"only {decided.sum().item()} of {ref.shape[0]} rows decided"
+    want = torch.from_numpy(golden["qwen3_8b_int8_l2__argmax"].astype(np.int64))
+    got = greedy(ours)
+    assert torch.equal(got[decided], want[decided]), f"argmax differs on {(got != want)[decided].sum().item()} rows"

@@ -97,3 +97,35 @@ def test_linear_down_and_o(golden):
         out = golden[f"{name}__out"]
         B, H, D = out.shape
         _close(O.linear(out.reshape(B, 1, H * D), golden[f"{name}__o_w"]), golden[f"{name}__o_y"], 1e-5, 1e-6)
+
+
+def test_mla_module_prefill_math_vs_reference(golden):
+    """B200MLAttention's restated prefill math (used when the module was not
+    built by wrapping a reference MLAttention) equals the reference module's
+    prefill on the same weights (CPU, fp32; the decode steps are checked on
+    the GPU in tests/test_gpu_mla.py)."""
+    import torch
+    from llms_b200.mla import B200MLAttention
+
+    class Cache:
+        def __init__(self, B, S):
+            self.c_kv = [torch.zeros(B, S, 256)]
+            self.k_rope_pre = [torch.zeros(B, S, 8, 32)]
+
+    m = B200MLAttention(hidden_size=2560, num_heads=32, num_kv_heads=8, head_dim=128, rms_eps=1e-6, rank=256,
+                        d_rope=32, max_position_embeddings=64, rope_theta=1e6)
+    m.load_state_dict({k: torch.from_numpy(v) for k, v in I.mla_module().items()})
+    x0, _ = I.mla_steps()
+    with torch.no_grad():
+        y = m._eager(torch.from_numpy(x0), kv_cache=Cache(2, 24), layer_idx=0, start_pos=0)
+    _close(y[:, -2:].numpy(), golden["mla_4b_module_steps__prefill_tail"], 1e-4, 1e-5)
+
+
+def test_mla_module_rejects_cpu_tensors():
+    """No CPU path: the drop-in module raises on CPU inputs."""
+    import torch
+    from llms_b200.mla import B200MLAttention
+    m = B200MLAttention(hidden_size=64, num_heads=4, num_kv_heads=2, head_dim=16, rms_eps=1e-6, rank=32,
+                        d_rope=8, max_position_embeddings=16, rope_theta=1e4)
+    with pytest.raises(RuntimeError, match="CPU"):
+        m(torch.zeros(1, 1, 64), kv_cache=None, layer_idx=0, start_pos=0)
