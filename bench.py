@@ -71,7 +71,8 @@ def parse_args():
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--no-suite", action="store_true", help="skip the per-op sub-metrics")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
-    p.add_argument("--profile-op", choices=["qkv", "gate_up", "qkv_w8", "gate_up_w8", "mla", "gqa", "down"],
+    p.add_argument("--profile-op", choices=["qkv", "gate_up", "qkv_w8", "gate_up_w8", "mla", "gqa", "down",
+                                            "mla_fill", "qwen3_step"],
                    help="run one op 3 times and exit (a small driver for ncu captures)")
     p.add_argument("--M", type=int, default=1, help="--profile-op: rows of x")
     p.add_argument("--B", type=int, default=32, help="--profile-op mla / gqa: batch")
@@ -89,7 +90,45 @@ def profile_op(args):
     torch.cuda.set_device(0)
     g = torch.Generator(device="cuda").manual_seed(0)
     bf = dict(device="cuda", dtype=torch.bfloat16, generator=g)
-    if args.profile_op == "mla":
+    if args.profile_op == "qwen3_step":
+        # the Qwen3-8B int8 decode step (config 5) at batch --B: a prefill,
+        # then three decode steps, each one replay of a CUDA graph of the
+        # whole step (what the bench times); ncu sees the graph's kernels
+        from llms_b200.kernels import apply_linear_kernels
+        from llms_b200.qwen3 import synthetic_int8_model
+        model = synthetic_int8_model(seed=4)
+        apply_linear_kernels(model)
+        B, P = args.B, 16
+        ids = torch.randint(0, model.shape.vocab_size, (B, P), device="cuda", generator=g)
+        nxt = torch.randint(0, model.shape.vocab_size, (B, 1), device="cuda", generator=g)
+        with torch.inference_mode():
+            cache = model.alloc_cache(P + 8, max_batch=B)
+            model(ids, cache, start_pos=0)
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                model(nxt, cache, start_pos=P)
+            torch.cuda.current_stream().wait_stream(s)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                model(nxt, cache, start_pos=P)
+            torch.cuda.synchronize()
+            for _ in range(3):
+                graph.replay()
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_op": args.profile_op, "ok": True}))
+        return
+    if args.profile_op == "mla_fill":  # side-band fill of a prefilled MLA cache (B x L tokens)
+        B, L, KV, D, DR, R = args.B, args.L, 8, 128, 32, 256
+        c = torch.randn(B, L, R, **bf)
+        kr = torch.randn(B, L, KV, DR, **bf)
+        wuk = torch.randn(KV, D - DR, R, **bf) * 0.25
+        kw, inv = torch.ones(D, device="cuda"), mla.rope_inv_freq(D, DR, 1e6, "cuda")
+        ks = torch.empty(B, L, KV, device="cuda")
+        kz = torch.empty(B, L, KV, DR, device="cuda", dtype=torch.bfloat16)
+        fn = lambda: mla.mla_append(c, kr, wuk, kw, inv, ks, kz, B=B, t0=0, t1=L, num_kv_heads=KV, head_dim=D,
+                                    eps=1e-6)
+    elif args.profile_op == "mla":
         B, L, H, KV, D, DR, R = args.B, args.L, 32, 8, 128, 32, 256
         c = torch.randn(B, L, R, **bf)
         kr = torch.randn(B, L, KV, DR, **bf)
@@ -496,7 +535,13 @@ def suite(job):
         kw = torch.ones(D, device="cuda")
         inv = mla.rope_inv_freq(D, DR, 1e6, "cuda")
         ks, kz = mla.mla_sidebands(c, kr, wuk, kw, inv, B=B, L=L, num_kv_heads=KV, head_dim=D, eps=1e-6)
-        del kr  # the decode step reads the latent and the two side-bands
+        # the side-band fill of a prefilled cache (every token of every row),
+        # as the first decode after a prefill runs it
+        fill = lambda: mla.mla_append(c, kr, wuk, kw, inv, ks, kz, B=B, t0=0, t1=L, num_kv_heads=KV, head_dim=D,
+                                      eps=1e-6)
+        g, _ = job.capture(fill)
+        fill_us = time_graph(g, 5, 2, 1) / 5 * 1e6
+        del g, kr  # the decode step reads the latent and the two side-bands
         ws = torch.empty(mla.workspace_bytes(B, H, KV, D, DR, R, L, torch.bfloat16), dtype=torch.uint8, device="cuda")
         o = torch.empty(B, H, D, device="cuda", dtype=torch.bfloat16)
         fn = lambda: mla.mla_decode(q, c, kz, ks, wuk, wuv, kw, inv, L=L, scale=D ** -0.5, eps=1e-6, out=o,
@@ -508,6 +553,11 @@ def suite(job):
         out[f"mla_b{B}_l{L}"] = {"us_per_step": per * 1e6, "GB/s": alg / per / 1e9, "launches": launches,
                                  "bytes_note": "512*B*L latent + 512*B*L RoPE'd-key side-band + 32*B*L k-RMS "
                                                "side-band + weights + q/out"}
+        fill_bytes = B * L * (512 + 512 + 512 + 32)  # read c, k_rope_pre; write kz, kscale
+        out[f"mla_sideband_fill_b{B}_l{L}"] = {
+            "us": fill_us, "x_decode_step": fill_us / (per * 1e6), "GB/s": fill_bytes / fill_us / 1e3,
+            "TFLOP/s": 2 * B * L * 256 * 768 / fill_us / 1e6,
+            "note": "kscale and kz for every cached token (tcgen05 contraction [B*L x 256] x [256 x 768])"}
         del g, c, kz, ks, ws
     # GQA decode attention (the engine's decode_attn_op seam) at Qwen3 shapes:
     # GB/s of the K/V cache read once per step, against the reference's own
@@ -633,18 +683,21 @@ def qwen3_8b_int8_decode_sharded(rank, world, batches=(1, 16, 64), prompt=16, st
     return res
 
 
-def mla_sharded(rank, world, steps=10):
-    """BASELINE configs[3] across GPUs: MLA decode at B = 32, L = 32768 split
-    by batch row (llms_b200.mla.batch_shard; no collective in the op), one
-    CUDA graph of one decode per rank, device time max over ranks; GB/s is
-    the whole job's algorithmic bytes over that time."""
+def mla_sharded(rank, world, B=32, steps=10):
+    """BASELINE configs[3] across GPUs: MLA decode at L = 32768 split by batch
+    row, and for batches smaller than the GPU count by KV group too
+    (llms_b200.mla.decode_shard; no collective in the op), one CUDA graph of
+    one decode per rank, device time max over ranks.  GB/s is the whole
+    job's algorithmic bytes (each cached token once) over that time; a group
+    split reads the latent of its rows on every GPU of the row, which the
+    per-rank byte count next to it shows."""
     from llms_b200 import mla
 
-    H, KV, D, DR, R, B, L = 32, 8, 128, 32, 256, 32, 32768
-    rows = mla.batch_shard(B, world, rank)
+    H, KV, D, DR, R, L = 32, 8, 128, 32, 256, 32768
+    rows, groups = mla.decode_shard(B, KV, world, rank)
     b = len(rows)
-    if b:
-        gg = torch.Generator(device="cuda").manual_seed(3 + 1000 * rank)
+    if b and len(groups):
+        gg = torch.Generator(device="cuda").manual_seed(3 + 1000 * rows.start)
         c = torch.randn(b, L, R, device="cuda", dtype=torch.bfloat16, generator=gg)
         kr = torch.randn(b, L, KV, DR, device="cuda", dtype=torch.bfloat16, generator=gg)
         wuk = torch.randn(KV, D - DR, R, device="cuda", dtype=torch.bfloat16, generator=gg) * 0.25
@@ -654,11 +707,9 @@ def mla_sharded(rank, world, steps=10):
         inv = mla.rope_inv_freq(D, DR, 1e6, "cuda")
         ks, kz = mla.mla_sidebands(c, kr, wuk, kw, inv, B=b, L=L, num_kv_heads=KV, head_dim=D, eps=1e-6)
         del kr
-        ws = torch.empty(mla.workspace_bytes(b, H, KV, D, DR, R, L, torch.bfloat16), dtype=torch.uint8,
-                         device="cuda")
-        o = torch.empty(b, H, D, device="cuda", dtype=torch.bfloat16)
-        fn = lambda: mla.mla_decode(q, c, kz, ks, wuk, wuv, kw, inv, L=L, scale=D ** -0.5, eps=1e-6, out=o,
-                                    workspace=ws)
+        local = range(0, b)
+        fn = lambda: mla.mla_decode_shard(q, c, kz, ks, wuk, wuv, kw, inv, rows=local, groups=groups, L=L,
+                                          scale=D ** -0.5, eps=1e-6)
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
@@ -669,15 +720,19 @@ def mla_sharded(rank, world, steps=10):
         with torch.cuda.graph(g):
             fn()
         sec = time_graph(g, steps, 3, world)
-    else:  # more ranks than batch rows: this rank idles but joins the timing
+        rank_bytes = b * L * (512 + (512 + 32) * len(groups) // KV)
+    else:  # no work for this rank: it idles but joins the timing
         class _Idle:
             def replay(self):
                 pass
         sec = time_graph(_Idle(), steps, 3, world)
+        rank_bytes = 0
     per = sec / steps
     alg = 1024 * B * L + 32 * B * L + 917504 + 512 * B
+    split = "batch rows" if B >= world else "batch rows x KV groups"
     return {"GB/s": alg / per / 1e9, "us_per_step": per * 1e6, "B": B, "L": L,
-            "split": f"batch rows over {world} GPUs (no collective in the op)",
+            "split": f"{split} over {world} GPUs (no collective in the op)",
+            "rank0_cache_bytes": rank_bytes if rank == 0 else None,
             "bytes_note": "512*B*L latent + 512*B*L RoPE'd-key side-band + 32*B*L k-RMS side-band + weights + q/out"}
 
 
@@ -824,6 +879,10 @@ def submetrics(suite_res):
         if r and "GB/s" in r:
             us = r.get("us_per_launch", r.get("us_per_step"))
             out[k] = {"GB/s": round(r["GB/s"], 1), "frac": round(r["GB/s"] / hbm, 3), "us": round(us, 2)}
+    r = suite_res.get("mla_sideband_fill_b32_l32768")
+    if r:
+        out["mla_sideband_fill_b32_l32768"] = {"us": round(r["us"], 1), "x_decode_step": round(r["x_decode_step"], 2),
+                                               "TFLOP/s": round(r["TFLOP/s"], 1)}
     for k in ("qkv_m2048", "gate_up_m2048"):
         r = suite_res.get(k)
         if r and "TFLOP/s" in r:
@@ -1005,6 +1064,10 @@ def main():
         # the sub-metrics next to the headline: a failure costs its own key only
         for key, fn in (("mla_decode_b32_l32768_sharded", lambda: {"mla_decode_b32_l32768_sharded":
                                                                     mla_sharded(rank, world)}),
+                        ("mla_decode_b8_l32768_sharded", lambda: {"mla_decode_b8_l32768_sharded":
+                                                                   mla_sharded(rank, world, B=8)}),
+                        ("mla_decode_b1_l32768_sharded", lambda: {"mla_decode_b1_l32768_sharded":
+                                                                   mla_sharded(rank, world, B=1)}),
                         ("qwen3_8b_int8_decode_sharded", lambda: qwen3_8b_int8_decode_sharded(rank, world))):
             try:
                 extra.update(fn())

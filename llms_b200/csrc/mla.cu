@@ -636,6 +636,7 @@ size_t mla_workspace_bytes(const b200mm_mla_shape& s, int64_t L) {
 }
 
 int mla_append_launch(const MlaAppendArgs& a) {
+  if (!g_force_generic.load(std::memory_order_relaxed) && mla_fill_tc_supported(a)) return mla_fill_tc_launch(a);
   if (a.s.dtype == B200MM_BF16) return append_t<__nv_bfloat16>(a);
   if (a.s.dtype == B200MM_F16) return append_t<__half>(a);
   return append_t<float>(a);

@@ -84,6 +84,12 @@ int mla_validate_shape(const b200mm_mla_shape& s);
 MlaWorkspace mla_plan(const b200mm_mla_shape& s, int64_t L, bool fast);
 size_t mla_workspace_bytes(const b200mm_mla_shape& s, int64_t L);
 int mla_append_launch(const MlaAppendArgs& a);
+
+// side-band fill on the tensor cores (R=256, D=128, DR=32, KV=8, 16-bit), for
+// ranges of at least kMlaFillTcMinTokens tokens per batch row
+constexpr int64_t kMlaFillTcMinTokens = 64;
+bool mla_fill_tc_supported(const MlaAppendArgs& a);
+int mla_fill_tc_launch(const MlaAppendArgs& a);
 int mla_decode_launch(const MlaDecodeArgs& a);
 
 // production-shape split kernel (R=256, D=128, DR=32, H=32, KV=8, 16-bit dtype)

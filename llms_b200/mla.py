@@ -68,6 +68,48 @@ def batch_shard(B: int, world: int, rank: int) -> range:
     return range(B * rank // world, B * (rank + 1) // world)
 
 
+def decode_shard(B: int, KV: int, world: int, rank: int) -> tuple[range, range]:
+    """Batch rows and KV groups of an MLA decode that GPU ``rank`` of ``world``
+    serves.  With ``B >= world``: a batch-row split (``batch_shard``), every
+    group.  With fewer rows than GPUs: the groups are split too -- ``gs``
+    group shards (the divisor of KV that keeps the most GPUs busy) times
+    ``world // gs`` row shards; rank r takes row shard ``r // gs`` and group
+    shard ``r % gs``.  A group shard reads the whole latent of its rows (the
+    latent is shared by every group) but only its groups' RoPE'd keys and
+    scales, and serves only those groups' heads.  No collective inside the
+    op; surplus ranks get empty ranges."""
+    if world < 1 or not 0 <= rank < world or B < 0 or KV < 1:
+        raise ValueError(f"bad shard request: B={B} KV={KV} world={world} rank={rank}")
+    if B >= world or B == 0:
+        return batch_shard(B, world, rank), range(KV)
+    # the divisor of KV that keeps the most GPUs busy (ties: fewer group
+    # shards, i.e. less replicated latent reading)
+    gs = max((d for d in range(1, KV + 1) if KV % d == 0 and d <= world),
+             key=lambda d: (min(world // d, B) * d, -d))
+    rs = world // gs
+    if rank >= rs * gs:
+        return range(0), range(0)
+    rows = batch_shard(B, rs, rank // gs)
+    gi = rank % gs
+    return rows, range(KV * gi // gs, KV * (gi + 1) // gs)
+
+
+def mla_decode_shard(q: torch.Tensor, c_kv: torch.Tensor, kz: torch.Tensor | None, kscale: torch.Tensor,
+                     w_uk: torch.Tensor | None, w_uv: torch.Tensor, k_norm_w: torch.Tensor,
+                     inv_freq: torch.Tensor | None, *, rows: range, groups: range, L: int, scale: float,
+                     eps: float) -> torch.Tensor:
+    """``mla_decode`` of batch rows ``rows`` and KV groups ``groups`` only
+    (``decode_shard``): the heads of those groups, ``(len(rows), hpg *
+    len(groups), D)``.  The slices are views (no copy): the side-bands keep
+    their token strides and the kernels read only the selected groups."""
+    KV, H = w_uv.shape[0], q.shape[1]
+    hpg = H // KV
+    r0, r1, g0, g1 = rows.start, rows.stop, groups.start, groups.stop
+    return mla_decode(q[r0:r1, g0 * hpg:g1 * hpg], c_kv[r0:r1], None if kz is None else kz[r0:r1, :, g0:g1],
+                      kscale[r0:r1, :, g0:g1], None if w_uk is None else w_uk[g0:g1], w_uv[g0:g1], k_norm_w,
+                      inv_freq, L=L, scale=scale, eps=eps)
+
+
 def workspace_bytes(B: int, H: int, KV: int, D: int, DR: int, R: int, L: int, dtype, eps: float = 1e-6) -> int:
     shp = _shape(B, H, KV, D, DR, R, dtype, eps)
     return int(_capi.lib.b200mm_mla_decode_workspace_size(ctypes.byref(shp), L))

@@ -219,3 +219,63 @@ def test_cfg4_large_sampled_rows(B, L):
     rows = sorted({0, B // 2, B - 1})
     sub = {k: (v[rows] if k in ("q", "c_kv", "k_rope_pre") else v) for k, v in d.items()}
     bf16_check(host(out)[rows], oracle_out(sub, L, dims))
+
+
+@pytest.mark.parametrize("B,S,t0,t1", [(3, 700, 0, 700), (2, 1000, 37, 901), (1, 300, 100, 164), (4, 4096, 0, 4096)])
+def test_sideband_fill_tensor_core_vs_generic(B, S, t0, t1):
+    """The tensor-core side-band fill (ranges of >= 64 tokens at the
+    production shape) against the scalar append kernel: kz to within one bf16
+    rounding, kscale within fp32 reassociation and against the oracle; tokens outside
+    [t0, t1) untouched."""
+    from llms_b200 import mla
+    KV, D, DR, R = 8, 128, 32, 256
+    g = torch.Generator(device="cuda").manual_seed(B * 1000 + t0)
+    c = torch.randn(B + 1, S, R, device="cuda", generator=g).to(torch.bfloat16)
+    kr = torch.randn(B + 1, S, KV, DR, device="cuda", generator=g).to(torch.bfloat16)
+    wuk = (torch.randn(KV, D - DR, R, device="cuda", generator=g) * 0.25).to(torch.bfloat16)
+    kw = 1 + 0.1 * torch.randn(D, device="cuda", generator=g)
+    inv = mla.rope_inv_freq(D, DR, 1e6, "cuda")
+    res = []
+    for generic in (False, True):
+        ks = torch.full((B + 1, S, KV), float("nan"), device="cuda")
+        kz = torch.full((B + 1, S, KV, DR), float("nan"), device="cuda", dtype=torch.bfloat16)
+        if generic:
+            with force_generic():
+                mla.mla_append(c, kr, wuk, kw, inv, ks, kz, B=B, t0=t0, t1=t1, num_kv_heads=KV, head_dim=D,
+                               eps=1e-6)
+        else:
+            mla.mla_append(c, kr, wuk, kw, inv, ks, kz, B=B, t0=t0, t1=t1, num_kv_heads=KV, head_dim=D, eps=1e-6)
+        torch.cuda.synchronize()
+        res.append((ks, kz))
+    (ks, kz), (ks_g, kz_g) = res
+    assert torch.isnan(ks[:, :t0]).all() and torch.isnan(ks[:, t1:]).all() and torch.isnan(ks[B:]).all()
+    assert torch.isnan(kz[:, :t0].float()).all() and torch.isnan(kz[B:].float()).all()
+    torch.testing.assert_close(ks[:B, t0:t1], ks_g[:B, t0:t1], rtol=2e-6, atol=0)
+    # same formula per element; the compiler may contract it differently: one bf16 rounding step at most
+    torch.testing.assert_close(kz[:B, t0:t1].float(), kz_g[:B, t0:t1].float(), rtol=2 ** -7, atol=1e-3)
+    e = O.mla_kv_scales(host(c[:B, t0:t1]), host(kr[:B, t0:t1]), host(wuk), 1e-6, 128)
+    np.testing.assert_allclose(host(ks[:B, t0:t1]), e, rtol=2e-5, atol=0)
+
+
+@pytest.mark.parametrize("B,world", [(1, 8), (3, 4), (2, 2)])
+def test_decode_shards_reassemble_full_decode(B, world):
+    """Every (row, group) shard of decode_shard, run one after another on one
+    GPU through mla_decode_shard, reassembles the unsharded decode."""
+    from llms_b200 import mla
+    dims = dict(H=32, KV=8, D=128, DR=32, R=256)
+    L = 700
+    d = I.cfg4(B, L, **dims)
+    c, kr = dev(d["c_kv"]), dev(d["k_rope_pre"])
+    wuk, wuv, q = dev(d["w_uk"]), dev(d["w_uv"]), dev(d["q"])
+    kw, inv = torch.ones(128, device="cuda"), mla.rope_inv_freq(128, 32, 1e6, "cuda")
+    ks, kz = mla.mla_sidebands(c, kr, wuk, kw, inv, B=B, L=L, num_kv_heads=8, head_dim=128, eps=1e-6)
+    full = mla.mla_decode(q, c, kz, ks, wuk, wuv, kw, inv, L=L, scale=128 ** -0.5, eps=1e-6)
+    got = torch.full_like(full, float("nan"))
+    for r in range(world):
+        rows, groups = mla.decode_shard(B, 8, world, r)
+        if len(rows) and len(groups):
+            part = mla.mla_decode_shard(q, c, kz, ks, wuk, wuv, kw, inv, rows=rows, groups=groups, L=L,
+                                        scale=128 ** -0.5, eps=1e-6)
+            got[rows.start:rows.stop, groups.start * 4:groups.stop * 4] = part
+    bf16_check(host(got), host(full).astype(np.float64))
+    bf16_check(host(got), oracle_out(d, L, dims))
