@@ -42,7 +42,7 @@ constexpr int gemv_min_blocks() {
 
 template <typename TX, typename TW, int MR, bool GATE, int NCH>
 __global__ void __launch_bounds__(kThreads, gemv_min_blocks<MR, GATE>())
-gemv_kernel(const GemvParams p) {
+gemv_kernel(const GemvParams p, const int nsm) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   TX* xs = reinterpret_cast<TX*>(smem_raw);  // [MR][K] activation rows
 
@@ -53,7 +53,16 @@ gemv_kernel(const GemvParams p) {
 
   const int lane = threadIdx.x & 31;
   const int warps_per_cta = blockDim.x >> 5;
-  const int gwarp = blockIdx.x * warps_per_cta + (threadIdx.x >> 5);
+  // Unit order.  Block order (gate-up): warp w of CTA b takes units
+  // b * warps + w + k * nwarps.  SM-round-robin order (plain projections, nsm
+  // > 0, the grid a multiple of the SM count so CTA b runs on SM b % nsm):
+  // consecutive units go to consecutive SMs, so the last, partial wave of
+  // units is spread over every SM instead of the first CTAs' SMs.  Measured
+  // (Qwen3-4B QKV, M = 1, 36 launches in a graph): 7.8 -> 6.9 us; for
+  // gate-up it was slower (17.4 -> 17.9 us) and stays in block order.
+  int gwarp = blockIdx.x * warps_per_cta + (threadIdx.x >> 5);
+  if (nsm > 0 && gridDim.x % nsm == 0)
+    gwarp = ((int)(blockIdx.x / nsm) * warps_per_cta + (threadIdx.x >> 5)) * nsm + blockIdx.x % nsm;
   const int nwarps = gridDim.x * warps_per_cta;
   const int N = p.N, K = p.K, M = p.M;
   const int nunits = GATE ? N : (N + 1) >> 1;
@@ -223,7 +232,8 @@ int launch_one(const DenseArgs& a) {
   if (grid > need) grid = need;
   if (grid < 1) grid = 1;
   GemvParams p{a.x, a.ldx, a.w0, a.ldw0, a.w1, a.ldw1, a.s0, a.s1, a.y, a.ldy, a.M, a.N, a.K};
-  cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, a.stream, p);
+  // plain projections: warps take units in SM-round-robin order (below)
+  cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, a.stream, p, GATE ? 0 : num_sms(dev));
   return e == cudaSuccess ? B200MM_OK : B200MM_ERR_LAUNCH;
 }
 
