@@ -94,10 +94,11 @@ def profile_op(args):
         # the Qwen3-8B int8 decode step (config 5) at batch --B: a prefill,
         # then three decode steps, each one replay of a CUDA graph of the
         # whole step (what the bench times); ncu sees the graph's kernels
-        from llms_b200.kernels import apply_linear_kernels
+        from llms_b200.kernels import apply_decode_attn, apply_linear_kernels
         from llms_b200.qwen3 import synthetic_int8_model
         model = synthetic_int8_model(seed=4)
-        apply_linear_kernels(model)
+        apply_linear_kernels(model, lm_head=True)
+        apply_decode_attn(model)
         B, P = args.B, 16
         ids = torch.randint(0, model.shape.vocab_size, (B, P), device="cuda", generator=g)
         nxt = torch.randint(0, model.shape.vocab_size, (B, 1), device="cuda", generator=g)
@@ -791,7 +792,7 @@ def qwen3_8b_int8_decode(batches=(1, 16, 64), prompt=16):
     greedy agreement is reported on decided rows and on all rows, for both
     bf16 paths, next to their logit rel-L2.  The 2-layer version of this
     model is pinned to the reference engine itself by tests/golden."""
-    from llms_b200.kernels import apply_linear_kernels
+    from llms_b200.kernels import apply_decode_attn, apply_linear_kernels
     from llms_b200.qwen3 import dequantized_dense_model, greedy, synthetic_int8_model
 
     model = synthetic_int8_model(seed=4)
@@ -835,7 +836,8 @@ def qwen3_8b_int8_decode(batches=(1, 16, 64), prompt=16):
     del dense
     torch.cuda.empty_cache()
     cublas = {B: step_logits_and_time(model, B)[1] for B in batches}
-    apply_linear_kernels(model)
+    apply_linear_kernels(model, lm_head=True)
+    apply_decode_attn(model)
     res = {}
     try:
         res["qwen3_8b_int8_decode_loop_b1"] = decode_loop(model, prompt)
@@ -850,8 +852,11 @@ def qwen3_8b_int8_decode(batches=(1, 16, 64), prompt=16):
         ours_ok, base_ok = greedy(logits) == want, greedy(base) == want
         rel = lambda a: float(((a - ref).norm() / ref.norm()).item())
         res[f"qwen3_8b_int8_decode_b{B}"] = {
-            "ms_per_step": sec / 20 * 1e3, "tok/s": B * 20 / sec, "o_down": "b200mm_linear",
-            "tok/s_o_down_cublas": B * 20 / cublas[B],
+            "ms_per_step": sec / 20 * 1e3, "tok/s": B * 20 / sec,
+            "path": "int8 QKV / gate-up; o, down, LM head on b200mm_linear; norms + residual adds on "
+                    "b200mm_rmsnorm; q/k norm + RoPE + cache write on b200mm_qk_norm_rope; attention on "
+                    "b200mm_gqa_decode",
+            "tok/s_o_down_lm_head_cublas_torch_attention": B * 20 / cublas[B],
             "tok/s_reference_bf16_dequant_torch": B * 20 / ref_sec[B],
             "rows": B, "decided_rows": int(decided.sum().item()),
             "argmax_agree_decided": bool(ours_ok[decided].all().item()),

@@ -26,6 +26,10 @@
  *   b200mm_mla_decode        <- engine/mla.py:195-264, the T == 1 branch of
  *                               MLAttention.forward (everything between the
  *                               q/dkv/kr projections and the o projection)
+ *   b200mm_rmsnorm           <- engine/attention.py:20-33 RMSNorm.forward, with the
+ *                               residual add of engine/model.py:54-63 folded in
+ *   b200mm_qk_norm_rope      <- engine/attention.py:119-131 (T == 1): q_norm,
+ *                               k_norm, apply_rope and the KV-cache write
  */
 #ifndef B200MM_H_
 #define B200MM_H_
@@ -257,6 +261,51 @@ int b200mm_mla_decode(const b200mm_mla_shape* shape,
                       void* out, int64_t o_sb,
                       void* workspace, size_t workspace_bytes,
                       void* stream);
+
+/*
+ * RMSNorm with the engine's rounding (src/engine/attention.py:20-33):
+ *   y[m, :] = weight * cast(x32 * rsqrt(mean(x32^2) + eps)),  x32 = float(h[m, :])
+ * on h = x, or, when `residual` is given, on h = cast(x + residual) -- the
+ * residual add that precedes every norm of a decoder block
+ * (src/engine/model.py:54-63: h = x + attn(norm1(x)); norm2(h)); h is then also
+ * stored to `h_out` when it is not NULL.  x, residual, weight, h_out and y share
+ * `dtype`; rows are 16-byte aligned; N <= 16384.  One launch replaces the
+ * engine's chain of elementwise kernels (cast, pow, mean, rsqrt, mul, cast,
+ * mul, and the add).
+ */
+int b200mm_rmsnorm(const void* x, int64_t ldx,
+                   const void* residual, int64_t ldr,
+                   void* h_out, int64_t ldh,
+                   const void* weight,
+                   void* y, int64_t ldy,
+                   int64_t M, int64_t N, float eps,
+                   int dtype, void* stream);
+
+/*
+ * QK-norm, RoPE and the KV-cache write of one new token per row
+ * (src/engine/attention.py:119-131 for T == 1), straight from the fused QKV
+ * projection's output qkv[b, :] = [q heads | k heads | v heads] (H, KV, KV
+ * heads of D):
+ *   q_out[b, h, :]          = rope(q_norm(q[b, h, :]), pos)
+ *   k_cache[b, kh, pos, :]  = rope(k_norm(k[b, kh, :]), pos)
+ *   v_cache[b, kh, pos, :]  = v[b, kh, :]
+ * with the engine's rounding: the norms as b200mm_rmsnorm over D, RoPE as
+ * x * cos + rotate_half(x) * sin in `dtype` (apply_rope, attention.py:59-72),
+ * each product and the sum rounded to `dtype`; the cos / sin tables
+ * [max_pos, D] are in `dtype` (the engine's model casts its tables with the
+ * module).  The position is `pos`, or *pos_dev when pos_dev is not NULL (a
+ * device scalar, for one CUDA graph replayed at every position; the caller
+ * keeps it inside [0, max_pos)).  D is 64, 128 or 256.
+ */
+int b200mm_qk_norm_rope(const void* qkv, int64_t ldq,
+                        int64_t B, int64_t H, int64_t KV, int64_t D,
+                        const void* q_norm_w, const void* k_norm_w,
+                        const void* cos_table, const void* sin_table, int64_t max_pos,
+                        int64_t pos, const int64_t* pos_dev,
+                        void* q_out, int64_t q_sb, int64_t q_sh,
+                        void* k_cache, int64_t k_sb, int64_t k_sh, int64_t k_st,
+                        void* v_cache, int64_t v_sb, int64_t v_sh, int64_t v_st,
+                        float eps, int dtype, void* stream);
 
 /*
  * b200mm_mla_decode_noalloc -- no counterpart in the reference.

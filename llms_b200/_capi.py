@@ -7,6 +7,7 @@ time if it is missing: there is no Python or CPU fallback for the kernels.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
 from pathlib import Path
@@ -85,6 +86,17 @@ SIGNATURES: dict[str, tuple] = {
          _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, ctypes.c_float, _c_i64, _c_p, _c_i64,
          _c_p, ctypes.c_size_t, _c_p],
     ),
+    "b200mm_rmsnorm": (
+        ctypes.c_int,
+        [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, ctypes.c_float, ctypes.c_int,
+         _c_p],
+    ),
+    "b200mm_qk_norm_rope": (
+        ctypes.c_int,
+        [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_i64, _c_p,
+         _c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, ctypes.c_float,
+         ctypes.c_int, _c_p],
+    ),
     "b200mm_mla_decode_noalloc": (
         ctypes.c_int,
         [ctypes.POINTER(MlaShape), _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64,
@@ -125,6 +137,19 @@ def dtype_code(dtype: torch.dtype) -> int:
         return DTYPE_CODES[dtype]
     except KeyError:
         raise ValueError(f"unsupported dtype {dtype}; expected float32, float16 or bfloat16") from None
+
+
+_SAME_DEVICE = contextlib.nullcontext()
+
+
+def on_device(t: torch.Tensor):
+    """``torch.cuda.device(t.device)`` when ``t`` is not on the current device,
+    else a no-op context (entering the device context costs more host time
+    than the kernel launch it guards, on every eager call)."""
+    idx = t.device.index
+    if idx is None or idx == torch.cuda.current_device():
+        return _SAME_DEVICE
+    return torch.cuda.device(t.device)
 
 
 def stream_of(t: torch.Tensor) -> int:

@@ -183,6 +183,48 @@ int b200mm_linear_w8(const void* x, int64_t ldx, const int8_t* w, const float* s
   return b200mm_qkv_w8(x, ldx, w, s, ldw, y, ldy, M, N, K, dtype, stream);
 }
 
+int b200mm_rmsnorm(const void* x, int64_t ldx, const void* residual, int64_t ldr, void* h_out, int64_t ldh,
+                   const void* weight, void* y, int64_t ldy, int64_t M, int64_t N, float eps, int dtype,
+                   void* stream) {
+  if (dtype != B200MM_F32 && dtype != B200MM_F16 && dtype != B200MM_BF16) return B200MM_ERR_DTYPE;
+  if (M < 0 || M > 2147483647LL || N < 1 || N > 16384) return B200MM_ERR_SHAPE;
+  if (ldx < N || ldy < N || (residual && ldr < N) || (h_out && ldh < N)) return B200MM_ERR_SHAPE;
+  if (!x || !weight || !y || (h_out && !residual) || !(eps >= 0.f)) return B200MM_ERR_ARG;
+  if (M == 0) return B200MM_OK;
+  int st = check_device();
+  if (st != B200MM_OK) return st;
+  st = glue_rmsnorm(x, ldx, residual, ldr, h_out, ldh, weight, y, ldy, (int)M, (int)N, eps, dtype,
+                    static_cast<cudaStream_t>(stream));
+  if (st != B200MM_OK) return st;
+  return launch_status();
+}
+
+int b200mm_qk_norm_rope(const void* qkv, int64_t ldq, int64_t B, int64_t H, int64_t KV, int64_t D,
+                        const void* q_norm_w, const void* k_norm_w, const void* cos_table, const void* sin_table,
+                        int64_t max_pos, int64_t pos, const int64_t* pos_dev, void* q_out, int64_t q_sb,
+                        int64_t q_sh, void* k_cache, int64_t k_sb, int64_t k_sh, int64_t k_st, void* v_cache,
+                        int64_t v_sb, int64_t v_sh, int64_t v_st, float eps, int dtype, void* stream) {
+  if (dtype != B200MM_F32 && dtype != B200MM_F16 && dtype != B200MM_BF16) return B200MM_ERR_DTYPE;
+  if (B < 0 || B > 65535 || KV < 1 || H < KV || H % KV || H > 4096 || (D != 64 && D != 128 && D != 256))
+    return B200MM_ERR_SHAPE;
+  if (ldq < (H + 2 * KV) * D || q_sh < D || q_sb < 0 || k_st < D || v_st < D || k_sh < 0 || v_sh < 0 ||
+      k_sb < 0 || v_sb < 0)
+    return B200MM_ERR_SHAPE;
+  if (!qkv || !q_norm_w || !k_norm_w || !cos_table || !sin_table || !q_out || !k_cache || !v_cache ||
+      !(eps >= 0.f))
+    return B200MM_ERR_ARG;
+  // a host position is checked here; a device position is the caller's to keep in [0, max_pos)
+  if (!pos_dev && (pos < 0 || pos >= max_pos)) return B200MM_ERR_SHAPE;
+  if (B == 0) return B200MM_OK;
+  int st = check_device();
+  if (st != B200MM_OK) return st;
+  st = glue_qk_norm_rope(qkv, ldq, (int)B, (int)H, (int)KV, (int)D, q_norm_w, k_norm_w, cos_table, sin_table, pos,
+                         pos_dev, q_out, q_sb, q_sh, k_cache, k_sb, k_sh, k_st, v_cache, v_sb, v_sh, v_st, eps, dtype,
+                         static_cast<cudaStream_t>(stream));
+  if (st != B200MM_OK) return st;
+  return launch_status();
+}
+
 namespace {
 bool gqa_shape_ok(int64_t B, int64_t H, int64_t KV, int64_t D, int64_t L) {
   return B >= 0 && B <= 65535 && KV >= 1 && H >= KV && H <= 65535 && H % KV == 0 && D >= 2 && D <= 1024 &&

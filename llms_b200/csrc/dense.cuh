@@ -35,6 +35,14 @@ int swap_launch(const DenseArgs& a);
 bool tc_supported(const DenseArgs& a);
 int tc_launch(const DenseArgs& a);
 
+// Decode-step glue (glue.cu); shapes validated by the caller.
+int glue_rmsnorm(const void* x, int64_t ldx, const void* r, int64_t ldr, void* h, int64_t ldh, const void* w, void* y,
+                 int64_t ldy, int M, int N, float eps, int dtype, cudaStream_t st);
+int glue_qk_norm_rope(const void* qkv, int64_t ldq, int B, int H, int KV, int D, const void* qw, const void* kw,
+                      const void* cos_t, const void* sin_t, int64_t pos, const int64_t* pos_dev, void* q_out,
+                      int64_t q_sb, int64_t q_sh, void* kc, int64_t k_sb, int64_t k_sh, int64_t k_st, void* vc,
+                      int64_t v_sb, int64_t v_sh, int64_t v_st, float eps, int dtype, cudaStream_t st);
+
 // GQA single-query decode attention (gqa.cu); shapes validated by the caller.
 size_t gqa_workspace_bytes(int B, int H, int KV, int D, int64_t L);
 int gqa_decode(const void* q, int64_t q_sb, int64_t q_sh, const void* k, int64_t k_sb, int64_t k_sh, int64_t k_st,

@@ -22,9 +22,10 @@
 //               M = 128, N = 192, K = 16) into two accumulator buffers of 192
 //               columns, so chunk j + 1 accumulates while chunk j is read;
 //   warps 3-10  two per TMEM lane quadrant: warp half h takes group 2n + h of
-//               chunk n (its 96 accumulator columns, squared and summed in
-//               registers) and, before that, the RoPE half of its four groups
-//               from the token's own k_rope_pre row (its squares, and kz).
+//               chunk n -- its 96 accumulator columns, squared and summed in
+//               registers (the buffer goes back to the MMAs at once), then
+//               the group's RoPE half from the token's own k_rope_pre row
+//               (its squares, and kz).
 // Every wait is bounded; a CTA whose wait expires stops issuing, drains its
 // own copies, frees TMEM and writes NaN scales for its tokens.
 #include "mla.cuh"
@@ -113,6 +114,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_map(&mc);
     prefetch_map(&mw);
   }
+  // the RoPE half's k_norm weights and the RoPE frequencies, read by every
+  // epilogue thread for every token: staged once
+  __shared__ float s_kw[FDR], s_inv[FDR / 2];
+  if (threadIdx.x < FDR) s_kw[threadIdx.x] = p.k_norm_w[FDN + threadIdx.x];
+  if (threadIdx.x < FDR / 2) s_inv[threadIdx.x] = p.inv_freq[threadIdx.x];
   if (warp == 2) tmem_alloc(tmem_slot, kTmemCols);
   tc_fence_before();
   __syncthreads();
@@ -206,53 +212,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- epilogue: warps 3..10 ----------------
     const int q = warp & 3, h = (warp - 3) >> 2;  // lane quadrant, group parity
     const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16);
-    const int half = FDR / 2;
+    constexpr int half = FDR / 2;
     bool bad = false;
     int jc = 0;
     for (int j = 0; j < mine; ++j) {
       const int u = blockIdx.x + j * gridDim.x, b = u / p.tiles_per_row, i = u % p.tiles_per_row;
       const int64_t t = p.t0 + (int64_t)i * TM + 32 * q + lane;
       const bool valid = t < p.t1;
-      // RoPE half of groups h, h + 2, h + 4, h + 6 (independent of the MMAs)
-      float ssq_r[4] = {0.f, 0.f, 0.f, 0.f};
+      float sn[half], cs[half];
       if (valid) {
-        float sn[half], cs[half];
 #pragma unroll
-        for (int ii = 0; ii < half; ++ii) sincosf((float)t * p.inv_freq[ii], &sn[ii], &cs[ii]);
-#pragma unroll
-        for (int gi = 0; gi < 4; ++gi) {
-          const int grp = 2 * gi + h;
-          const T* src = static_cast<const T*>(p.kr) + (int64_t)b * p.r_sb + t * p.r_st + grp * FDR;
-          float x[FDR];
-#pragma unroll
-          for (int c = 0; c < FDR / 8; ++c) Chunk<T>::unpack(*reinterpret_cast<const uint4*>(src + 8 * c), x + 8 * c);
-          float z[FDR];
-#pragma unroll
-          for (int jj = 0; jj < FDR; ++jj) {
-            ssq_r[gi] = fmaf(x[jj], x[jj], ssq_r[gi]);
-            const int ii = jj < half ? jj : jj - half;
-            const float rot = jj < half ? -p.k_norm_w[FDN + jj + half] * x[jj + half]
-                                        : p.k_norm_w[FDN + jj - half] * x[jj - half];
-            z[jj] = p.k_norm_w[FDN + jj] * x[jj] * cs[ii] + rot * sn[ii];
-          }
-          T* dst = static_cast<T*>(p.kz) + (int64_t)b * p.z_sb + t * p.z_st + grp * FDR;
-#pragma unroll
-          for (int c = 0; c < FDR / 8; ++c) {
-            uint4 o;
-            o.x = pack2<T>(z[8 * c + 0], z[8 * c + 1]);
-            o.y = pack2<T>(z[8 * c + 2], z[8 * c + 3]);
-            o.z = pack2<T>(z[8 * c + 4], z[8 * c + 5]);
-            o.w = pack2<T>(z[8 * c + 6], z[8 * c + 7]);
-            *reinterpret_cast<uint4*>(dst + 8 * c) = o;
-          }
-        }
+        for (int ii = 0; ii < half; ++ii) sincosf((float)t * s_inv[ii], &sn[ii], &cs[ii]);
       }
-      // no-RoPE half: |W_uk,g c_t|^2 for g = 2n + h, from chunk n's accumulators
-      float ssq_n[4];
-#pragma unroll
+      // chunk n holds groups 2n and 2n + 1: this warp takes group 2n + h --
+      // its 96 accumulator columns first (so the buffer is handed back to the
+      // MMAs at once), then the group's RoPE half from the token's own row
+#pragma unroll 1
       for (int n = 0; n < NCHUNK; ++n, ++jc) {
         const int buf = jc & 1;
-        ssq_n[n] = 0.f;
+        float ssq = 0.f;
         if (!bad) {
           bad = !mbar_wait(&acc_full[buf], (uint32_t)((jc >> 1) & 1)) || *failed;
           tc_fence_after();
@@ -263,17 +241,37 @@ __global__ void __launch_bounds__(kThreads, 1)
             float v[32];
             tmem_ld32(tq + buf * kBufCols + h * FDN + c, v);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) ssq_n[n] = fmaf(v[e], v[e], ssq_n[n]);
+            for (int e = 0; e < 32; ++e) ssq = fmaf(v[e], v[e], ssq);
           }
           tc_fence_before();
           mbar_arrive(&acc_empty[buf]);
         }
-      }
-      if (valid) {
-        float* ks = p.kscale + (int64_t)b * p.s_sb + t * p.s_st;
+        if (!valid) continue;
+        const int grp = 2 * n + h;
+        const T* src = static_cast<const T*>(p.kr) + (int64_t)b * p.r_sb + t * p.r_st + grp * FDR;
+        float x[FDR];
 #pragma unroll
-        for (int gi = 0; gi < 4; ++gi)
-          ks[2 * gi + h] = bad ? __int_as_float(0x7fc00000) : rsqrtf((ssq_n[gi] + ssq_r[gi]) / (float)FD + p.eps);
+        for (int c = 0; c < FDR / 8; ++c) Chunk<T>::unpack(*reinterpret_cast<const uint4*>(src + 8 * c), x + 8 * c);
+        float z[FDR];
+#pragma unroll
+        for (int jj = 0; jj < FDR; ++jj) {
+          ssq = fmaf(x[jj], x[jj], ssq);
+          const int ii = jj < half ? jj : jj - half;
+          const float rot = jj < half ? -s_kw[jj + half] * x[jj + half] : s_kw[jj - half] * x[jj - half];
+          z[jj] = s_kw[jj] * x[jj] * cs[ii] + rot * sn[ii];
+        }
+        T* dst = static_cast<T*>(p.kz) + (int64_t)b * p.z_sb + t * p.z_st + grp * FDR;
+#pragma unroll
+        for (int c = 0; c < FDR / 8; ++c) {
+          uint4 o;
+          o.x = pack2<T>(z[8 * c + 0], z[8 * c + 1]);
+          o.y = pack2<T>(z[8 * c + 2], z[8 * c + 3]);
+          o.z = pack2<T>(z[8 * c + 4], z[8 * c + 5]);
+          o.w = pack2<T>(z[8 * c + 6], z[8 * c + 7]);
+          *reinterpret_cast<uint4*>(dst + 8 * c) = o;
+        }
+        p.kscale[(int64_t)b * p.s_sb + t * p.s_st + grp] =
+            bad ? __int_as_float(0x7fc00000) : rsqrtf(ssq / (float)FD + p.eps);
       }
     }
   }

@@ -68,7 +68,7 @@ def b200_decode_attn(q: torch.Tensor, full_k: torch.Tensor, full_v: torch.Tensor
     qq = q if q.stride(-1) == 1 else q.contiguous()
     k = full_k if full_k.stride(-1) == 1 else full_k.contiguous()
     v = full_v if full_v.stride(-1) == 1 else full_v.contiguous()
-    with torch.cuda.device(q.device):
+    with _capi.on_device(q):
         stream = _capi.stream_of(q)
         need = _capi.lib.b200mm_gqa_decode_workspace_size(B, H, KV, D, L)
         if need == 0:

@@ -60,7 +60,7 @@ def triton_fused_gate_up_silu(x: torch.Tensor, Wg: torch.Tensor, Wu: torch.Tenso
         return y.zero_().reshape(*lead, N)
     _capi.require_cuda(x)
     Wg2, Wu2 = _rows(Wg), _rows(Wu)
-    with torch.cuda.device(x.device):
+    with _capi.on_device(x):
         st = _capi.lib.b200mm_gate_up_silu(
             x2.data_ptr(), x2.stride(0),
             Wg2.data_ptr(), Wg2.stride(0),

@@ -15,6 +15,7 @@ from torch import nn
 
 from .. import _capi
 from ._eager import RMSNorm, rope
+from .glue import fits_qk_norm_rope, qk_norm_rope_cache
 
 
 def _check_qkv_args(x: torch.Tensor, W_qkv: torch.Tensor, n_q: int, n_k: int) -> None:
@@ -62,7 +63,7 @@ def triton_fused_qkv(
         else:
             _capi.require_cuda(x)
             W = W_qkv if W_qkv.stride(-1) == 1 else W_qkv.contiguous()
-            with torch.cuda.device(x.device):
+            with _capi.on_device(x):
                 st = _capi.lib.b200mm_qkv(
                     x2.data_ptr(), x2.stride(0), W.data_ptr(), W.stride(0),
                     y.data_ptr(), y.stride(0), M, n_total, K,
@@ -72,6 +73,17 @@ def triton_fused_qkv(
     y = y.reshape(*lead, n_total)
     q, k, v = y.split([n_q, n_k, n_k], dim=-1)
     return q, k, v
+
+
+def _one_buffer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor | None:
+    """The [*, n_q + 2 n_k] buffer q / k / v are split views of (the fused
+    projections return such views), or None if they are not adjacent."""
+    n_q, n_k = q.shape[-1], k.shape[-1]
+    e = q.element_size()
+    if (q.stride(-1) != 1 or k.stride() != q.stride() or v.stride() != q.stride()
+            or k.data_ptr() != q.data_ptr() + n_q * e or v.data_ptr() != k.data_ptr() + n_k * e):
+        return None
+    return q.as_strided(q.shape[:-1] + (n_q + 2 * n_k,), q.stride())
 
 
 class TritonAttention(nn.Module):
@@ -125,14 +137,22 @@ class TritonAttention(nn.Module):
                 sin: torch.Tensor, start_pos: int) -> torch.Tensor:
         B, T, _ = x.shape
         qf, kf, vf = self.project_qkv(x)
-        q = self.q_norm(qf.view(B, T, self.num_heads, self.head_dim)).transpose(1, 2)
-        k = self.k_norm(kf.view(B, T, self.num_kv_heads, self.head_dim)).transpose(1, 2)
-        v = vf.view(B, T, self.num_kv_heads, self.head_dim).transpose(1, 2)
-        q, k = rope(q, cos, sin), rope(k, cos, sin)
-
         end = start_pos + T
-        kv_cache.k[layer_idx][:B, :, start_pos:end, :] = k
-        kv_cache.v[layer_idx][:B, :, start_pos:end, :] = v
+        flat = _one_buffer(qf, kf, vf)
+        if T == 1 and flat is not None and fits_qk_norm_rope(flat, self.q_norm, self.k_norm, cos, self.head_dim):
+            # one launch for q_norm, k_norm, RoPE and the cache write of the
+            # decode token (the same rounding as the eager lines below)
+            q = qk_norm_rope_cache(flat, self.q_norm, self.k_norm, cos, sin, num_heads=self.num_heads,
+                                   num_kv_heads=self.num_kv_heads, head_dim=self.head_dim,
+                                   k_cache=kv_cache.k[layer_idx][:, :, start_pos:],
+                                   v_cache=kv_cache.v[layer_idx][:, :, start_pos:], pos=0)
+        else:
+            q = self.q_norm(qf.view(B, T, self.num_heads, self.head_dim)).transpose(1, 2)
+            k = self.k_norm(kf.view(B, T, self.num_kv_heads, self.head_dim)).transpose(1, 2)
+            v = vf.view(B, T, self.num_kv_heads, self.head_dim).transpose(1, 2)
+            q, k = rope(q, cos, sin), rope(k, cos, sin)
+            kv_cache.k[layer_idx][:B, :, start_pos:end, :] = k
+            kv_cache.v[layer_idx][:B, :, start_pos:end, :] = v
         full_k = kv_cache.k[layer_idx][:B, :, :end, :]
         full_v = kv_cache.v[layer_idx][:B, :, :end, :]
         op = getattr(self, "decode_attn_op", None)

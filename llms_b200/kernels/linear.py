@@ -59,7 +59,7 @@ def b200_linear(x: torch.Tensor, W: torch.Tensor) -> torch.Tensor:
         return y.zero_().reshape(*lead, N)
     _capi.require_cuda(x)
     W2 = _rows(W)
-    with torch.cuda.device(x.device):
+    with _capi.on_device(x):
         st = _capi.lib.b200mm_linear(
             x2.data_ptr(), x2.stride(0), W2.data_ptr(), W2.stride(0), y.data_ptr(), y.stride(0),
             M, N, K, _capi.dtype_code(x.dtype), _capi.stream_of(x),
@@ -89,7 +89,7 @@ def int8_linear(x: torch.Tensor, q: torch.Tensor, s: torch.Tensor) -> torch.Tens
         return y.zero_().reshape(*lead, N)
     _capi.require_cuda(x)
     q2, s2 = _rows(q), s.contiguous()
-    with torch.cuda.device(x.device):
+    with _capi.on_device(x):
         st = _capi.lib.b200mm_linear_w8(
             x2.data_ptr(), x2.stride(0), q2.data_ptr(), s2.data_ptr(), q2.stride(0),
             y.data_ptr(), y.stride(0), M, N, K, _capi.dtype_code(x.dtype), _capi.stream_of(x),

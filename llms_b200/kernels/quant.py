@@ -60,7 +60,7 @@ def int8_fused_gate_up_silu(x: torch.Tensor, qg: torch.Tensor, sg: torch.Tensor,
     if M and N:
         _capi.require_cuda(x)
         qg2, qu2 = qg.contiguous(), qu.contiguous()
-        with torch.cuda.device(x.device):
+        with _capi.on_device(x):
             st = _capi.lib.b200mm_gate_up_silu_w8(
                 x2.data_ptr(), x2.stride(0), qg2.data_ptr(), sg.data_ptr(), qu2.data_ptr(),
                 su.data_ptr(), qg2.stride(0), y.data_ptr(), y.stride(0), M, N, K,
@@ -85,7 +85,7 @@ def int8_fused_qkv(x: torch.Tensor, q_qkv: torch.Tensor, s_qkv: torch.Tensor, *,
     if M and n_total:
         _capi.require_cuda(x)
         W = q_qkv if q_qkv.stride(-1) == 1 else q_qkv.contiguous()
-        with torch.cuda.device(x.device):
+        with _capi.on_device(x):
             st = _capi.lib.b200mm_qkv_w8(
                 x2.data_ptr(), x2.stride(0), W.data_ptr(), s_qkv.data_ptr(), W.stride(0),
                 y.data_ptr(), y.stride(0), M, n_total, K,

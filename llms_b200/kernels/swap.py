@@ -41,18 +41,23 @@ def apply_int8_kernels(model: nn.Module, *, ffn: bool = True, qkv: bool = True) 
     return model
 
 
-def apply_linear_kernels(model: nn.Module, *, int8: bool = False, o: bool = True, down: bool = True) -> nn.Module:
+def apply_linear_kernels(model: nn.Module, *, int8: bool = False, o: bool = True, down: bool = True,
+                         lm_head: bool = False) -> nn.Module:
     """Route each layer's attention output projection ``attn.o`` and FFN
     ``ffn.down`` through the B200 projection kernels (:class:`B200Linear`,
     sharing the weight; or :class:`Int8Linear` with ``int8=True``).  Works on
     the engine modules and on the fused-kernel modules alike, since both call
-    ``self.o(...)`` / ``self.down(...)``.  Idempotent; returns ``model``."""
+    ``self.o(...)`` / ``self.down(...)``.  ``lm_head=True`` routes the
+    model's untied LM head (engine/model.py:93-96) the same way.  Idempotent;
+    returns ``model``."""
     cls = Int8Linear if int8 else B200Linear
     for block in model.layers:
         if o and isinstance(block.attn.o, nn.Linear):
             block.attn.o = cls.from_linear(block.attn.o)
         if down and isinstance(block.ffn.down, nn.Linear):
             block.ffn.down = cls.from_linear(block.ffn.down)
+    if lm_head and isinstance(getattr(model, "lm_head", None), nn.Linear):
+        model.lm_head = cls.from_linear(model.lm_head)
     return model
 
 

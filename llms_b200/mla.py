@@ -131,7 +131,7 @@ def mla_append(c_kv: torch.Tensor, k_rope_pre: torch.Tensor | None, w_uk: torch.
     shp = _shape(B, num_kv_heads, num_kv_heads, head_dim, DR, R, c_kv.dtype, eps)
     if kscale.dtype != torch.float32 or kscale.stride(-1) != 1:
         raise ValueError("kscale must be float32 with a dense last dim")
-    with torch.cuda.device(c_kv.device):
+    with _capi.on_device(c_kv):
         st = _capi.lib.b200mm_mla_append(
             ctypes.byref(shp), c_kv.data_ptr(), c_kv.stride(0), c_kv.stride(1),
             _ptr(k_rope_pre), 0 if k_rope_pre is None else k_rope_pre.stride(0),
@@ -187,7 +187,7 @@ def mla_decode(q: torch.Tensor, c_kv: torch.Tensor, kz: torch.Tensor | None, ksc
         workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
     if out is None:
         out = torch.empty((B, H, D), dtype=q.dtype, device=q.device)
-    with torch.cuda.device(q.device):
+    with _capi.on_device(q):
         st = _capi.lib.b200mm_mla_decode(
             ctypes.byref(shp), q.data_ptr(), q.stride(0),
             c_kv.data_ptr(), c_kv.stride(0), c_kv.stride(1),

@@ -23,6 +23,8 @@ import torch.nn.functional as F
 from torch import nn
 
 from .kernels._eager import RMSNorm, rope
+from .kernels.fused_qkv import _one_buffer
+from .kernels.glue import fits_qk_norm_rope, fits_rms_norm, qk_norm_rope_cache, rms_norm
 from .kernels.quant import Int8Attention, Int8FFN, dequantize_per_row
 
 
@@ -96,7 +98,7 @@ def _project_qkv(attn, x):
     return attn.q(x), attn.k(x), attn.v(x)
 
 
-def static_decode_attention(attn, x, kv_cache, layer_idx, cos, sin, pos):
+def static_decode_attention(attn, x, kv_cache, layer_idx, cos, sin, pos, tables=None):
     """One decode token (x: B, 1, C) through ``attn`` with its position ``pos``
     a device tensor: the cache row is written with ``index_copy_`` and the
     softmax runs over the whole static cache with a mask computed on the
@@ -112,13 +114,20 @@ def static_decode_attention(attn, x, kv_cache, layer_idx, cos, sin, pos):
     B = x.shape[0]
     H, KV, D = attn.num_heads, attn.num_kv_heads, attn.head_dim
     qf, kf, vf = _project_qkv(attn, x)
-    q = attn.q_norm(qf.reshape(B, 1, H, D)).transpose(1, 2)
-    k = attn.k_norm(kf.reshape(B, 1, KV, D)).transpose(1, 2)
-    v = vf.reshape(B, 1, KV, D).transpose(1, 2)
-    q, k = rope(q, cos, sin), rope(k, cos, sin)
     kc, vc = kv_cache.k[layer_idx][:B], kv_cache.v[layer_idx][:B]
-    kc.index_copy_(2, pos, k.to(kc.dtype))
-    vc.index_copy_(2, pos, v.to(vc.dtype))
+    flat = _one_buffer(qf, kf, vf)
+    if (tables is not None and flat is not None and kc.dtype == flat.dtype
+            and fits_qk_norm_rope(flat, attn.q_norm, attn.k_norm, tables[0], D)):
+        # norms, RoPE (position read on the device) and the cache write in one launch
+        q = qk_norm_rope_cache(flat, attn.q_norm, attn.k_norm, tables[0], tables[1], num_heads=H, num_kv_heads=KV,
+                               head_dim=D, k_cache=kc, v_cache=vc, pos=pos)
+    else:
+        q = attn.q_norm(qf.reshape(B, 1, H, D)).transpose(1, 2)
+        k = attn.k_norm(kf.reshape(B, 1, KV, D)).transpose(1, 2)
+        v = vf.reshape(B, 1, KV, D).transpose(1, 2)
+        q, k = rope(q, cos, sin), rope(k, cos, sin)
+        kc.index_copy_(2, pos, k.to(kc.dtype))
+        vc.index_copy_(2, pos, v.to(vc.dtype))
     S = kc.shape[2]
     mask = (torch.arange(S, device=x.device) <= pos).view(1, 1, 1, S)
     a = F.scaled_dot_product_attention(q, kc, vc, attn_mask=mask, enable_gqa=H != KV)
@@ -201,11 +210,41 @@ class Qwen3Model(nn.Module):
         h = self.embed(input_ids)
         cos = self.rope_cos[start_pos:start_pos + T].to(h.dtype)
         sin = self.rope_sin[start_pos:start_pos + T].to(h.dtype)
-        for i, layer in enumerate(self.layers):
-            h = layer(h, kv_cache=kv_cache, layer_idx=i, cos=cos, sin=sin, start_pos=start_pos)
-        logits = self.lm_head(self.final_norm(h))
+        if self._fused_norms_fit(h):
+            y = self._blocks_fused(h, lambda blk, i, x: blk.attn(x, kv_cache=kv_cache, layer_idx=i, cos=cos,
+                                                                 sin=sin, start_pos=start_pos))
+        else:
+            for i, layer in enumerate(self.layers):
+                h = layer(h, kv_cache=kv_cache, layer_idx=i, cos=cos, sin=sin, start_pos=start_pos)
+            y = self.final_norm(h)
+        logits = self.lm_head(y)
         kv_cache.cur_len = start_pos + T
         return logits
+
+    def _fused_norms_fit(self, h: torch.Tensor) -> bool:
+        if not getattr(self, "fused_glue", True):
+            return False
+        norms = [self.final_norm] + [n for blk in self.layers for n in (blk.norm1, blk.norm2)]
+        return all(fits_rms_norm(h, n.weight) for n in norms)
+
+    def _blocks_fused(self, h: torch.Tensor, attn):
+        """The decoder blocks with every norm and residual add on
+        ``b200mm_rmsnorm``: block i computes h = x + attn(norm1(x)) and
+        x' = h + ffn(norm2(h)) (engine/model.py:54-63); each residual add is
+        folded into the norm that reads its result, so a block is two norm
+        launches around its attention and FFN, and the last add is folded
+        into the final norm.  Returns final_norm(x_last)."""
+        x, f = h, None
+        for i, blk in enumerate(self.layers):
+            if f is None:
+                y = rms_norm(x, blk.norm1.weight, blk.norm1.eps)
+            else:
+                x, y = rms_norm(f, blk.norm1.weight, blk.norm1.eps, residual=x)
+            a = attn(blk, i, y)
+            x, y = rms_norm(a, blk.norm2.weight, blk.norm2.eps, residual=x)
+            f = blk.ffn(y)
+        _, y = rms_norm(f, self.final_norm.weight, self.final_norm.eps, residual=x)
+        return y
 
     def forward_static(self, input_ids: torch.Tensor, kv_cache: KVCache, pos: torch.Tensor) -> torch.Tensor:
         """One decode step (input_ids: B, 1) at the position held in the device
@@ -216,6 +255,10 @@ class Qwen3Model(nn.Module):
         h = self.embed(input_ids)
         cos = self.rope_cos.index_select(0, pos).to(h.dtype)
         sin = self.rope_sin.index_select(0, pos).to(h.dtype)
+        if self._fused_norms_fit(h):
+            return self.lm_head(self._blocks_fused(
+                h, lambda blk, i, x: static_decode_attention(blk.attn, x, kv_cache, i, cos, sin, pos,
+                                                             tables=(self.rope_cos, self.rope_sin))))
         for i, blk in enumerate(self.layers):
             h = h + static_decode_attention(blk.attn, blk.norm1(h), kv_cache, i, cos, sin, pos)
             h = h + blk.ffn(blk.norm2(h))
@@ -372,10 +415,12 @@ def dequantized_dense_model(model: Qwen3Model) -> Qwen3Model:
     projection dequantised (``W = q * s``), rounded to the model dtype and
     split back into the engine's q / k / v and gate / up ``nn.Linear``s
     (engine/attention.py:95-98, engine/model.py:30-32); ``o``, ``down``,
-    norms, embedding and LM head shared with ``model``."""
+    norms, embedding and LM head shared with ``model``; norms and residual
+    adds as the engine's eager torch ops (``fused_glue = False``)."""
     shape, p = model.shape, model.lm_head.weight
     out = Qwen3Model(shape, build_projections=False)
     out.to(device=p.device, dtype=p.dtype)
+    out.fused_glue = False  # the engine's own eager norms and adds, too
     out.embed, out.lm_head, out.final_norm = model.embed, model.lm_head, model.final_norm
     nq = shape.num_attention_heads * shape.head_dim
     nk = shape.num_key_value_heads * shape.head_dim
