@@ -686,18 +686,20 @@ def qwen3_8b_int8_decode_sharded(rank, world, batches=(1, 16, 64), prompt=16, st
 
 def mla_sharded(rank, world, B=32, steps=10):
     """BASELINE configs[3] across GPUs: MLA decode at L = 32768 split by batch
-    row, and for batches smaller than the GPU count by KV group too
-    (llms_b200.mla.decode_shard; no collective in the op), one CUDA graph of
-    one decode per rank, device time max over ranks.  GB/s is the whole
-    job's algorithmic bytes (each cached token once) over that time; a group
-    split reads the latent of its rows on every GPU of the row, which the
-    per-rank byte count next to it shows."""
+    row (no collective in the op) or, with fewer rows than GPUs, by context
+    (llms_b200.mla.decode_shard): each rank streams its slice of every row's
+    cache, and the slices' partial softmaxes (B x H x (R + 2) floats per rank)
+    are all-gathered and merged before the W_uv step -- the flash-decoding
+    split across GPUs; the gather and the merge are inside the timed step.
+    One CUDA graph per rank, device time max over ranks; GB/s is the whole
+    job's algorithmic bytes (each cached token once) over that time."""
     from llms_b200 import mla
 
     H, KV, D, DR, R, L = 32, 8, 128, 32, 256, 32768
-    rows, groups = mla.decode_shard(B, KV, world, rank)
+    rows, toks = mla.decode_shard(B, L, world, rank)
     b = len(rows)
-    if b and len(groups):
+    ctx = B < world
+    if b:
         gg = torch.Generator(device="cuda").manual_seed(3 + 1000 * rows.start)
         c = torch.randn(b, L, R, device="cuda", dtype=torch.bfloat16, generator=gg)
         kr = torch.randn(b, L, KV, DR, device="cuda", dtype=torch.bfloat16, generator=gg)
@@ -708,9 +710,26 @@ def mla_sharded(rank, world, B=32, steps=10):
         inv = mla.rope_inv_freq(D, DR, 1e6, "cuda")
         ks, kz = mla.mla_sidebands(c, kr, wuk, kw, inv, B=b, L=L, num_kv_heads=KV, head_dim=D, eps=1e-6)
         del kr
-        local = range(0, b)
-        fn = lambda: mla.mla_decode_shard(q, c, kz, ks, wuk, wuv, kw, inv, rows=local, groups=groups, L=L,
-                                          scale=D ** -0.5, eps=1e-6)
+        if ctx:
+            import torch.distributed as dist
+            av_all = torch.empty(world, b, H, R, device="cuda")
+            ml_all = torch.empty(world, b, H, 2, device="cuda")
+            ws = torch.empty(mla.workspace_bytes(b, H, KV, D, DR, R, len(toks), torch.bfloat16), dtype=torch.uint8,
+                             device="cuda")
+
+            def fn():
+                av, ml = mla.mla_decode_partial(q, c, kz, ks, wuk, kw, inv, num_kv_heads=KV, L=L, tokens=toks,
+                                                scale=D ** -0.5, eps=1e-6, workspace=ws)
+                dist.all_gather_into_tensor(av_all, av)
+                dist.all_gather_into_tensor(ml_all, ml)
+                return mla.mla_combine_partials(av_all, ml_all, wuv, head_dim=D, d_rope=DR, dtype=torch.bfloat16,
+                                                 eps=1e-6)
+        else:
+            ws = torch.empty(mla.workspace_bytes(b, H, KV, D, DR, R, L, torch.bfloat16), dtype=torch.uint8,
+                             device="cuda")
+            o = torch.empty(b, H, D, device="cuda", dtype=torch.bfloat16)
+            fn = lambda: mla.mla_decode(q, c, kz, ks, wuk, wuv, kw, inv, L=L, scale=D ** -0.5, eps=1e-6, out=o,
+                                        workspace=ws)
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
@@ -721,7 +740,7 @@ def mla_sharded(rank, world, B=32, steps=10):
         with torch.cuda.graph(g):
             fn()
         sec = time_graph(g, steps, 3, world)
-        rank_bytes = b * L * (512 + (512 + 32) * len(groups) // KV)
+        rank_bytes = b * len(toks) * (1024 + 32)
     else:  # no work for this rank: it idles but joins the timing
         class _Idle:
             def replay(self):
@@ -730,10 +749,10 @@ def mla_sharded(rank, world, B=32, steps=10):
         rank_bytes = 0
     per = sec / steps
     alg = 1024 * B * L + 32 * B * L + 917504 + 512 * B
-    split = "batch rows" if B >= world else "batch rows x KV groups"
+    split = ("context slices of every row, partial softmaxes all-gathered and merged" if ctx
+             else "batch rows (no collective in the op)")
     return {"GB/s": alg / per / 1e9, "us_per_step": per * 1e6, "B": B, "L": L,
-            "split": f"{split} over {world} GPUs (no collective in the op)",
-            "rank0_cache_bytes": rank_bytes if rank == 0 else None,
+            "split": f"{split} over {world} GPUs", "rank0_cache_bytes": rank_bytes if rank == 0 else None,
             "bytes_note": "512*B*L latent + 512*B*L RoPE'd-key side-band + 32*B*L k-RMS side-band + weights + q/out"}
 
 

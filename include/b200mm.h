@@ -263,6 +263,43 @@ int b200mm_mla_decode(const b200mm_mla_shape* shape,
                       void* stream);
 
 /*
+ * The MLA decode split over the context, for a step spread across GPUs when
+ * the batch has fewer rows than GPUs (each GPU streams a slice of every row's
+ * cache; the slices' partial softmaxes are merged afterwards).  Same math as
+ * b200mm_mla_decode (engine/mla.py:195-264), cut in two:
+ *
+ * b200mm_mla_decode_partial: tokens [t_begin, t_end) of rows 0..B-1 for a
+ *   query at position L - 1 (the RoPE of the query uses L; the pointers are
+ *   the whole cache's).  Writes av_out fp32 [B, H, R] -- sum_t p_t c_t with p
+ *   the softmax over the range -- and ml_out fp32 [B, H, 2] -- the range's
+ *   (max score, sum of exp).  No W_uv step.  Workspace as
+ *   b200mm_mla_decode_workspace_size(shape, t_end - t_begin).
+ * b200mm_mla_combine_partials: nparts ranges' av / ml stacked [nparts, B, H, R]
+ *   and [nparts, B, H, 2] (nparts <= 64) -> out [B, H, D] =
+ *   W_uv . (sum_r s_r e^(m_r - M) av_r / sum_r s_r e^(m_r - M)).  Workspace as
+ *   b200mm_mla_decode_workspace_size(shape, 1).
+ * No reference counterpart of the split itself: the reference runs one GPU.
+ */
+int b200mm_mla_decode_partial(const b200mm_mla_shape* shape,
+                              const void* q, int64_t q_sb,
+                              const void* c_kv, int64_t c_sb, int64_t c_st,
+                              const void* kz, int64_t z_sb, int64_t z_st,
+                              const float* kscale, int64_t s_sb, int64_t s_st,
+                              const void* w_uk,
+                              const float* k_norm_w, const float* rope_inv_freq,
+                              float scale, int64_t L, int64_t t_begin, int64_t t_end,
+                              float* av_out, float* ml_out,
+                              void* workspace, size_t workspace_bytes,
+                              void* stream);
+
+int b200mm_mla_combine_partials(const b200mm_mla_shape* shape,
+                                const float* av_parts, const float* ml_parts, int64_t nparts,
+                                const void* w_uv,
+                                void* out, int64_t o_sb,
+                                void* workspace, size_t workspace_bytes,
+                                void* stream);
+
+/*
  * RMSNorm with the engine's rounding (src/engine/attention.py:20-33):
  *   y[m, :] = weight * cast(x32 * rsqrt(mean(x32^2) + eps)),  x32 = float(h[m, :])
  * on h = x, or, when `residual` is given, on h = cast(x + residual) -- the

@@ -86,6 +86,16 @@ SIGNATURES: dict[str, tuple] = {
          _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, ctypes.c_float, _c_i64, _c_p, _c_i64,
          _c_p, ctypes.c_size_t, _c_p],
     ),
+    "b200mm_mla_decode_partial": (
+        ctypes.c_int,
+        [ctypes.POINTER(MlaShape), _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64,
+         _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_p, ctypes.c_float, _c_i64, _c_i64, _c_i64, _c_p, _c_p,
+         _c_p, ctypes.c_size_t, _c_p],
+    ),
+    "b200mm_mla_combine_partials": (
+        ctypes.c_int,
+        [ctypes.POINTER(MlaShape), _c_p, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p, ctypes.c_size_t, _c_p],
+    ),
     "b200mm_rmsnorm": (
         ctypes.c_int,
         [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, ctypes.c_float, ctypes.c_int,

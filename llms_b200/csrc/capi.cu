@@ -306,6 +306,7 @@ int b200mm_mla_decode(const b200mm_mla_shape* shape, const void* q, int64_t q_sb
   a.scale = scale; a.L = L; a.out = out; a.o_sb = o_sb;
   a.ws = workspace; a.ws_bytes = workspace_bytes;
   a.stream = static_cast<cudaStream_t>(stream);
+  a.qpos = L - 1;
   int st = mla_validate_shape(a.s);
   if (st != B200MM_OK) return st;
   if (L < 1 || L >= (int64_t(1) << 31)) return B200MM_ERR_SHAPE;
@@ -320,6 +321,66 @@ int b200mm_mla_decode(const b200mm_mla_shape* shape, const void* q, int64_t q_sb
   st = check_device();
   if (st != B200MM_OK) return st;
   st = mla_decode_launch(a);
+  if (st != B200MM_OK) return st;
+  return launch_status();
+}
+
+int b200mm_mla_decode_partial(const b200mm_mla_shape* shape, const void* q, int64_t q_sb, const void* c_kv,
+                              int64_t c_sb, int64_t c_st, const void* kz, int64_t z_sb, int64_t z_st,
+                              const float* kscale, int64_t s_sb, int64_t s_st, const void* w_uk,
+                              const float* k_norm_w, const float* rope_inv_freq, float scale, int64_t L,
+                              int64_t t_begin, int64_t t_end, float* av_out, float* ml_out, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+  if (!shape) return B200MM_ERR_ARG;
+  int st = mla_validate_shape(*shape);
+  if (st != B200MM_OK) return st;
+  if (L < 1 || L >= (int64_t(1) << 31) || t_begin < 0 || t_end <= t_begin || t_end > L) return B200MM_ERR_SHAPE;
+  if (!q || !c_kv || !kscale || !k_norm_w || !av_out || !ml_out) return B200MM_ERR_ARG;
+  if (shape->DR > 0 && (!kz || !rope_inv_freq)) return B200MM_ERR_ARG;
+  if (shape->D - shape->DR > 0 && !w_uk) return B200MM_ERR_ARG;
+  if (!(scale > 0.f)) return B200MM_ERR_ARG;
+  if (shape->B == 0) return B200MM_OK;
+  MlaDecodeArgs a{};
+  a.s = *shape;
+  const int esz = shape->dtype == B200MM_F32 ? 4 : 2;
+  // the range's tokens: every per-token pointer starts at t_begin
+  a.q = q; a.q_sb = q_sb;
+  a.c_kv = static_cast<const unsigned char*>(c_kv) + t_begin * c_st * esz; a.c_sb = c_sb; a.c_st = c_st;
+  a.kz = kz ? static_cast<const unsigned char*>(kz) + t_begin * z_st * esz : nullptr; a.z_sb = z_sb; a.z_st = z_st;
+  a.kscale = kscale + t_begin * s_st; a.s_sb = s_sb; a.s_st = s_st;
+  a.w_uk = w_uk; a.w_uv = nullptr; a.k_norm_w = k_norm_w; a.inv_freq = rope_inv_freq;
+  a.scale = scale; a.L = t_end - t_begin; a.qpos = L - 1;
+  a.av_out = av_out; a.ml_out = ml_out;
+  a.ws = workspace; a.ws_bytes = workspace_bytes;
+  a.stream = static_cast<cudaStream_t>(stream);
+  const size_t need = mla_workspace_bytes(a.s, a.L);
+  if (!workspace || workspace_bytes < need || ((uintptr_t)workspace & 255u)) return B200MM_ERR_WORKSPACE;
+  st = check_device();
+  if (st != B200MM_OK) return st;
+  st = mla_decode_launch(a);
+  if (st != B200MM_OK) return st;
+  return launch_status();
+}
+
+int b200mm_mla_combine_partials(const b200mm_mla_shape* shape, const float* av_parts, const float* ml_parts,
+                                int64_t nparts, const void* w_uv, void* out, int64_t o_sb, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  if (!shape) return B200MM_ERR_ARG;
+  int st = mla_validate_shape(*shape);
+  if (st != B200MM_OK) return st;
+  if (nparts < 1 || nparts > 64) return B200MM_ERR_SHAPE;
+  if (!av_parts || !ml_parts || !w_uv || !out) return B200MM_ERR_ARG;
+  if (shape->B == 0) return B200MM_OK;
+  MlaDecodeArgs a{};
+  a.s = *shape;
+  a.w_uv = w_uv; a.out = out; a.o_sb = o_sb; a.L = 1; a.qpos = 0;
+  a.ws = workspace; a.ws_bytes = workspace_bytes;
+  a.stream = static_cast<cudaStream_t>(stream);
+  const size_t need = mla_workspace_bytes(a.s, 1);
+  if (!workspace || workspace_bytes < need || ((uintptr_t)workspace & 255u)) return B200MM_ERR_WORKSPACE;
+  st = check_device();
+  if (st != B200MM_OK) return st;
+  st = mla_combine_partials_launch(a, av_parts, ml_parts, (int)nparts);
   if (st != B200MM_OK) return st;
   return launch_status();
 }

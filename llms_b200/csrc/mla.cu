@@ -210,7 +210,7 @@ __global__ void __launch_bounds__(kThreads) mla_absorb_kernel(const MlaDecodeArg
   if (blockIdx.z != 0) return;
   // qr = rope at position L-1 (rotate-half convention, angle = pos * inv_freq)
   const int half = DR / 2;
-  const float pos = (float)(a.L - 1);
+  const float pos = (float)a.qpos;
   float* qr = ws + w.off_qr / 4 + ((int64_t)b * H + h0) * DR;
   for (int o = threadIdx.x; o < hpg * DR; o += blockDim.x) {
     const int hq = o / DR, j = o % DR;
@@ -411,12 +411,22 @@ __global__ void __launch_bounds__(kThreads) mla_merge_kernel(const MlaDecodeArgs
       l += e * p[1];
     }
     l = warp_sum(l);
-    if (lane == 0) s_inv_l = 1.f / l;
+    if (lane == 0) {
+      s_inv_l = 1.f / l;
+      if (a.ml_out && blockIdx.z == 0) {
+        // a split kernel that gave up on a bounded wait poisons the partial
+        // (NaN propagates through the cross-range merge), as the combine
+        // step does for a whole decode
+        const bool failed = *reinterpret_cast<const int*>(reinterpret_cast<const unsigned char*>(ws) + w.off_err) != 0;
+        a.ml_out[((int64_t)b * H + h) * 2] = failed ? __int_as_float(0x7fc00000) : mx;
+        a.ml_out[((int64_t)b * H + h) * 2 + 1] = l;
+      }
+    }
   }
   __syncthreads();
   const int64_t step = (int64_t)H * R;
   const float* pc = pacc + (((int64_t)i0 + b) * H + h) * R + r0;
-  float* av = const_cast<float*>(ws) + w.off_av / 4 + ((int64_t)b * H + h) * R + r0;
+  float* av = (a.av_out ? a.av_out : const_cast<float*>(ws) + w.off_av / 4) + ((int64_t)b * H + h) * R + r0;
   if ((R & 3) == 0)
     merge_cols<float4>(pc, step, wgt, n, r1 - r0, s_inv_l, av, red);
   else
@@ -579,7 +589,60 @@ int decode_t(const MlaDecodeArgs& a) {
   if (st) return st;
   st = launch_smem(mla_merge_kernel<T>, dim3(H, B, w.rchunks), merge_smem_bytes(w), a.stream, a, w);
   if (st) return st;
+  if (a.av_out) return B200MM_OK;  // a partial decode stops at the range's merged latent
   return launch_smem(mla_combine_kernel<T>, dim3(a.s.KV, B, (a.s.D + kCombDims - 1) / kCombDims),
+                     combine_smem_bytes(a.s), a.stream, a, w);
+}
+
+// --- merge of per-range partials (a context split across GPUs) --------------
+// grid: (H, B); block 256.  Range r covered its tokens with max score m_r and
+// sum of exp s_r and left av_r normalised over them:
+//   av[b,h,:] = sum_r s_r e^(m_r - M) av_r / sum_r s_r e^(m_r - M),  M = max_r m_r
+__global__ void __launch_bounds__(kThreads) mla_rank_merge_kernel(const MlaDecodeArgs a, MlaWorkspace w,
+                                                                  const float* __restrict__ avp,
+                                                                  const float* __restrict__ mlp, int n) {
+  const int H = a.s.H, R = a.s.R, B = a.s.B;
+  const int h = blockIdx.x, b = blockIdx.y;
+  __shared__ float wgt[64];
+  pdl_trigger();
+  pdl_wait();
+  // the W_uv step that follows checks this workspace's error flag: nothing
+  // here waits, so it is clear (a failed range already carries NaN)
+  if (h == 0 && b == 0 && threadIdx.x == 0)
+    *reinterpret_cast<int*>(static_cast<unsigned char*>(a.ws) + w.off_err) = 0;
+  if (threadIdx.x < 32) {
+    float mx = -INFINITY;
+    for (int r = threadIdx.x; r < n; r += 32) mx = fmaxf(mx, mlp[(((int64_t)r * B + b) * H + h) * 2]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float tot = 0.f;
+    for (int r = threadIdx.x; r < n; r += 32) {
+      const float* p = mlp + (((int64_t)r * B + b) * H + h) * 2;
+      const float e = p[1] > 0.f ? p[1] * expf(p[0] - mx) : 0.f;
+      wgt[r] = e;
+      tot += e;
+    }
+    tot = warp_sum(tot);
+    for (int r = threadIdx.x; r < n; r += 32) wgt[r] /= tot;
+  }
+  __syncthreads();
+  float* av = static_cast<float*>(a.ws) + w.off_av / 4 + ((int64_t)b * H + h) * R;
+  for (int c = threadIdx.x; c < R; c += blockDim.x) {
+    float s = 0.f;
+    for (int r = 0; r < n; ++r) s = fmaf(wgt[r], avp[(((int64_t)r * B + b) * H + h) * R + c], s);
+    av[c] = s;
+  }
+}
+
+template <typename T>
+int combine_partials_t(const MlaDecodeArgs& a, const float* avp, const float* mlp, int n) {
+  const MlaWorkspace w = mla_plan(a.s, 1, false);
+  int st = launch_pdl(mla_rank_merge_kernel, dim3(a.s.H, a.s.B), dim3(kThreads), 0, a.stream, a, w, avp, mlp, n) ==
+                   cudaSuccess
+               ? B200MM_OK
+               : B200MM_ERR_LAUNCH;
+  if (st) return st;
+  return launch_smem(mla_combine_kernel<T>, dim3(a.s.KV, a.s.B, (a.s.D + kCombDims - 1) / kCombDims),
                      combine_smem_bytes(a.s), a.stream, a, w);
 }
 
@@ -640,6 +703,12 @@ int mla_append_launch(const MlaAppendArgs& a) {
   if (a.s.dtype == B200MM_BF16) return append_t<__nv_bfloat16>(a);
   if (a.s.dtype == B200MM_F16) return append_t<__half>(a);
   return append_t<float>(a);
+}
+
+int mla_combine_partials_launch(const MlaDecodeArgs& a, const float* av_parts, const float* ml_parts, int nparts) {
+  if (a.s.dtype == B200MM_BF16) return combine_partials_t<__nv_bfloat16>(a, av_parts, ml_parts, nparts);
+  if (a.s.dtype == B200MM_F16) return combine_partials_t<__half>(a, av_parts, ml_parts, nparts);
+  return combine_partials_t<float>(a, av_parts, ml_parts, nparts);
 }
 
 int mla_decode_launch(const MlaDecodeArgs& a) {

@@ -29,6 +29,9 @@ struct MlaDecodeArgs {
   void* out; int64_t o_sb;
   void* ws; size_t ws_bytes;
   cudaStream_t stream;
+  int64_t qpos;             // position of the query token (L - 1 unless the tokens are a slice of the context)
+  float* av_out;            // partial decode: the merged latent of the range [B, H, R] (normalised over it) ...
+  float* ml_out;            // ... and its (max score, sum of exp) per (row, head) [B, H, 2]; no W_uv step
 };
 
 // Work plan shared by the split kernels and the combine kernel.
@@ -91,6 +94,9 @@ constexpr int64_t kMlaFillTcMinTokens = 64;
 bool mla_fill_tc_supported(const MlaAppendArgs& a);
 int mla_fill_tc_launch(const MlaAppendArgs& a);
 int mla_decode_launch(const MlaDecodeArgs& a);
+// merge per-range partials (av_parts [n][B][H][R], ml_parts [n][B][H][2]) into the
+// workspace's av, then the W_uv step into a.out
+int mla_combine_partials_launch(const MlaDecodeArgs& a, const float* av_parts, const float* ml_parts, int nparts);
 
 // production-shape split kernel (R=256, D=128, DR=32, H=32, KV=8, 16-bit dtype)
 struct MlaMaps {

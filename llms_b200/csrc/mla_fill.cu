@@ -17,7 +17,7 @@
 //               tokens] (64 KB, 128-byte swizzle), into a 2-slot ring, so the
 //               next tile's rows stream in under this tile's MMAs;
 //   warp 1      TMA: W_uk boxes [64 k x 192 rows] (24 KB, from L2: all SMs
-//               read the same 393 KB) into a 3-stage ring;
+//               read the same 393 KB) into a 4-stage ring;
 //   warp 2      TMEM allocation; one thread issues tcgen05.mma (kind::f16,
 //               M = 128, N = 192, K = 16) into two accumulator buffers of 192
 //               columns, so chunk j + 1 accumulates while chunk j is read;
@@ -42,7 +42,7 @@ constexpr int NCHUNK = FKV * FDN / CN;           // 4
 constexpr int KB = FR / 64;                      // 64-wide K boxes: 4
 constexpr uint32_t A_BYTES = TM * FR * 2;        // 64 KB: one tile's latent rows
 constexpr uint32_t W_BYTES = CN * 64 * 2;        // 24 KB: one W_uk box
-constexpr int A_SLOTS = 2, W_STAGES = 3;
+constexpr int A_SLOTS = 2, W_STAGES = 4;
 constexpr uint32_t kTmemCols = 512;              // two accumulator buffers
 constexpr uint32_t kBufCols = 256;               // buffer b at column 256 b (CN used)
 constexpr int kThreads = 11 * 32;
@@ -219,6 +219,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int u = blockIdx.x + j * gridDim.x, b = u / p.tiles_per_row, i = u % p.tiles_per_row;
       const int64_t t = p.t0 + (int64_t)i * TM + 32 * q + lane;
       const bool valid = t < p.t1;
+      const T* krow = static_cast<const T*>(p.kr) + (int64_t)b * p.r_sb + t * p.r_st + h * FDR;
+      // k_rope_pre of this thread's groups, one chunk ahead of its use: the
+      // loads are in flight while the accumulators are read and the previous
+      // group is rotated
+      uint4 kx[2][FDR / 8];
+      auto load_kr = [&](uint4 (&dst)[FDR / 8], int n) {
+#pragma unroll
+        for (int c = 0; c < FDR / 8; ++c)
+          dst[c] = valid ? *reinterpret_cast<const uint4*>(krow + 2 * n * FDR + 8 * c) : make_uint4(0, 0, 0, 0);
+      };
+      load_kr(kx[0], 0);
       float sn[half], cs[half];
       if (valid) {
 #pragma unroll
@@ -227,8 +238,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // chunk n holds groups 2n and 2n + 1: this warp takes group 2n + h --
       // its 96 accumulator columns first (so the buffer is handed back to the
       // MMAs at once), then the group's RoPE half from the token's own row
-#pragma unroll 1
+#pragma unroll
       for (int n = 0; n < NCHUNK; ++n, ++jc) {
+        if (n + 1 < NCHUNK) load_kr(kx[(n + 1) & 1], n + 1);
         const int buf = jc & 1;
         float ssq = 0.f;
         if (!bad) {
@@ -248,10 +260,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!valid) continue;
         const int grp = 2 * n + h;
-        const T* src = static_cast<const T*>(p.kr) + (int64_t)b * p.r_sb + t * p.r_st + grp * FDR;
         float x[FDR];
 #pragma unroll
-        for (int c = 0; c < FDR / 8; ++c) Chunk<T>::unpack(*reinterpret_cast<const uint4*>(src + 8 * c), x + 8 * c);
+        for (int c = 0; c < FDR / 8; ++c) Chunk<T>::unpack(kx[n & 1][c], x + 8 * c);
         float z[FDR];
 #pragma unroll
         for (int jj = 0; jj < FDR; ++jj) {

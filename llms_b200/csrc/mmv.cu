@@ -299,6 +299,11 @@ inline bool al16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 int cluster_of(const DenseArgs& a) {
   const int groups = (a.N + kRows - 1) / kRows;
   int cs = groups * 4 < num_sms(current_device()) ? 8 : 4;
+  // int8 weights up to 16 rows: a unit is half the bytes of a 16-bit one, so
+  // the eight-way split keeps twice the CTAs streaming (measured, Qwen3-8B
+  // int8 at M = 16: QKV 22.6 -> 15.7 us, gate-up 47.5 -> 45.0 us; at M = 32
+  // it was slower)
+  if (a.w8 && a.M <= 16) cs = 8;
 #ifdef SWAP_TRACE
   if (const char* e = getenv("B200MM_MMV_CS")) cs = atoi(e) == 8 ? 8 : 4;
 #endif

@@ -19,6 +19,8 @@
 //               is handed back to the issuer.
 // Every mbarrier wait is bounded; a CTA whose wait expires stops issuing,
 // drains its own copies in flight, frees TMEM and writes NaN over its tiles.
+#include <type_traits>
+
 #include "dense.cuh"
 #include "tcgen05.cuh"
 
@@ -40,7 +42,7 @@ struct Cfg {
   static constexpr int STAGES = (200 * 1024 / STAGE_BYTES) > 8 ? 8 : (200 * 1024 / STAGE_BYTES);
   static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
   static_assert(NB * BN <= (int)kTmemCols, "accumulators exceed the TMEM allocation");
-  static_assert(BN % 32 == 0 && BN >= 32 && NB * BN <= 256, "MMA N = NB * BN must be a multiple of 32 in [32, 256]");
+  static_assert(BN % 16 == 0 && BN >= 32 && NB * BN <= 256, "MMA N = NB * BN must be a multiple of 16 in [32, 256]");
   static_assert(B_BYTES % 1024 == 0, "W boxes must keep the 1024-byte swizzle-atom alignment");
 };
 
@@ -54,6 +56,12 @@ struct TcParams {
 template <typename T, int N>
 constexpr uint32_t idesc() {
   return idesc_f16<T>(BM, N);
+}
+
+template <int WC>
+__device__ __forceinline__ void tmem_ldn(uint32_t taddr, float* v) {
+  if constexpr (WC == 32) tmem_ld32(taddr, v);
+  else tmem_ld16(taddr, v);
 }
 
 template <typename T> __device__ __forceinline__ uint32_t pack_out(float a, float b);
@@ -72,7 +80,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const __grid_constant__ CUtensorMap mw1, const TcParams p) {
   using C = Cfg<GATE, BN>;
   constexpr uint32_t ACC = C::NB * BN;  // TMEM columns of one tile's accumulators
-  static_assert(2 * ACC <= kTmemCols, "two accumulator buffers must fit the TMEM allocation");
+  constexpr uint32_t BUF = kTmemCols / 2;  // buffer b starts at column BUF * b (256-aligned)
+  static_assert(ACC <= BUF, "two accumulator buffers must fit the TMEM allocation");
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                        ~uintptr_t(1023));
@@ -161,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem + b * ACC;
+        const uint32_t d = tmem + b * BUF;
         for (int kb = 0; kb < nk; ++kb, ++g) {
           const int s = g % C::STAGES, it = g / C::STAGES;
           if (!mbar_wait(&full[s], (uint32_t)(it & 1)) || *failed) {
@@ -201,25 +210,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = tm * BM + 32 * q + lane;
       T* yrow = static_cast<T*>(p.y) + (int64_t)row * p.ldy;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        float v[32];
+      // one block of WC accumulator columns (32, or a 16-column tail when
+      // BN is an odd multiple of 16): TMEM -> registers -> 16-byte stores
+      auto cols = [&](int c, auto wc) {
+        constexpr int WC = decltype(wc)::value;
+        float v[WC];
         if (!bad) {
-          tmem_ld32(tq + b * ACC + c, v);
+          tmem_ldn<WC>(tq + b * BUF + c, v);
           if (GATE) {
-            float u[32];
-            tmem_ld32(tq + b * ACC + BN + c, u);
+            float u[WC];
+            tmem_ldn<WC>(tq + b * BUF + BN + c, u);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = silu_mul(v[i], u[i]);
+            for (int i = 0; i < WC; ++i) v[i] = silu_mul(v[i], u[i]);
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __int_as_float(0x7fc00000);
+          for (int i = 0; i < WC; ++i) v[i] = __int_as_float(0x7fc00000);
         }
         if (row < p.M) {
           const int n0 = tn * BN + c;
-          if (n0 + 32 <= p.N) {
+          if (n0 + WC <= p.N) {
 #pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
+            for (int jj = 0; jj < WC / 8; ++jj) {
               uint4 o;
               o.x = pack_out<T>(v[8 * jj + 0], v[8 * jj + 1]);
               o.y = pack_out<T>(v[8 * jj + 2], v[8 * jj + 3]);
@@ -229,11 +241,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
+            for (int i = 0; i < WC; ++i)
               if (n0 + i < p.N) yrow[n0 + i] = from_f<T>(v[i]);
           }
         }
-      }
+      };
+#pragma unroll 1
+      for (int c = 0; c + 32 <= BN; c += 32) cols(c, std::integral_constant<int, 32>{});
+      if constexpr (BN % 32 != 0) cols(BN - 16, std::integral_constant<int, 16>{});
       if (!bad) {
         tc_fence_before();
         mbar_arrive(&acc_empty[b]);  // buffer b may take tile j + 2

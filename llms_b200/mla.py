@@ -68,46 +68,78 @@ def batch_shard(B: int, world: int, rank: int) -> range:
     return range(B * rank // world, B * (rank + 1) // world)
 
 
-def decode_shard(B: int, KV: int, world: int, rank: int) -> tuple[range, range]:
-    """Batch rows and KV groups of an MLA decode that GPU ``rank`` of ``world``
-    serves.  With ``B >= world``: a batch-row split (``batch_shard``), every
-    group.  With fewer rows than GPUs: the groups are split too -- ``gs``
-    group shards (the divisor of KV that keeps the most GPUs busy) times
-    ``world // gs`` row shards; rank r takes row shard ``r // gs`` and group
-    shard ``r % gs``.  A group shard reads the whole latent of its rows (the
-    latent is shared by every group) but only its groups' RoPE'd keys and
-    scales, and serves only those groups' heads.  No collective inside the
-    op; surplus ranks get empty ranges."""
-    if world < 1 or not 0 <= rank < world or B < 0 or KV < 1:
-        raise ValueError(f"bad shard request: B={B} KV={KV} world={world} rank={rank}")
+def decode_shard(B: int, L: int, world: int, rank: int) -> tuple[range, range]:
+    """Batch rows and context tokens of an MLA decode step that GPU ``rank`` of
+    ``world`` serves.  With ``B >= world``: a batch-row split (``batch_shard``),
+    each rank its rows' whole context, no collective.  With fewer rows than
+    GPUs: a context split -- every rank streams its slice
+    ``[L*r/world, L*(r+1)/world)`` of every row's cache
+    (``mla_decode_partial``), and the slices' partial softmaxes meet in one
+    small exchange (B x H x (R + 2) floats per rank) before the W_uv step
+    (``mla_combine_partials``): the flash-decoding split, across GPUs."""
+    if world < 1 or not 0 <= rank < world or B < 0 or L < 1:
+        raise ValueError(f"bad shard request: B={B} L={L} world={world} rank={rank}")
     if B >= world or B == 0:
-        return batch_shard(B, world, rank), range(KV)
-    # the divisor of KV that keeps the most GPUs busy (ties: fewer group
-    # shards, i.e. less replicated latent reading)
-    gs = max((d for d in range(1, KV + 1) if KV % d == 0 and d <= world),
-             key=lambda d: (min(world // d, B) * d, -d))
-    rs = world // gs
-    if rank >= rs * gs:
-        return range(0), range(0)
-    rows = batch_shard(B, rs, rank // gs)
-    gi = rank % gs
-    return rows, range(KV * gi // gs, KV * (gi + 1) // gs)
+        return batch_shard(B, world, rank), range(0, L)
+    if L < world:
+        raise ValueError(f"a context of {L} tokens cannot be split over {world} GPUs")
+    return range(0, B), range(L * rank // world, L * (rank + 1) // world)
 
 
-def mla_decode_shard(q: torch.Tensor, c_kv: torch.Tensor, kz: torch.Tensor | None, kscale: torch.Tensor,
-                     w_uk: torch.Tensor | None, w_uv: torch.Tensor, k_norm_w: torch.Tensor,
-                     inv_freq: torch.Tensor | None, *, rows: range, groups: range, L: int, scale: float,
-                     eps: float) -> torch.Tensor:
-    """``mla_decode`` of batch rows ``rows`` and KV groups ``groups`` only
-    (``decode_shard``): the heads of those groups, ``(len(rows), hpg *
-    len(groups), D)``.  The slices are views (no copy): the side-bands keep
-    their token strides and the kernels read only the selected groups."""
-    KV, H = w_uv.shape[0], q.shape[1]
-    hpg = H // KV
-    r0, r1, g0, g1 = rows.start, rows.stop, groups.start, groups.stop
-    return mla_decode(q[r0:r1, g0 * hpg:g1 * hpg], c_kv[r0:r1], None if kz is None else kz[r0:r1, :, g0:g1],
-                      kscale[r0:r1, :, g0:g1], None if w_uk is None else w_uk[g0:g1], w_uv[g0:g1], k_norm_w,
-                      inv_freq, L=L, scale=scale, eps=eps)
+def mla_decode_partial(q: torch.Tensor, c_kv: torch.Tensor, kz: torch.Tensor | None, kscale: torch.Tensor,
+                       w_uk: torch.Tensor | None, k_norm_w: torch.Tensor, inv_freq: torch.Tensor | None, *,
+                       num_kv_heads: int, L: int, tokens: range, scale: float, eps: float,
+                       workspace: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """The decode step over cache tokens ``tokens`` only, for a query at
+    position ``L - 1``: returns ``av`` fp32 (B, H, R) (the latent mixed by the
+    softmax over those tokens) and ``ml`` fp32 (B, H, 2) (their max score and
+    sum of exp).  No W_uv step: ``mla_combine_partials`` merges ranges."""
+    B, H, D = q.shape
+    R = c_kv.shape[-1]
+    DR = 0 if kz is None else kz.shape[-1]
+    _capi.require_cuda(q, c_kv, kscale)
+    if q.stride(-1) != 1 or q.stride(1) != D:
+        q = q.contiguous()
+    shp = _shape(B, H, num_kv_heads, D, DR, R, q.dtype, eps)
+    n = len(tokens)
+    ws_bytes = int(_capi.lib.b200mm_mla_decode_workspace_size(ctypes.byref(shp), max(n, 1)))
+    if workspace is None or workspace.numel() < ws_bytes:
+        workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
+    av = torch.empty((B, H, R), dtype=torch.float32, device=q.device)
+    ml = torch.empty((B, H, 2), dtype=torch.float32, device=q.device)
+    with _capi.on_device(q):
+        st = _capi.lib.b200mm_mla_decode_partial(
+            ctypes.byref(shp), q.data_ptr(), q.stride(0), c_kv.data_ptr(), c_kv.stride(0), c_kv.stride(1),
+            _ptr(kz), 0 if kz is None else kz.stride(0), 0 if kz is None else kz.stride(1),
+            kscale.data_ptr(), kscale.stride(0), kscale.stride(1), _ptr(w_uk), k_norm_w.data_ptr(), _ptr(inv_freq),
+            float(scale), L, tokens.start, tokens.stop, av.data_ptr(), ml.data_ptr(), workspace.data_ptr(),
+            workspace.numel(), _capi.stream_of(q))
+    _capi.check(st, "b200mm_mla_decode_partial")
+    return av, ml
+
+
+def mla_combine_partials(av_parts: torch.Tensor, ml_parts: torch.Tensor, w_uv: torch.Tensor, *, head_dim: int,
+                         d_rope: int, dtype: torch.dtype, eps: float, out: torch.Tensor | None = None,
+                         workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Merge the partial decodes of ``n`` token ranges (``av_parts`` (n, B, H,
+    R), ``ml_parts`` (n, B, H, 2), fp32, as gathered from the ranks) and apply
+    W_uv: the decode output (B, H, D) in ``dtype``."""
+    n, B, H, R = av_parts.shape
+    KV = w_uv.shape[0]
+    _capi.require_cuda(av_parts, ml_parts, w_uv)
+    shp = _shape(B, H, KV, head_dim, d_rope, R, dtype, eps)
+    ws_bytes = int(_capi.lib.b200mm_mla_decode_workspace_size(ctypes.byref(shp), 1))
+    if workspace is None or workspace.numel() < ws_bytes:
+        workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=av_parts.device)
+    if out is None:
+        out = torch.empty((B, H, head_dim), dtype=dtype, device=av_parts.device)
+    av_parts, ml_parts = av_parts.contiguous(), ml_parts.contiguous()
+    with _capi.on_device(av_parts):
+        st = _capi.lib.b200mm_mla_combine_partials(
+            ctypes.byref(shp), av_parts.data_ptr(), ml_parts.data_ptr(), n, w_uv.data_ptr(), out.data_ptr(),
+            out.stride(0), workspace.data_ptr(), workspace.numel(), _capi.stream_of(av_parts))
+    _capi.check(st, "b200mm_mla_combine_partials")
+    return out
 
 
 def workspace_bytes(B: int, H: int, KV: int, D: int, DR: int, R: int, L: int, dtype, eps: float = 1e-6) -> int:

@@ -90,23 +90,44 @@ def test_q_latent_weight_is_one_buffer_of_views():
 
 @pytest.mark.parametrize("B", [1, 2, 3, 8, 32])
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
-def test_decode_shards_cover_every_row_and_group_once(B, world):
+def test_decode_shards_cover_every_row_and_token_once(B, world):
     from llms_b200.mla import decode_shard
-    KV = 8
-    seen = np.zeros((B, KV), int)
-    busy = 0
+    L = 1000
+    seen = np.zeros((B, L), int)
     for r in range(world):
-        rows, groups = decode_shard(B, KV, world, r)
-        for b in rows:
-            for g in groups:
-                seen[b, g] += 1
-        busy += bool(len(rows) and len(groups))
+        rows, toks = decode_shard(B, L, world, r)
+        seen[rows.start:rows.stop, toks.start:toks.stop] += 1
+        if B < world:  # fewer rows than GPUs: every GPU streams a slice of every row
+            assert len(rows) == B and len(toks) > 0
     assert (seen == 1).all()
-    if B < world:  # fewer rows than GPUs: the group split keeps (nearly) every GPU busy
-        assert busy >= min(world, B * KV) - (world % B if B > 1 else 0)
 
 
-def _group_worker(rank, world, port, out):
+def _partial(d, rows, toks, inv, L):
+    """Float64 restatement of one context range's partial decode: the softmax
+    of the range's tokens (max m, sum s) and the latent they mix (av)."""
+    from oracle import reference_math as O
+    q = np.asarray(d["q"][rows], np.float64)
+    c = np.asarray(d["c_kv"][rows], np.float64)
+    kr = np.asarray(d["k_rope_pre"][rows], np.float64)
+    B, H, D = q.shape
+    KV, DN, R = d["w_uk"].shape
+    DR = D - DN
+    k_nope = np.einsum("blr,gnr->blgn", c[:, :L], np.asarray(d["w_uk"], np.float64))
+    k = O.rms_norm(np.concatenate([k_nope, kr[:, :L]], -1), d["k_norm_w"], 1e-6)
+    cq, sq = O.rope_cos_sin(np.array([L - 1]), inv)
+    ck, sk = O.rope_cos_sin(np.arange(L), inv)
+    qr = q[..., DN:]
+    q = np.concatenate([q[..., :DN], qr * cq[0] + O.rotate_half(qr) * sq[0]], -1)
+    krr = k[..., DN:] * ck[None, :, None] + O.rotate_half(k[..., DN:]) * sk[None, :, None]
+    k = np.repeat(np.concatenate([k[..., :DN], krr], -1), H // KV, axis=2)[:, toks.start:toks.stop]
+    s = np.einsum("bhd,blhd->bhl", q, k) * D ** -0.5
+    m = s.max(-1)
+    p = np.exp(s - m[..., None])
+    av = np.einsum("bhl,blr->bhr", p, c[:, toks.start:toks.stop]) / p.sum(-1)[..., None]
+    return m, p.sum(-1), av
+
+
+def _context_worker(rank, world, port, out):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     import torch.distributed as dist
     from llms_b200.mla import decode_shard
@@ -114,34 +135,31 @@ def _group_worker(rank, world, port, out):
     from oracle import reference_math as O
 
     dist.init_process_group("gloo", rank=rank, world_size=world)
-    B, L, dims = 1, 40, dict(H=8, KV=4, D=32, DR=8, R=24)
+    B, L, dims = 1, 40, dict(H=8, KV=2, D=32, DR=8, R=24)
     d = I.cfg4(B, L, seed=9, **dims)
     inv = O.mla_inv_freq(dims["D"], dims["DR"], 1e6)
-    rows, groups = decode_shard(B, dims["KV"], world, rank)
-    hpg = dims["H"] // dims["KV"]
-    g0, g1 = groups.start, groups.stop
-    # this rank reads its rows' whole latent, but only its groups' keys and heads
-    mine = O.mla_decode(d["q"][list(rows)][:, g0 * hpg:g1 * hpg], d["c_kv"][list(rows)],
-                        d["k_rope_pre"][list(rows)][:, :, g0:g1], d["w_uk"][g0:g1], d["w_uv"][g0:g1],
-                        d["k_norm_w"], 1e-6, inv, L)
+    rows, toks = decode_shard(B, L, world, rank)
+    mine = _partial(d, list(rows), toks, inv, L)  # this rank streams only its token slice
     parts = [None] * world
-    dist.all_gather_object(parts, (list(rows), (g0, g1), mine))
+    dist.all_gather_object(parts, mine)  # the one exchange: B x H x (R + 2) numbers per rank
     if rank == 0:
+        M = np.max([m for m, _, _ in parts], axis=0)
+        wts = [s * np.exp(m - M) for m, s, _ in parts]
+        av = sum(w[..., None] * a for w, (_, _, a) in zip(wts, parts)) / sum(wts)[..., None]
+        g_of = np.arange(dims["H"]) // (dims["H"] // dims["KV"])
+        got = np.einsum("bhr,hdr->bhd", av, np.asarray(d["w_uv"], np.float64)[g_of])
         full = O.mla_decode(d["q"], d["c_kv"], d["k_rope_pre"], d["w_uk"], d["w_uv"], d["k_norm_w"], 1e-6, inv, L)
-        got = np.full_like(full, np.nan)
-        for rws, (a, b), m in parts:
-            if rws and b > a:
-                got[rws, a * hpg:b * hpg] = m
         out.put(float(np.abs(got - full).max()))
     dist.destroy_process_group()
 
 
-def test_group_sharded_decode_gathers_to_full_output_gloo():
-    """B = 1 on two ranks: each rank serves half the KV groups' heads."""
+def test_context_split_decode_merges_to_full_output_gloo():
+    """B = 1 on two ranks: each rank takes half the context; the merged
+    partials equal the unsharded decode."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = 29900 + os.getpid() % 1000
-    procs = [ctx.Process(target=_group_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_context_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
     err = q.get(timeout=120)
