@@ -16,8 +16,10 @@
 //   warp 0      TMA: the tile's latent rows, one 4-D box [4 x 64 cols x 128
 //               tokens] (64 KB, 128-byte swizzle), into a 2-slot ring, so the
 //               next tile's rows stream in under this tile's MMAs;
-//   warp 1      TMA: W_uk boxes [64 k x 192 rows] (24 KB, from L2: all SMs
-//               read the same 393 KB) into a 4-stage ring;
+//   warp 1      TMA: W_uk stages of two boxes [64 k x 192 rows] (48 KB, one
+//               3-D load; all SMs read the same 393 KB from L2) into a
+//               2-stage ring -- one stage per commit, since every
+//               tcgen05.commit stalls the issuing thread;
 //   warp 2      TMEM allocation; one thread issues tcgen05.mma (kind::f16,
 //               M = 128, N = 192, K = 16) into two accumulator buffers of 192
 //               columns, so chunk j + 1 accumulates while chunk j is read;
@@ -41,8 +43,9 @@ constexpr int CN = 192;                          // W_uk rows per chunk (MMA N):
 constexpr int NCHUNK = FKV * FDN / CN;           // 4
 constexpr int KB = FR / 64;                      // 64-wide K boxes: 4
 constexpr uint32_t A_BYTES = TM * FR * 2;        // 64 KB: one tile's latent rows
-constexpr uint32_t W_BYTES = CN * 64 * 2;        // 24 KB: one W_uk box
-constexpr int A_SLOTS = 2, W_STAGES = 4;
+constexpr int WKB = 2;                           // K boxes per W stage (one TMA, one commit)
+constexpr uint32_t W_BYTES = WKB * CN * 64 * 2;  // 48 KB: two W_uk boxes [64 k x 192 rows]
+constexpr int A_SLOTS = 2, W_STAGES = 2;
 constexpr uint32_t kTmemCols = 512;              // two accumulator buffers
 constexpr uint32_t kBufCols = 256;               // buffer b at column 256 b (CN used)
 constexpr int kThreads = 11 * 32;
@@ -50,6 +53,8 @@ constexpr int kEpi = 8 * 32;                     // epilogue threads
 constexpr size_t kSmem = (size_t)A_SLOTS * A_BYTES + (size_t)W_STAGES * W_BYTES + 1024 + 256;
 static_assert(FKV * FDN % CN == 0 && CN == 2 * FDN, "a chunk is exactly two groups");
 static_assert(W_BYTES % 1024 == 0 && A_BYTES % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
+static_assert(KB % WKB == 0, "a chunk's K boxes fill whole stages");
+static_assert(kSmem + 1024 <= 232448, "shared memory (with the static arrays) fits one CTA");
 static_assert(CN <= (int)kBufCols && 2 * kBufCols <= kTmemCols, "two accumulator buffers fit the allocation");
 
 template <typename T>
@@ -57,6 +62,20 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   const T lo = from_f<T>(a), hi = from_f<T>(b);
   return (uint32_t)(*reinterpret_cast<const uint16_t*>(&lo)) | ((uint32_t)(*reinterpret_cast<const uint16_t*>(&hi)) << 16);
 }
+
+#ifdef FILL_TRACE
+// Development trace (trace builds only): %globaltimer per (CTA < 4, tile < 8,
+// event < 16), read back with b200mm_fill_trace.
+__device__ unsigned long long g_fill_trace[4][8][16];
+#define FTRACE(j, e)                                                                    \
+  do {                                                                                  \
+    if (blockIdx.x < 4 && (j) < 8) g_fill_trace[blockIdx.x][(j)][(e)] = global_ns();   \
+  } while (0)
+#else
+#define FTRACE(j, e) \
+  do {               \
+  } while (0)
+#endif
 
 struct FillParams {
   int64_t t0, t1;
@@ -141,6 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (*failed) break;
         mbar_expect_tx(&a_full[s], A_BYTES);
+        FTRACE(j, 11);
         tma_load_4d(sa + s * A_BYTES, &mc, 0, (int)(p.t0 + (int64_t)i * TM), 0, b, &a_full[s]);
       }
       *a_issued = j;
@@ -152,7 +172,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int j = 0; ok && j < mine; ++j)
         for (int n = 0; ok && n < NCHUNK; ++n)
-          for (int kb = 0; kb < KB; ++kb, ++g) {
+          for (int kb = 0; kb < KB; kb += WKB, ++g) {
             const int s = g % W_STAGES;
             if (g >= W_STAGES && !mbar_wait(&w_empty[s], (uint32_t)(((g / W_STAGES) - 1) & 1))) ok = false;
             if (!ok || *failed) {
@@ -160,7 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             mbar_expect_tx(&w_full[s], W_BYTES);
-            tma_load_2d(sw + s * W_BYTES, &mw, kb * 64, n * CN, &w_full[s]);
+            tma_load_3d(sw + s * W_BYTES, &mw, 0, n * CN, kb, &w_full[s]);
           }
       if (!ok) *failed = 1;
       *w_issued = g;
@@ -173,11 +193,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (; ok && j < mine; ++j) {
         const int s = j % A_SLOTS;
+        FTRACE(j, 0);
         if (!mbar_wait(&a_full[s], (uint32_t)((j / A_SLOTS) & 1)) || *failed) {
           ok = false;
           break;
         }
         tc_fence_after();
+        FTRACE(j, 1);
         const uint32_t abase = smem_u32(sa + s * A_BYTES);
         for (int n = 0; ok && n < NCHUNK; ++n, ++jc) {
           const int buf = jc & 1;
@@ -187,19 +209,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint32_t d = tmem + buf * kBufCols;
-          for (int kb = 0; kb < KB; ++kb, ++g) {
+          for (int kb = 0; kb < KB; kb += WKB, ++g) {
             const int ws = g % W_STAGES;
             if (!mbar_wait(&w_full[ws], (uint32_t)((g / W_STAGES) & 1)) || *failed) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint64_t ad = sdesc(abase + kb * (TM * 128)), bd = sdesc(smem_u32(sw + ws * W_BYTES));
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) mma_f16(d, ad + 2 * kk, bd + 2 * kk, ID, (kb | kk) != 0);
-            mma_commit(&w_empty[ws]);
+            for (int kw = 0; kw < WKB; ++kw) {
+              const uint64_t ad = sdesc(abase + (kb + kw) * (TM * 128));
+              const uint64_t bd = sdesc(smem_u32(sw + ws * W_BYTES + kw * (CN * 128)));
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) mma_f16(d, ad + 2 * kk, bd + 2 * kk, ID, (kb | kw | kk) != 0);
+            }
+            mma_commit(&w_empty[ws]);  // one commit per two K boxes: each commit stalls the issuer
           }
           if (ok) mma_commit(&acc_full[buf]);
+          FTRACE(j, 2 + n);
         }
         if (ok) mma_commit(&a_empty[s]);  // the tile's rows may be overwritten once its MMAs complete
       }
@@ -247,6 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           bad = !mbar_wait(&acc_full[buf], (uint32_t)((jc >> 1) & 1)) || *failed;
           tc_fence_after();
         }
+        if (warp == 3 && lane == 0) FTRACE(j, 6 + n);
         if (!bad) {
 #pragma unroll
           for (int c = 0; c < FDN; c += 32) {
@@ -318,7 +346,8 @@ int launch_t(const MlaAppendArgs& a) {
   const uint32_t box[4] = {64, (uint32_t)TM, 4, 1};
   CUtensorMap mc, mw;
   if (!make_map_4d(&mc, dt, a.c_kv, cd, cs, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map_2d(&mw, dt, a.w_uk, FR, (uint64_t)FKV * FDN, FR * 2, 64, CN, CU_TENSOR_MAP_SWIZZLE_128B))
+      !make_map_3d(&mw, dt, a.w_uk, 64, (uint64_t)FKV * FDN, KB, FR * 2, 128, 64, CN, WKB,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
     return B200MM_ERR_ALIGN;
   auto kern = mla_fill_tc_kernel<T>;
   static bool configured[64] = {false};
@@ -360,6 +389,12 @@ bool mla_fill_tc_supported(const MlaAppendArgs& a) {
   if (!al16(a.kz) || (a.z_st * 2) % 16 || (a.z_sb * 2) % 16) return false;
   return true;
 }
+
+#ifdef FILL_TRACE
+extern "C" int b200mm_fill_trace(void* dst) {
+  return cudaMemcpyFromSymbol(dst, g_fill_trace, sizeof(g_fill_trace)) == cudaSuccess ? 0 : 4;
+}
+#endif
 
 int mla_fill_tc_launch(const MlaAppendArgs& a) {
   if (a.s.dtype == B200MM_BF16) return launch_t<__nv_bfloat16>(a);
