@@ -32,3 +32,22 @@ def test_reference_arm_prints_contract_line():
 def test_reference_arm_other_ranks_exit_quietly():
     r = _run({"WORLD_SIZE": "2", "RANK": "1"})
     assert r.returncode == 0 and r.stdout.strip() == "", (r.stdout, r.stderr[-2000:])
+
+
+def test_submetrics_summarise_the_suite():
+    """The compact `submetrics` key: each BASELINE sub-metric with its
+    fraction of the measured peak (GB/s of HBM, TFLOP/s of dense bf16)."""
+    import sys
+    sys.path.insert(0, str(ROOT))
+    import bench
+    hbm, tf, _ = bench.measured_peaks()
+    suite = {"qkv_m1": {"us_per_launch": 7.0, "GB/s": hbm / 2},
+             "qkv_m2048": {"us_per_launch": 60.0, "TFLOP/s": tf / 4},
+             "mla_b32_l32768": {"us_per_step": 229.0, "GB/s": hbm * 0.75},
+             "mla_sideband_fill_b32_l32768": {"us": 575.0, "x_decode_step": 2.5, "TFLOP/s": 700.0}}
+    sm = bench.submetrics(suite)
+    assert sm["qkv_m1"]["frac"] == 0.5 and sm["qkv_m1"]["us"] == 7.0
+    assert sm["qkv_m2048"]["frac"] == 0.25
+    assert sm["mla_b32_l32768"]["frac"] == 0.75 and sm["mla_b32_l32768"]["us"] == 229.0
+    assert sm["mla_sideband_fill_b32_l32768"]["x_decode_step"] == 2.5
+    assert "gate_up_m1" not in sm  # absent parts are left out, not invented
