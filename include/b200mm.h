@@ -274,8 +274,10 @@ int b200mm_mla_decode(const b200mm_mla_shape* shape,
  *   the softmax over the range -- and ml_out fp32 [B, H, 2] -- the range's
  *   (max score, sum of exp).  No W_uv step.  Workspace as
  *   b200mm_mla_decode_workspace_size(shape, t_end - t_begin).
- * b200mm_mla_combine_partials: nparts ranges' av / ml stacked [nparts, B, H, R]
- *   and [nparts, B, H, 2] (nparts <= 64) -> out [B, H, D] =
+ * b200mm_mla_combine_partials: nparts ranges' partials -- range r's av
+ *   [B, H, R] at av_parts + r * av_part_stride and its ml [B, H, 2] at
+ *   ml_parts + r * ml_part_stride (elements; nparts <= 64; so one gathered
+ *   buffer per rank can hold both) -> out [B, H, D] =
  *   W_uv . (sum_r s_r e^(m_r - M) av_r / sum_r s_r e^(m_r - M)).  Workspace as
  *   b200mm_mla_decode_workspace_size(shape, 1).
  * No reference counterpart of the split itself: the reference runs one GPU.
@@ -293,7 +295,8 @@ int b200mm_mla_decode_partial(const b200mm_mla_shape* shape,
                               void* stream);
 
 int b200mm_mla_combine_partials(const b200mm_mla_shape* shape,
-                                const float* av_parts, const float* ml_parts, int64_t nparts,
+                                const float* av_parts, int64_t av_part_stride,
+                                const float* ml_parts, int64_t ml_part_stride, int64_t nparts,
                                 const void* w_uv,
                                 void* out, int64_t o_sb,
                                 void* workspace, size_t workspace_bytes,

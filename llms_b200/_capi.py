@@ -94,7 +94,8 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "b200mm_mla_combine_partials": (
         ctypes.c_int,
-        [ctypes.POINTER(MlaShape), _c_p, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p, ctypes.c_size_t, _c_p],
+        [ctypes.POINTER(MlaShape), _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_p, ctypes.c_size_t,
+         _c_p],
     ),
     "b200mm_rmsnorm": (
         ctypes.c_int,

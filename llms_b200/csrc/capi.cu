@@ -362,14 +362,16 @@ int b200mm_mla_decode_partial(const b200mm_mla_shape* shape, const void* q, int6
   return launch_status();
 }
 
-int b200mm_mla_combine_partials(const b200mm_mla_shape* shape, const float* av_parts, const float* ml_parts,
-                                int64_t nparts, const void* w_uv, void* out, int64_t o_sb, void* workspace,
-                                size_t workspace_bytes, void* stream) {
+int b200mm_mla_combine_partials(const b200mm_mla_shape* shape, const float* av_parts, int64_t av_part_stride,
+                                const float* ml_parts, int64_t ml_part_stride, int64_t nparts, const void* w_uv,
+                                void* out, int64_t o_sb, void* workspace, size_t workspace_bytes, void* stream) {
   if (!shape) return B200MM_ERR_ARG;
   int st = mla_validate_shape(*shape);
   if (st != B200MM_OK) return st;
   if (nparts < 1 || nparts > 64) return B200MM_ERR_SHAPE;
   if (!av_parts || !ml_parts || !w_uv || !out) return B200MM_ERR_ARG;
+  const int64_t bh = (int64_t)shape->B * shape->H;
+  if (av_part_stride < bh * shape->R || ml_part_stride < bh * 2) return B200MM_ERR_SHAPE;
   if (shape->B == 0) return B200MM_OK;
   MlaDecodeArgs a{};
   a.s = *shape;
@@ -380,7 +382,7 @@ int b200mm_mla_combine_partials(const b200mm_mla_shape* shape, const float* av_p
   if (!workspace || workspace_bytes < need || ((uintptr_t)workspace & 255u)) return B200MM_ERR_WORKSPACE;
   st = check_device();
   if (st != B200MM_OK) return st;
-  st = mla_combine_partials_launch(a, av_parts, ml_parts, (int)nparts);
+  st = mla_combine_partials_launch(a, av_parts, av_part_stride, ml_parts, ml_part_stride, (int)nparts);
   if (st != B200MM_OK) return st;
   return launch_status();
 }

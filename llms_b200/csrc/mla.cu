@@ -599,9 +599,10 @@ int decode_t(const MlaDecodeArgs& a) {
 // sum of exp s_r and left av_r normalised over them:
 //   av[b,h,:] = sum_r s_r e^(m_r - M) av_r / sum_r s_r e^(m_r - M),  M = max_r m_r
 __global__ void __launch_bounds__(kThreads) mla_rank_merge_kernel(const MlaDecodeArgs a, MlaWorkspace w,
-                                                                  const float* __restrict__ avp,
-                                                                  const float* __restrict__ mlp, int n) {
-  const int H = a.s.H, R = a.s.R, B = a.s.B;
+                                                                  const float* __restrict__ avp, int64_t avs,
+                                                                  const float* __restrict__ mlp, int64_t mls,
+                                                                  int n) {
+  const int H = a.s.H, R = a.s.R;
   const int h = blockIdx.x, b = blockIdx.y;
   __shared__ float wgt[64];
   pdl_trigger();
@@ -612,12 +613,12 @@ __global__ void __launch_bounds__(kThreads) mla_rank_merge_kernel(const MlaDecod
     *reinterpret_cast<int*>(static_cast<unsigned char*>(a.ws) + w.off_err) = 0;
   if (threadIdx.x < 32) {
     float mx = -INFINITY;
-    for (int r = threadIdx.x; r < n; r += 32) mx = fmaxf(mx, mlp[(((int64_t)r * B + b) * H + h) * 2]);
+    for (int r = threadIdx.x; r < n; r += 32) mx = fmaxf(mx, mlp[r * mls + ((int64_t)b * H + h) * 2]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float tot = 0.f;
     for (int r = threadIdx.x; r < n; r += 32) {
-      const float* p = mlp + (((int64_t)r * B + b) * H + h) * 2;
+      const float* p = mlp + r * mls + ((int64_t)b * H + h) * 2;
       const float e = p[1] > 0.f ? p[1] * expf(p[0] - mx) : 0.f;
       wgt[r] = e;
       tot += e;
@@ -629,16 +630,16 @@ __global__ void __launch_bounds__(kThreads) mla_rank_merge_kernel(const MlaDecod
   float* av = static_cast<float*>(a.ws) + w.off_av / 4 + ((int64_t)b * H + h) * R;
   for (int c = threadIdx.x; c < R; c += blockDim.x) {
     float s = 0.f;
-    for (int r = 0; r < n; ++r) s = fmaf(wgt[r], avp[(((int64_t)r * B + b) * H + h) * R + c], s);
+    for (int r = 0; r < n; ++r) s = fmaf(wgt[r], avp[r * avs + ((int64_t)b * H + h) * R + c], s);
     av[c] = s;
   }
 }
 
 template <typename T>
-int combine_partials_t(const MlaDecodeArgs& a, const float* avp, const float* mlp, int n) {
+int combine_partials_t(const MlaDecodeArgs& a, const float* avp, int64_t avs, const float* mlp, int64_t mls, int n) {
   const MlaWorkspace w = mla_plan(a.s, 1, false);
-  int st = launch_pdl(mla_rank_merge_kernel, dim3(a.s.H, a.s.B), dim3(kThreads), 0, a.stream, a, w, avp, mlp, n) ==
-                   cudaSuccess
+  int st = launch_pdl(mla_rank_merge_kernel, dim3(a.s.H, a.s.B), dim3(kThreads), 0, a.stream, a, w, avp, avs, mlp,
+                      mls, n) == cudaSuccess
                ? B200MM_OK
                : B200MM_ERR_LAUNCH;
   if (st) return st;
@@ -705,10 +706,11 @@ int mla_append_launch(const MlaAppendArgs& a) {
   return append_t<float>(a);
 }
 
-int mla_combine_partials_launch(const MlaDecodeArgs& a, const float* av_parts, const float* ml_parts, int nparts) {
-  if (a.s.dtype == B200MM_BF16) return combine_partials_t<__nv_bfloat16>(a, av_parts, ml_parts, nparts);
-  if (a.s.dtype == B200MM_F16) return combine_partials_t<__half>(a, av_parts, ml_parts, nparts);
-  return combine_partials_t<float>(a, av_parts, ml_parts, nparts);
+int mla_combine_partials_launch(const MlaDecodeArgs& a, const float* av_parts, int64_t av_stride,
+                                const float* ml_parts, int64_t ml_stride, int nparts) {
+  if (a.s.dtype == B200MM_BF16) return combine_partials_t<__nv_bfloat16>(a, av_parts, av_stride, ml_parts, ml_stride, nparts);
+  if (a.s.dtype == B200MM_F16) return combine_partials_t<__half>(a, av_parts, av_stride, ml_parts, ml_stride, nparts);
+  return combine_partials_t<float>(a, av_parts, av_stride, ml_parts, ml_stride, nparts);
 }
 
 int mla_decode_launch(const MlaDecodeArgs& a) {

@@ -94,9 +94,11 @@ constexpr int64_t kMlaFillTcMinTokens = 64;
 bool mla_fill_tc_supported(const MlaAppendArgs& a);
 int mla_fill_tc_launch(const MlaAppendArgs& a);
 int mla_decode_launch(const MlaDecodeArgs& a);
-// merge per-range partials (av_parts [n][B][H][R], ml_parts [n][B][H][2]) into the
+// merge per-range partials (part r's av [B][H][R] at av_parts + r * av_stride,
+// its ml [B][H][2] at ml_parts + r * ml_stride) into the
 // workspace's av, then the W_uv step into a.out
-int mla_combine_partials_launch(const MlaDecodeArgs& a, const float* av_parts, const float* ml_parts, int nparts);
+int mla_combine_partials_launch(const MlaDecodeArgs& a, const float* av_parts, int64_t av_stride,
+                                const float* ml_parts, int64_t ml_stride, int nparts);
 
 // production-shape split kernel (R=256, D=128, DR=32, H=32, KV=8, 16-bit dtype)
 struct MlaMaps {

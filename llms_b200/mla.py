@@ -75,8 +75,9 @@ def decode_shard(B: int, L: int, world: int, rank: int) -> tuple[range, range]:
     GPUs: a context split -- every rank streams its slice
     ``[L*r/world, L*(r+1)/world)`` of every row's cache
     (``mla_decode_partial``), and the slices' partial softmaxes meet in one
-    small exchange (B x H x (R + 2) floats per rank) before the W_uv step
-    (``mla_combine_partials``): the flash-decoding split, across GPUs."""
+    small exchange (one all-gather of B x H x (R + 2) floats per rank) before
+    the W_uv step (``mla_combine_partials``): the flash-decoding split, across
+    GPUs."""
     if world < 1 or not 0 <= rank < world or B < 0 or L < 1:
         raise ValueError(f"bad shard request: B={B} L={L} world={world} rank={rank}")
     if B >= world or B == 0:
@@ -86,14 +87,21 @@ def decode_shard(B: int, L: int, world: int, rank: int) -> tuple[range, range]:
     return range(0, B), range(L * rank // world, L * (rank + 1) // world)
 
 
+def partial_numel(B: int, H: int, R: int) -> int:
+    """fp32 elements of one partial decode: av [B, H, R] then ml [B, H, 2]."""
+    return B * H * (R + 2)
+
+
 def mla_decode_partial(q: torch.Tensor, c_kv: torch.Tensor, kz: torch.Tensor | None, kscale: torch.Tensor,
                        w_uk: torch.Tensor | None, k_norm_w: torch.Tensor, inv_freq: torch.Tensor | None, *,
                        num_kv_heads: int, L: int, tokens: range, scale: float, eps: float,
-                       workspace: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+                       out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
     """The decode step over cache tokens ``tokens`` only, for a query at
-    position ``L - 1``: returns ``av`` fp32 (B, H, R) (the latent mixed by the
-    softmax over those tokens) and ``ml`` fp32 (B, H, 2) (their max score and
-    sum of exp).  No W_uv step: ``mla_combine_partials`` merges ranges."""
+    position ``L - 1``: returns one flat fp32 buffer of ``partial_numel``
+    elements -- ``av`` (B, H, R), the latent mixed by the softmax over those
+    tokens, then ``ml`` (B, H, 2), their max score and sum of exp -- so one
+    all-gather moves a rank's whole partial.  No W_uv step:
+    ``mla_combine_partials`` merges the ranges."""
     B, H, D = q.shape
     R = c_kv.shape[-1]
     DR = 0 if kz is None else kz.shape[-1]
@@ -105,39 +113,47 @@ def mla_decode_partial(q: torch.Tensor, c_kv: torch.Tensor, kz: torch.Tensor | N
     ws_bytes = int(_capi.lib.b200mm_mla_decode_workspace_size(ctypes.byref(shp), max(n, 1)))
     if workspace is None or workspace.numel() < ws_bytes:
         workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
-    av = torch.empty((B, H, R), dtype=torch.float32, device=q.device)
-    ml = torch.empty((B, H, 2), dtype=torch.float32, device=q.device)
+    numel = partial_numel(B, H, R)
+    if out is None:
+        out = torch.empty(numel, dtype=torch.float32, device=q.device)
+    if out.dtype != torch.float32 or out.numel() != numel or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous float32 buffer of {numel} elements")
     with _capi.on_device(q):
         st = _capi.lib.b200mm_mla_decode_partial(
             ctypes.byref(shp), q.data_ptr(), q.stride(0), c_kv.data_ptr(), c_kv.stride(0), c_kv.stride(1),
             _ptr(kz), 0 if kz is None else kz.stride(0), 0 if kz is None else kz.stride(1),
             kscale.data_ptr(), kscale.stride(0), kscale.stride(1), _ptr(w_uk), k_norm_w.data_ptr(), _ptr(inv_freq),
-            float(scale), L, tokens.start, tokens.stop, av.data_ptr(), ml.data_ptr(), workspace.data_ptr(),
-            workspace.numel(), _capi.stream_of(q))
+            float(scale), L, tokens.start, tokens.stop, out.data_ptr(), out.data_ptr() + 4 * B * H * R,
+            workspace.data_ptr(), workspace.numel(), _capi.stream_of(q))
     _capi.check(st, "b200mm_mla_decode_partial")
-    return av, ml
+    return out
 
 
-def mla_combine_partials(av_parts: torch.Tensor, ml_parts: torch.Tensor, w_uv: torch.Tensor, *, head_dim: int,
+def mla_combine_partials(parts: torch.Tensor, w_uv: torch.Tensor, *, batch: int, num_heads: int, head_dim: int,
                          d_rope: int, dtype: torch.dtype, eps: float, out: torch.Tensor | None = None,
                          workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """Merge the partial decodes of ``n`` token ranges (``av_parts`` (n, B, H,
-    R), ``ml_parts`` (n, B, H, 2), fp32, as gathered from the ranks) and apply
-    W_uv: the decode output (B, H, D) in ``dtype``."""
-    n, B, H, R = av_parts.shape
-    KV = w_uv.shape[0]
-    _capi.require_cuda(av_parts, ml_parts, w_uv)
+    """Merge the partial decodes of ``n`` token ranges -- ``parts`` (n,
+    partial_numel) fp32, one row per range as ``mla_decode_partial`` wrote
+    them (an all-gather of the ranks' buffers) -- and apply W_uv: the decode
+    output (batch, num_heads, head_dim) in ``dtype``."""
+    n = parts.shape[0]
+    KV, _, R = w_uv.shape
+    B, H = batch, num_heads
+    _capi.require_cuda(parts, w_uv)
+    if parts.dtype != torch.float32 or parts.dim() != 2 or parts.shape[1] != partial_numel(B, H, R) \
+            or parts.stride(1) != 1:
+        raise ValueError(f"parts must be float32 (n, {partial_numel(B, H, R)}) with unit inner stride")
     shp = _shape(B, H, KV, head_dim, d_rope, R, dtype, eps)
     ws_bytes = int(_capi.lib.b200mm_mla_decode_workspace_size(ctypes.byref(shp), 1))
     if workspace is None or workspace.numel() < ws_bytes:
-        workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=av_parts.device)
+        workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=parts.device)
     if out is None:
-        out = torch.empty((B, H, head_dim), dtype=dtype, device=av_parts.device)
-    av_parts, ml_parts = av_parts.contiguous(), ml_parts.contiguous()
-    with _capi.on_device(av_parts):
+        out = torch.empty((B, H, head_dim), dtype=dtype, device=parts.device)
+    with _capi.on_device(parts):
         st = _capi.lib.b200mm_mla_combine_partials(
-            ctypes.byref(shp), av_parts.data_ptr(), ml_parts.data_ptr(), n, w_uv.data_ptr(), out.data_ptr(),
-            out.stride(0), workspace.data_ptr(), workspace.numel(), _capi.stream_of(av_parts))
+            ctypes.byref(shp), parts.data_ptr(), parts.stride(0), parts.data_ptr() + 4 * B * H * R, parts.stride(0),
+            n, w_uv.data_ptr(), out.data_ptr(), out.stride(0), workspace.data_ptr(), workspace.numel(),
+            _capi.stream_of(parts))
     _capi.check(st, "b200mm_mla_combine_partials")
     return out
 

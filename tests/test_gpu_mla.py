@@ -276,15 +276,13 @@ def test_context_split_reassembles_full_decode(B, L, world):
     kw, inv = torch.ones(128, device="cuda"), mla.rope_inv_freq(128, 32, 1e6, "cuda")
     ks, kz = mla.mla_sidebands(c, kr, wuk, kw, inv, B=B, L=L, num_kv_heads=8, head_dim=128, eps=1e-6)
     full = mla.mla_decode(q, c, kz, ks, wuk, wuv, kw, inv, L=L, scale=128 ** -0.5, eps=1e-6)
-    avs, mls = [], []
+    parts = torch.empty(world, mla.partial_numel(B, 32, 256), device="cuda")  # what an all-gather fills
     for rank in range(world):
         rows, toks = mla.decode_shard(B, L, world, rank)
         assert len(rows) == B
-        av, ml = mla.mla_decode_partial(q, c, kz, ks, wuk, kw, inv, num_kv_heads=8, L=L, tokens=toks,
-                                        scale=128 ** -0.5, eps=1e-6)
-        avs.append(av)
-        mls.append(ml)
-    got = mla.mla_combine_partials(torch.stack(avs), torch.stack(mls), wuv, head_dim=128, d_rope=32,
+        mla.mla_decode_partial(q, c, kz, ks, wuk, kw, inv, num_kv_heads=8, L=L, tokens=toks, scale=128 ** -0.5,
+                               eps=1e-6, out=parts[rank])
+    got = mla.mla_combine_partials(parts, wuv, batch=B, num_heads=32, head_dim=128, d_rope=32,
                                    dtype=torch.bfloat16, eps=1e-6)
     bf16_check(host(got), host(full).astype(np.float64))
     if d is not None:
