@@ -889,6 +889,9 @@ def qwen3_8b_int8_decode(batches=(1, 16, 64), prompt=16):
             "argmax_agree_decided": bool(ours_ok[decided].all().item()),
             "decided_rows_pairwise": int(decided_pw.sum().item()),
             "argmax_agree_decided_pairwise": bool(ours_ok[decided_pw].all().item()),
+            "argmax_disagree_rows_decided_pairwise": int((~ours_ok[decided_pw]).sum().item()),
+            "argmax_disagree_rows_all": int((~ours_ok).sum().item()),
+            "reference_bf16_argmax_disagree_rows_all": int((~base_ok).sum().item()),
             "argmax_agree_all": float(ours_ok.float().mean().item()),
             "logits_rel_l2": rel(logits),
             "reference_bf16_argmax_agree_decided": bool(base_ok[decided].all().item()),
