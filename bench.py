@@ -456,7 +456,8 @@ def suite(job):
                 b = op_bytes(2 * n_rows if gate else n_rows, HIDDEN, M, n_rows)
                 out[f"{name}_m{M}"] = {"us_per_launch": per * 1e6, "GB/s": b / per / 1e9}
             del g, x, y
-    # int8 weight-only at the Qwen3-8B shape (K = 4096): GB/s of int8 weights + activations
+    # int8 weight-only at the Qwen3-8B shape (K = 4096): GB/s of int8 weights +
+    # activations; 8 weight sets rotate (1 GB), so no launch finds its weights in L2
     gq = torch.Generator(device="cuda").manual_seed(4)
     K8, NQKV8, N8 = 4096, NQ + 2 * NK, 12288
     w8 = [(torch.randint(-127, 128, (NQKV8, K8), device="cuda", dtype=torch.int8, generator=gq),
@@ -464,8 +465,8 @@ def suite(job):
            torch.randint(-127, 128, (N8, K8), device="cuda", dtype=torch.int8, generator=gq),
            torch.rand(N8, device="cuda", generator=gq) * 9e-4 + 1e-4,
            torch.randint(-127, 128, (N8, K8), device="cuda", dtype=torch.int8, generator=gq),
-           torch.rand(N8, device="cuda", generator=gq) * 9e-4 + 1e-4) for _ in range(2)]
-    for M in (1, 16, 64):
+           torch.rand(N8, device="cuda", generator=gq) * 9e-4 + 1e-4) for _ in range(8)]
+    for M in (1, 4, 16, 64):
         for name, gate in (("qkv_w8", False), ("gate_up_w8", True)):
             x = torch.randn(M, K8, device="cuda", dtype=torch.bfloat16)
             n_rows = N8 if gate else NQKV8

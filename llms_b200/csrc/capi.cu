@@ -63,15 +63,17 @@ int dense_dispatch(const DenseArgs& a) {
     if (fam == "tc" && tc_supported(a)) return tc_launch(a);
   }
 #endif
-  // measured on B200 at the Qwen3 shapes: M <= 4 CUDA-core GEMV; small M the
-  // mma.sync GEMV (gate-up M <= 16, plain projections M <= 8, int8 M <= 32);
+  // measured on B200 at the Qwen3 shapes: M <= 4 CUDA-core GEMV (int8: M = 1;
+  // at M = 2..4 the mma.sync GEMV took 10 us for the 8B int8 QKV where the
+  // CUDA-core GEMV took 16); small M the mma.sync GEMV (gate-up M <= 16,
+  // plain projections M <= 8, int8 M <= 32);
   // then tcgen05 with the weights as the MMA's M side (16-bit up to M = 64,
   // and up to 128 for narrow plain projections (FFN down, K >= 2N, and
   // outputs up to 3072 wide such as the 2560-wide o), whose few output tiles
   // leave the GEMM tiled over X short of CTAs; int8 any M); otherwise the
   // tcgen05 GEMM tiled over X
   const bool narrow_deep = !a.gate && (a.K >= 2 * a.N || a.N <= 3072);
-  if (a.M <= 4 && gemv_supported(a)) return gemv_launch(a);
+  if (a.M <= (a.w8 ? 1 : 4) && gemv_supported(a)) return gemv_launch(a);
   if (a.M <= (a.w8 ? 32 : a.gate ? 16 : 8) && mmv_supported(a)) return mmv_launch(a);
   if ((a.w8 || a.M <= 64 || (narrow_deep && a.M <= 128)) && swap_supported(a)) return swap_launch(a);
   if (tc_supported(a)) return tc_launch(a);

@@ -242,7 +242,7 @@ def test_mid_m_tensor_core_gemv(M, gate):
     bf16_check(host(y), e)
 
 
-@pytest.mark.parametrize("M", [2, 5, 16, 33, 64])
+@pytest.mark.parametrize("M", [2, 3, 5, 16, 33, 64])
 def test_mid_m_int8_and_fp16(M):
     from llms_b200.kernels import int8_fused_gate_up_silu, int8_fused_qkv, triton_fused_qkv
     lay = I.cfg5_layer(M=M, seed=M)
