@@ -13,6 +13,9 @@
 //   * launched with programmatic dependent launch: a warp issues the loads of
 //     its first unit's weights before `griddepcontrol.wait`, so weight
 //     streaming overlaps the tail of the kernel that produced x.
+//   * shapes with fewer units than resident warps (column shards, narrow
+//     projections) split each unit's K range over 2-8 warps of a CTA, which
+//     sum their partials through shared memory.
 // Grid: (SM count) x (resident CTAs per SM), grid-stride over units.
 #include "dense.cuh"
 
@@ -42,44 +45,65 @@ constexpr int gemv_min_blocks() {
 
 template <typename TX, typename TW, int MR, bool GATE, int NCH>
 __global__ void __launch_bounds__(kThreads, gemv_min_blocks<MR, GATE>())
-gemv_kernel(const GemvParams p, const int nsm) {
+gemv_kernel(const GemvParams p, const int nsm, const int ks) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   TX* xs = reinterpret_cast<TX*>(smem_raw);  // [MR][K] activation rows
+  __shared__ float red[kThreads / 32][2][MR];  // K-slice partial sums (ks > 1)
 
   constexpr int WV = Chunk<TW>::kElems;      // weights per 16-byte chunk
   constexpr int XV = Chunk<TX>::kElems;      // activations per 16-byte chunk
   static_assert(WV % XV == 0, "weight chunk must cover whole activation chunks");
   constexpr int XPW = WV / XV;               // activation chunks per weight chunk
 
-  const int lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int warps_per_cta = blockDim.x >> 5;
-  // Unit order.  Block order (gate-up): warp w of CTA b takes units
-  // b * warps + w + k * nwarps.  SM-round-robin order (plain projections, nsm
-  // > 0, the grid a multiple of the SM count so CTA b runs on SM b % nsm):
-  // consecutive units go to consecutive SMs, so the last, partial wave of
-  // units is spread over every SM instead of the first CTAs' SMs.  Measured
-  // (Qwen3-4B QKV, M = 1, 36 launches in a graph): 7.8 -> 6.9 us; for
-  // gate-up it was slower (17.4 -> 17.9 us) and stays in block order.
-  int gwarp = blockIdx.x * warps_per_cta + (threadIdx.x >> 5);
-  if (nsm > 0 && gridDim.x % nsm == 0)
-    gwarp = ((int)(blockIdx.x / nsm) * warps_per_cta + (threadIdx.x >> 5)) * nsm + blockIdx.x % nsm;
-  const int nwarps = gridDim.x * warps_per_cta;
   const int N = p.N, K = p.K, M = p.M;
   const int nunits = GATE ? N : (N + 1) >> 1;
   const int nchunks = K / WV;
   constexpr int kSeg = 32 * NCH;
-  const int nseg = (nchunks + kSeg - 1) / kSeg;
+
+  // Work items.  ks == 1: a warp owns whole units, grid-stride.  Unit order:
+  // block order (gate-up): warp w of CTA b takes units b * warps + w + k *
+  // nwarps.  SM-round-robin order (plain projections, nsm > 0, the grid a
+  // multiple of the SM count so CTA b runs on SM b % nsm): consecutive units
+  // go to consecutive SMs, so the last, partial wave of units is spread over
+  // every SM instead of the first CTAs' SMs.  Measured (Qwen3-4B QKV, M = 1,
+  // 36 launches in a graph): 7.8 -> 6.9 us; for gate-up it was slower (17.4
+  // -> 17.9 us) and stays in block order.
+  // ks > 1 (too few units to give every warp one: column shards, narrow
+  // projections): the ks warps of a group split one unit's K range and sum
+  // their partials through shared memory; a CTA takes warps / ks units at a
+  // time, grid-stride, every warp of the CTA in step (the sums need
+  // __syncthreads).
+  const int upc = warps_per_cta / ks;  // units per CTA tile
+  const int slice = warp % ks;
+  const int cps = (nchunks + ks - 1) / ks;  // chunks per K slice
+  const int cbeg = slice * cps;
+  const int cend = cbeg + cps < nchunks ? cbeg + cps : nchunks;
+  const int nseg = (cend - cbeg + kSeg - 1) / kSeg;
+  int u, ustep;
+  if (ks == 1) {
+    u = blockIdx.x * warps_per_cta + warp;
+    if (nsm > 0 && gridDim.x % nsm == 0)
+      u = ((int)(blockIdx.x / nsm) * warps_per_cta + warp) * nsm + blockIdx.x % nsm;
+    ustep = gridDim.x * warps_per_cta;
+  } else {
+    u = blockIdx.x * upc + warp / ks;
+    ustep = gridDim.x * upc;
+  }
+  // ks > 1: every warp runs the tile loop while its CTA has a tile
+  const int ntile_units = ks == 1 ? nunits : ((nunits + upc - 1) / upc) * upc;
 
   const TW* w0 = static_cast<const TW*>(p.w0);
   const TW* w1 = static_cast<const TW*>(p.w1);
 
-  auto row_ptrs = [&](int u, const TW*& r0, const TW*& r1, bool& v1) {
+  auto row_ptrs = [&](int uu, const TW*& r0, const TW*& r1, bool& v1) {
     if (GATE) {
-      r0 = w0 + (int64_t)u * p.ldw0;
-      r1 = w1 + (int64_t)u * p.ldw1;
+      r0 = w0 + (int64_t)uu * p.ldw0;
+      r1 = w1 + (int64_t)uu * p.ldw1;
       v1 = true;
     } else {
-      const int n0 = 2 * u;
+      const int n0 = 2 * uu;
       r0 = w0 + (int64_t)n0 * p.ldw0;
       v1 = (n0 + 1) < N;
       r1 = w0 + (int64_t)(v1 ? n0 + 1 : n0) * p.ldw0;
@@ -87,13 +111,13 @@ gemv_kernel(const GemvParams p, const int nsm) {
   };
 
   uint4 wv[2][NCH];
-  auto load_seg = [&](int u, int seg) {
+  auto load_seg = [&](int uu, int seg) {
     const TW* r0; const TW* r1; bool v1;
-    row_ptrs(u, r0, r1, v1);
+    row_ptrs(uu, r0, r1, v1);
 #pragma unroll
     for (int i = 0; i < NCH; ++i) {
-      const int c = seg * kSeg + i * 32 + lane;
-      if (c < nchunks) {
+      const int c = cbeg + seg * kSeg + i * 32 + lane;
+      if (c < cend) {
         wv[0][i] = ld_stream16(r0 + (int64_t)c * WV);
         wv[1][i] = v1 ? ld_stream16(r1 + (int64_t)c * WV) : make_uint4(0, 0, 0, 0);
       } else {
@@ -108,20 +132,19 @@ gemv_kernel(const GemvParams p, const int nsm) {
   // of them; int8 units are half the bytes, so a warp walks twice as many).
   // Measured: int8 QKV 11.5 -> 10.3 us, gate-up 26.7 -> 25.1 us at M = 1;
   // for 16-bit weights it slowed both (gate-up 17.3 -> 18.9 us), so it is off.
-  const int64_t row_bytes = (int64_t)K * sizeof(TW);
   auto prefetch_unit = [&](int un) {
     const TW* r0; const TW* r1; bool v1;
     row_ptrs(un, r0, r1, v1);
-    const char* p0 = reinterpret_cast<const char*>(r0);
-    const char* p1 = reinterpret_cast<const char*>(r1);
-    for (int64_t off = (int64_t)lane * 128; off < row_bytes; off += 32 * 128) {
+    const char* p0 = reinterpret_cast<const char*>(r0 + (int64_t)cbeg * WV);
+    const char* p1 = reinterpret_cast<const char*>(r1 + (int64_t)cbeg * WV);
+    const int64_t bytes = (int64_t)(cend - cbeg) * 16;
+    for (int64_t off = (int64_t)lane * 128; off < bytes; off += 32 * 128) {
       prefetch_l2(p0 + off);
       if (v1) prefetch_l2(p1 + off);
     }
   };
 
   // Weights are never written by another kernel: start streaming them now.
-  int u = gwarp;
   if (u < nunits) load_seg(u, 0);
   pdl_trigger();
   pdl_wait();
@@ -140,21 +163,22 @@ gemv_kernel(const GemvParams p, const int nsm) {
   __syncthreads();
 
   bool preloaded = true;
-  for (; u < nunits; u += nwarps) {
-    if (sizeof(TW) == 1 && u + nwarps < nunits) prefetch_unit(u + nwarps);
+  for (; u < ntile_units; u += ustep) {
+    const bool live = u < nunits;
+    if (sizeof(TW) == 1 && live && u + ustep < nunits) prefetch_unit(u + ustep);
     float acc[2][MR];
 #pragma unroll
     for (int r = 0; r < 2; ++r)
 #pragma unroll
       for (int m = 0; m < MR; ++m) acc[r][m] = 0.f;
 
-    for (int seg = 0; seg < nseg; ++seg) {
+    for (int seg = 0; live && seg < nseg; ++seg) {
       if (!preloaded) load_seg(u, seg);
       preloaded = false;
 #pragma unroll
       for (int i = 0; i < NCH; ++i) {
-        const int c = seg * kSeg + i * 32 + lane;
-        if (c < nchunks) {
+        const int c = cbeg + seg * kSeg + i * 32 + lane;
+        if (c < cend) {
           float f0[WV], f1[WV];
           Chunk<TW>::unpack(wv[0][i], f0);
           Chunk<TW>::unpack(wv[1][i], f1);
@@ -175,14 +199,37 @@ gemv_kernel(const GemvParams p, const int nsm) {
         }
       }
     }
+    preloaded = false;
 
 #pragma unroll
     for (int r = 0; r < 2; ++r)
 #pragma unroll
       for (int m = 0; m < MR; ++m) acc[r][m] = warp_sum(acc[r][m]);
 
+    if (ks > 1) {
+      // the group's slices meet in shared memory; slice 0 stores
+      if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+          for (int m = 0; m < MR; ++m) red[warp][r][m] = acc[r][m];
+      }
+      __syncthreads();
+      if (slice == 0) {
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+          for (int m = 0; m < MR; ++m) {
+            float t = 0.f;
+            for (int s = 0; s < ks; ++s) t += red[warp + s][r][m];
+            acc[r][m] = t;
+          }
+      }
+      __syncthreads();
+    }
+
     // lanes 0..MR-1 store row m = lane (values are uniform across the warp)
-    if (lane < MR && lane < M) {
+    if (live && slice == 0 && lane < MR && lane < M) {
       float a0 = 0.f, a1 = 0.f;
 #pragma unroll
       for (int m = 0; m < MR; ++m)
@@ -227,13 +274,24 @@ int launch_one(const DenseArgs& a) {
   }
   const int nunits = a.gate ? a.N : (a.N + 1) / 2;
   const int warps_per_cta = kThreads / 32;
+  const int slots = num_sms(dev) * bps * warps_per_cta;  // resident warps
+  // K slices per unit: the most (1, 2, 4, 8) that keep every (unit, slice)
+  // in one wave of resident warps, each slice keeping at least one 16-byte
+  // chunk per lane.  Measured at M = 1 (graphs of launches, weights past L2):
+  // a QKV column shard of 768 rows 3.05 -> 2.71 us, 1536 rows 3.31 -> 3.16,
+  // a 320-row o shard 4.51 -> 2.51; slicing shapes that already fill one wave
+  // (the whole QKV, gate-up) made them 25-40 % slower, so they keep ks = 1.
+  constexpr int WV = 16 / (int)sizeof(TW);
+  int ks = 1;
+  while (ks < 8 && (int64_t)nunits * 2 * ks <= slots && a.K / WV / (2 * ks) >= 32) ks *= 2;
+  const int upc = warps_per_cta / ks;
   int grid = num_sms(dev) * bps;
-  const int need = (nunits + warps_per_cta - 1) / warps_per_cta;
+  const int need = (nunits + upc - 1) / upc;
   if (grid > need) grid = need;
   if (grid < 1) grid = 1;
   GemvParams p{a.x, a.ldx, a.w0, a.ldw0, a.w1, a.ldw1, a.s0, a.s1, a.y, a.ldy, a.M, a.N, a.K};
   // plain projections: warps take units in SM-round-robin order (below)
-  cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, a.stream, p, GATE ? 0 : num_sms(dev));
+  cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, a.stream, p, GATE ? 0 : num_sms(dev), ks);
   return e == cudaSuccess ? B200MM_OK : B200MM_ERR_LAUNCH;
 }
 
