@@ -630,58 +630,74 @@ def suite(job):
 def qwen3_8b_int8_decode_sharded(rank, world, batches=(1, 16, 64), prompt=16, steps=20):
     """BASELINE config 5 across GPUs (llms_b200.shard): every projection of
     each layer column-sharded (QKV head-aligned, gate-up by intermediate
-    columns, o / down by hidden columns) and followed by one NCCL all-gather;
-    attention, norms, embedding and LM head replicated.  Each rank builds the
-    same seeded model; before sharding it runs one unsharded decode step,
-    after sharding the same step, and the largest logit difference over
-    ranks is reported.  Timing: one decode step per CUDA graph (the
-    all-gathers captured inside), max over ranks; tok/s = batch / step."""
-    from llms_b200.kernels import apply_linear_kernels
+    columns, o / down by hidden columns) and followed by one all-gather;
+    attention, norms and embedding replicated.  The gathers run two
+    ways: b200mm_peer_gather over NVLink (llms_b200.peer, one launch per
+    gather, the headline tok/s) and NCCL all-gather + permute (for
+    comparison).  The LM head is sharded by vocabulary rows the same way;
+    attention runs on b200mm_gqa_decode as in the one-GPU step.  Each rank
+    builds the same seeded model; before sharding it
+    runs one unsharded decode step, after sharding the same step, and the
+    largest logit difference over ranks is reported.  Timing: one decode step
+    per CUDA graph (the gathers captured inside), max over ranks; tok/s =
+    batch / step."""
+    from llms_b200.kernels import apply_decode_attn, apply_linear_kernels
+    from llms_b200.peer import PeerGather
     from llms_b200.qwen3 import greedy, synthetic_int8_model
-    from llms_b200.shard import shard_decode_model
+    from llms_b200.shard import peer_bytes, shard_decode_model
 
-    model = synthetic_int8_model(seed=4)
-    apply_linear_kernels(model)
-    inputs = {}
-    for B in batches:
-        g = torch.Generator(device="cuda").manual_seed(100 + B)
-        inputs[B] = (torch.randint(0, model.shape.vocab_size, (B, prompt), generator=g, device="cuda"),
-                     torch.randint(0, model.shape.vocab_size, (B, 1), generator=g, device="cuda"))
-    with torch.inference_mode():
-        ids, nxt = inputs[batches[0]]
-        cache = model.alloc_cache(prompt + 8, max_batch=ids.shape[0])
-        model(ids, cache, start_pos=0)
-        ref = model(nxt, cache, start_pos=prompt)[:, -1].float()
-        del cache
-    shard_decode_model(model, rank, world)
-    torch.cuda.empty_cache()
     res = {}
-    with torch.inference_mode():
+    for mode in ("peer", "nccl"):
+        model = synthetic_int8_model(seed=4)
+        apply_linear_kernels(model, lm_head=True)
+        apply_decode_attn(model)
+        inputs = {}
         for B in batches:
-            ids, nxt = inputs[B]
-            cache = model.alloc_cache(prompt + 8, max_batch=B)
-            model(ids, cache, start_pos=0)
-            logits = model(nxt, cache, start_pos=prompt)[:, -1].float()
-            entry = {}
-            if B == batches[0]:
-                diff = (logits - ref).abs().max().item()
-                entry["max_abs_logit_diff_vs_unsharded"] = max_over_ranks(diff, world)
-                entry["argmax_agree_vs_unsharded"] = bool((greedy(logits) == greedy(ref)).all().item())
-            s = torch.cuda.Stream()
-            s.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(s):
-                model(nxt, cache, start_pos=prompt)
-            torch.cuda.current_stream().wait_stream(s)
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                model(nxt, cache, start_pos=prompt)
-            sec = time_graph(graph, steps, 3, world)
-            del graph, cache
-            res[f"qwen3_8b_int8_decode_b{B}_sharded"] = {
-                "ms_per_step": sec / steps * 1e3, "tok/s": B * steps / sec,
-                "split": f"column shards over {world} GPUs, NCCL all-gather after each projection", **entry}
-    del model
-    torch.cuda.empty_cache()
+            g = torch.Generator(device="cuda").manual_seed(100 + B)
+            inputs[B] = (torch.randint(0, model.shape.vocab_size, (B, prompt), generator=g, device="cuda"),
+                         torch.randint(0, model.shape.vocab_size, (B, 1), generator=g, device="cuda"))
+        if mode == "peer":
+            with torch.inference_mode():
+                ids, nxt = inputs[batches[0]]
+                cache = model.alloc_cache(prompt + 8, max_batch=ids.shape[0])
+                model(ids, cache, start_pos=0)
+                ref = model(nxt, cache, start_pos=prompt)[:, -1].float()
+                del cache
+            peer = PeerGather(peer_bytes(model, max(batches)))
+        else:
+            peer = None
+        shard_decode_model(model, rank, world, peer=peer, max_rows=max(batches))
+        torch.cuda.empty_cache()
+        with torch.inference_mode():
+            for B in batches:
+                ids, nxt = inputs[B]
+                cache = model.alloc_cache(prompt + 8, max_batch=B)
+                model(ids, cache, start_pos=0)
+                logits = model(nxt, cache, start_pos=prompt)[:, -1].float()
+                entry = res.setdefault(f"qwen3_8b_int8_decode_b{B}_sharded", {})
+                if B == batches[0] and mode == "peer":
+                    diff = (logits - ref).abs().max().item()
+                    entry["max_abs_logit_diff_vs_unsharded"] = max_over_ranks(diff, world)
+                    entry["argmax_agree_vs_unsharded"] = bool((greedy(logits) == greedy(ref)).all().item())
+                s = torch.cuda.Stream()
+                s.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(s):
+                    model(nxt, cache, start_pos=prompt)
+                torch.cuda.current_stream().wait_stream(s)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    model(nxt, cache, start_pos=prompt)
+                sec = time_graph(graph, steps, 3, world)
+                del graph, cache
+                if mode == "peer":
+                    entry.update({"ms_per_step": sec / steps * 1e3, "tok/s": B * steps / sec,
+                                  "split": f"column shards over {world} GPUs; b200mm_peer_gather over NVLink "
+                                           "after each projection (4 per layer + the LM head)",
+                                  "peer_status": peer.status()})
+                else:
+                    entry["tok/s_nccl_all_gather"] = B * steps / sec
+        del model, peer
+        torch.cuda.empty_cache()
     return res
 
 
@@ -1011,6 +1027,23 @@ def main():
         sec = time_graph(graph, args.steps, max(3, args.warmup), world, post)
     clocks = clk.summary()
     per_step = sec / args.steps
+    limiter = None
+    if world > 1:
+        # the step's two parts timed apart (device time, max over ranks): this
+        # rank's kernels (the graph alone) and the output all-gather alone
+        k_sec = time_graph(graph, args.steps, 3, world)
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            gather(job, world)
+        e1.record()
+        torch.cuda.synchronize()
+        g_sec = max_over_ranks(e0.elapsed_time(e1) / 1e3, world)
+        limiter = {"kernels_ms_per_step": k_sec / args.steps * 1e3, "all_gather_ms_per_step": g_sec / args.steps * 1e3,
+                   "kernel_GB/s_per_rank": job.bytes_step / (k_sec / args.steps) / 1e9,
+                   "gather_bytes_per_rank": job.out_numel * 2 * world}
     total_bytes = job.bytes_step * world
     value = total_bytes / per_step / 1e9
     parity = parity_layer0(job, rank, world)
@@ -1148,6 +1181,8 @@ def main():
                               "steps": eager_steps,
                               "path": "the same API calls issued from Python each step (72 calls + copies)"}},
         }
+        if limiter:
+            line["step_split"] = limiter
         if "suite" in extra:
             line["submetrics"] = submetrics(extra["suite"])
         line.update(extra)

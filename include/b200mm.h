@@ -348,6 +348,35 @@ int b200mm_qk_norm_rope(const void* qkv, int64_t ldq,
                         float eps, int dtype, void* stream);
 
 /*
+ * b200mm_peer_gather -- stands in for the NCCL all-gather after each
+ * column-sharded projection of the multi-GPU decode step (the reference
+ * engine runs on one GPU; the gather is the only collective its sharded form
+ * needs).  One launch: this rank's block src [rows, sum(part_widths)] is
+ * stored into every rank's gathered buffer dst[r] [rows, ld_dst] over peer
+ * memory, part j of rank q at column world * (w_0 + .. + w_{j-1}) + q * w_j,
+ * so a fused QKV block [q | k | v] gathers to [all q | all k | all v].
+ *   - dst[0..world) and flags[0..world) are device addresses valid on this
+ *     GPU (peer mappings of every rank's buffers, own rank included);
+ *     flags[r] is rank r's uint32 array [world][nctas], zeroed once before
+ *     the first gather; seen is this rank's uint32 [nctas] (zeroed once),
+ *     err a local int status word (zeroed once; set to 1 when a wait for a
+ *     peer ran out, after 5 s, and then stays set).
+ *   - Every rank must issue the same sequence of gathers with the same
+ *     nctas; calls on one stream per rank.  Each CTA waits, bounded, for the
+ *     peers' CTA of the same index, so when the kernel ends every rank's
+ *     block has arrived.  A peer may write the next gather into dst before
+ *     this rank has read the previous one unless each call site has its own
+ *     dst region (or the reads finish before this rank's next gather).
+ *   - dtype 0 / 1 / 2 (fp32 / fp16 / bf16); copies are 16 bytes wide when
+ *     every address, width and stride allows.  world <= 8, nparts <= 3.
+ */
+int b200mm_peer_gather(const void* src, int64_t ld_src, int64_t rows,
+                       const int64_t* part_widths, int nparts,
+                       void* const* dst, int64_t ld_dst, int dtype,
+                       int rank, int world, void* const* flags,
+                       void* seen, void* err, int nctas, void* stream);
+
+/*
  * b200mm_mla_decode_noalloc -- no counterpart in the reference.
  *
  * b200mm_mla_decode for callers that cannot allocate device memory at decode

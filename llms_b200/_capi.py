@@ -108,6 +108,11 @@ SIGNATURES: dict[str, tuple] = {
          _c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, ctypes.c_float,
          ctypes.c_int, _c_p],
     ),
+    "b200mm_peer_gather": (
+        ctypes.c_int,
+        [_c_p, _c_i64, _c_i64, ctypes.POINTER(ctypes.c_int64), ctypes.c_int, ctypes.POINTER(_c_p), _c_i64,
+         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_c_p), _c_p, _c_p, ctypes.c_int, _c_p],
+    ),
     "b200mm_mla_decode_noalloc": (
         ctypes.c_int,
         [ctypes.POINTER(MlaShape), _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64,

@@ -389,4 +389,16 @@ int b200mm_mla_combine_partials(const b200mm_mla_shape* shape, const float* av_p
   return launch_status();
 }
 
+int b200mm_peer_gather(const void* src, int64_t ld_src, int64_t rows, const int64_t* part_widths, int nparts,
+                       void* const* dst, int64_t ld_dst, int dtype, int rank, int world, void* const* flags,
+                       void* seen, void* err, int nctas, void* stream) {
+  const int eb = dtype == B200MM_F32 ? 4 : (dtype == B200MM_F16 || dtype == B200MM_BF16) ? 2 : 0;
+  if (!eb) return B200MM_ERR_DTYPE;
+  int st = check_device();
+  if (st != B200MM_OK) return st;
+  return peer_gather_launch(src, ld_src, rows, part_widths, nparts, dst, ld_dst, eb, rank, world,
+                            reinterpret_cast<unsigned* const*>(flags), static_cast<unsigned*>(seen),
+                            static_cast<int*>(err), nctas, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -25,6 +25,11 @@ inline void count_launch(uint64_t n = 1) { g_launches.fetch_add(n, std::memory_o
 int num_sms(int device);          // cached multiprocessor count of `device`
 int current_device();             // cudaGetDevice with caching of nothing
 
+// peer.cu: column-block all-gather over peer memory (b200mm_peer_gather)
+int peer_gather_launch(const void* src, int64_t ld_src, int64_t rows, const int64_t* widths, int nparts,
+                       void* const* dst, int64_t ld_dst, int elem_bytes, int rank, int world, unsigned* const* flags,
+                       unsigned* seen, int* err, int nctas, cudaStream_t stream);
+
 inline int launch_status() {
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? B200MM_OK : B200MM_ERR_LAUNCH;

@@ -18,6 +18,11 @@ logits.  Row-parallel projections with an all-reduce are not used (the path
 allows gathers only).  Every projection is one of this package's kernels on
 the local shard: ``int8_linear`` / ``int8_fused_gate_up_silu`` for the int8
 projections and ``b200_linear`` for ``o`` / ``down``.
+
+With a ``peer.PeerGather`` context (``shard_decode_model(..., peer=ctx)``)
+each of the four gathers per layer is one ``b200mm_peer_gather`` launch over
+NVLink into a region of its own instead of an NCCL all-gather plus a permute;
+batches above the context's row budget fall back to NCCL.
 """
 
 from __future__ import annotations
@@ -49,11 +54,13 @@ def qkv_rows(n_q: int, n_k: int, rank: int, world: int) -> list[int]:
     return list(q) + [n_q + i for i in k] + [n_q + n_k + i for i in k]
 
 
-def gather_cols(y: torch.Tensor, world: int, group=None) -> torch.Tensor:
+def gather_cols(y: torch.Tensor, world: int, group=None, site=None) -> torch.Tensor:
     """All-gather each rank's column block of ``y`` (..., c) into (..., world c),
-    blocks in rank order."""
+    blocks in rank order (over peer memory when ``site`` fits ``y``)."""
     if world == 1:
         return y
+    if site is not None and site.fits(y):
+        return site.gather(y)
     lead, c = y.shape[:-1], y.shape[-1]
     y2 = y.reshape(-1, c).contiguous()
     out = torch.empty((world * y2.shape[0], c), dtype=y.dtype, device=y.device)
@@ -61,12 +68,16 @@ def gather_cols(y: torch.Tensor, world: int, group=None) -> torch.Tensor:
     return out.view(world, y2.shape[0], c).permute(1, 0, 2).reshape(*lead, world * c)
 
 
-def gather_qkv(y: torch.Tensor, cq: int, ck: int, world: int, group=None):
+def gather_qkv(y: torch.Tensor, cq: int, ck: int, world: int, group=None, site=None):
     """All-gather per-rank [q_r | k_r | v_r] blocks (widths cq, ck, ck) into the
-    full q (world cq), k and v (world ck), each in head order."""
+    full q (world cq), k and v (world ck), each in head order (over peer
+    memory when ``site`` fits ``y``: views of one [..., world (cq + 2 ck)]
+    buffer)."""
     lead = y.shape[:-1]
     if world == 1:
         return y.split([cq, ck, ck], dim=-1)
+    if site is not None and site.fits(y):
+        return site.gather(y, (cq, ck, ck)).split([world * cq, world * ck, world * ck], dim=-1)
     y2 = y.reshape(-1, cq + 2 * ck).contiguous()
     out = torch.empty((world * y2.shape[0], cq + 2 * ck), dtype=y.dtype, device=y.device)
     dist.all_gather_into_tensor(out, y2, group=group)
@@ -81,10 +92,10 @@ class ShardedLinear(nn.Module):
     def __init__(self, weight: torch.Tensor, world: int, group=None) -> None:
         super().__init__()
         self.weight = nn.Parameter(weight, requires_grad=False)
-        self.world, self.group = world, group
+        self.world, self.group, self.site = world, group, None
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return gather_cols(b200_linear(x, self.weight), self.world, self.group)
+        return gather_cols(b200_linear(x, self.weight), self.world, self.group, self.site)
 
 
 class ShardedInt8Attention(Int8Attention):
@@ -106,12 +117,12 @@ class ShardedInt8Attention(Int8Attention):
         out.o = ShardedLinear(att.o.weight.detach()[hid.start:hid.stop].contiguous(), world, group)
         out.q_norm, out.k_norm = att.q_norm, att.k_norm
         out.decode_attn_op = getattr(att, "decode_attn_op", None)
-        out.world, out.group = world, group
+        out.world, out.group, out.site = world, group, None
         return out
 
     def project_qkv(self, x: torch.Tensor):
         y = int8_linear(x, self.q_qkv, self.s_qkv)
-        return gather_qkv(y, self.n_q // self.world, self.n_k // self.world, self.world, self.group)
+        return gather_qkv(y, self.n_q // self.world, self.n_k // self.world, self.world, self.group, self.site)
 
 
 class ShardedInt8FFN(Int8FFN):
@@ -129,23 +140,56 @@ class ShardedInt8FFN(Int8FFN):
         w = ffn.down.weight.detach()
         hid = even_range(w.shape[0], rank, world)
         out.down = ShardedLinear(w[hid.start:hid.stop].contiguous(), world, group)
-        out.world, out.group = world, group
+        out.world, out.group, out.site = world, group, None
         return out
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         h = int8_fused_gate_up_silu(x, self.qg, self.sg, self.qu, self.su)
-        return self.down(gather_cols(h, self.world, self.group))
+        return self.down(gather_cols(h, self.world, self.group, self.site))
 
 
-def shard_decode_model(model: nn.Module, rank: int, world: int, group=None) -> nn.Module:
-    """Replace every layer's int8 attention / FFN with its column-sharded
-    form (in place; the full projection weights are dropped).  Returns
-    ``model``."""
+def peer_bytes(model: nn.Module, max_rows: int) -> int:
+    """Bytes of gathered output one decode step of ``model`` needs at up to
+    ``max_rows`` tokens (four call sites per layer, 256-byte aligned)."""
+    total = 0
     for block in model.layers:
-        block.attn = ShardedInt8Attention.from_module(block.attn, rank, world, group)
-        block.ffn = ShardedInt8FFN.from_module(block.ffn, rank, world, group)
+        att, ffn = block.attn, block.ffn
+        inter = ffn.qg.shape[0] if hasattr(ffn, "qg") else ffn.gate.weight.shape[0]
+        esz = 2
+        for width in (att.n_q + 2 * att.n_k, att.hidden_size, inter, att.hidden_size):
+            total += (max_rows * width * esz + 255) // 256 * 256
+    vocab = model.lm_head.weight.shape[0]
+    return total + (max_rows * vocab * 2 + 255) // 256 * 256
+
+
+def shard_decode_model(model: nn.Module, rank: int, world: int, group=None, peer=None,
+                       max_rows: int = 64, lm_head: bool = True) -> nn.Module:
+    """Replace every layer's int8 attention / FFN with its column-sharded
+    form (in place; the full projection weights are dropped), and with
+    ``lm_head`` the LM head by vocabulary rows (the logits gathered).  With
+    ``peer`` (a ``peer.PeerGather`` of at least ``peer_bytes(model,
+    max_rows)``), the gathers of up to ``max_rows`` tokens run over peer
+    memory, one call-site region each.  Returns ``model``."""
+    dtype = model.layers[0].attn.o.weight.dtype
+    for block in model.layers:
+        att = ShardedInt8Attention.from_module(block.attn, rank, world, group)
+        ffn = ShardedInt8FFN.from_module(block.ffn, rank, world, group)
+        if peer is not None:
+            inter = ffn.qg.shape[0] * world
+            att.site = peer.site(max_rows, att.n_q + 2 * att.n_k, dtype)
+            att.o.site = peer.site(max_rows, att.hidden_size, dtype)
+            ffn.site = peer.site(max_rows, inter, dtype)
+            ffn.down.site = peer.site(max_rows, att.hidden_size, dtype)
+        block.attn, block.ffn = att, ffn
+    if lm_head:
+        w = model.lm_head.weight.detach()
+        rows = even_range(w.shape[0], rank, world)
+        head = ShardedLinear(w[rows.start:rows.stop].contiguous(), world, group)
+        if peer is not None:
+            head.site = peer.site(max_rows, w.shape[0], w.dtype)
+        model.lm_head = head
     return model
 
 
 __all__ = ["ShardedInt8Attention", "ShardedInt8FFN", "ShardedLinear", "even_range", "gather_cols",
-           "gather_qkv", "qkv_rows", "shard_decode_model"]
+           "gather_qkv", "peer_bytes", "qkv_rows", "shard_decode_model"]
