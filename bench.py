@@ -647,7 +647,7 @@ def qwen3_8b_int8_decode_sharded(rank, world, batches=(1, 16, 64), prompt=16, st
     from llms_b200.shard import peer_bytes, shard_decode_model
 
     res = {}
-    for mode in ("peer", "nccl"):
+    for mode in ("peer", "peer_unfused", "nccl"):
         model = synthetic_int8_model(seed=4)
         apply_linear_kernels(model, lm_head=True)
         apply_decode_attn(model)
@@ -663,7 +663,9 @@ def qwen3_8b_int8_decode_sharded(rank, world, batches=(1, 16, 64), prompt=16, st
                 model(ids, cache, start_pos=0)
                 ref = model(nxt, cache, start_pos=prompt)[:, -1].float()
                 del cache
+        if mode != "nccl":
             peer = PeerGather(peer_bytes(model, max(batches)))
+            peer.fused = mode == "peer"
         else:
             peer = None
         shard_decode_model(model, rank, world, peer=peer, max_rows=max(batches))
@@ -691,9 +693,12 @@ def qwen3_8b_int8_decode_sharded(rank, world, batches=(1, 16, 64), prompt=16, st
                 del graph, cache
                 if mode == "peer":
                     entry.update({"ms_per_step": sec / steps * 1e3, "tok/s": B * steps / sec,
-                                  "split": f"column shards over {world} GPUs; b200mm_peer_gather over NVLink "
-                                           "after each projection (4 per layer + the LM head)",
+                                  "split": f"column shards over {world} GPUs; each projection's gather over "
+                                           "NVLink: fused into the projection kernel (b200mm_*_peer) at batch 1 "
+                                           "int8 / <= 4 bf16, else one b200mm_peer_gather launch",
                                   "peer_status": peer.status()})
+                elif mode == "peer_unfused":
+                    entry["tok/s_projection_then_peer_gather"] = B * steps / sec
                 else:
                     entry["tok/s_nccl_all_gather"] = B * steps / sec
         del model, peer

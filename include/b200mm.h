@@ -377,6 +377,56 @@ int b200mm_peer_gather(const void* src, int64_t ld_src, int64_t rows,
                        void* seen, void* err, int nctas, void* stream);
 
 /*
+ * Peer output of a projection (b200mm_*_peer): instead of a local y, the
+ * projection stores its output columns straight into every rank's gathered
+ * buffer, at the positions b200mm_peer_gather would give them; the launch's
+ * last CTA counts the launch done on every peer, then waits,
+ * bounded (5 s; *err = 1 when it runs out), until every peer's launch has
+ * counted itself done here.
+ *   dst[r], flags[r]: rank r's gathered buffer for this call site and its
+ *     uint32 counter array [8] (zeroed once), as device addresses valid on
+ *     this GPU; ld_dst: the gathered row stride (elements); part_widths /
+ *     nparts: this rank's output columns as parts (the fused QKV: q, k, v);
+ *   ticket, seen: this rank's uint32 words (zeroed once), err its status.
+ * Every rank issues the same sequence of peer-output projections on one
+ * stream, with the same shapes.
+ */
+typedef struct b200mm_peer_out {
+  void* dst[8];
+  int64_t ld_dst;
+  int64_t part_widths[3];
+  int32_t nparts;
+  int32_t rank;
+  int32_t world;
+  int32_t reserved;
+  void* flags[8];
+  void* ticket;
+  void* seen;
+  void* err;
+} b200mm_peer_out;
+
+/*
+ * b200mm_linear_peer, b200mm_linear_w8_peer, b200mm_gate_up_silu_w8_peer --
+ * b200mm_linear / b200mm_linear_w8 / b200mm_gate_up_silu_w8 on this rank's
+ * column shard, fused with the all-gather that follows them in the
+ * column-sharded decode step (the compute step and the collective in one
+ * kernel: the output tiles cross NVLink as they are produced).  Only the
+ * decode regime runs fused -- M <= 4 for 16-bit weights, M = 1 for int8 --
+ * other calls return B200MM_ERR_SHAPE and launch nothing (run the projection
+ * into a local buffer and b200mm_peer_gather instead).
+ */
+int b200mm_linear_peer(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                       int64_t M, int64_t N, int64_t K, int dtype,
+                       const b200mm_peer_out* out, void* stream);
+int b200mm_linear_w8_peer(const void* x, int64_t ldx, const int8_t* w, const float* s, int64_t ldw,
+                          int64_t M, int64_t N, int64_t K, int dtype,
+                          const b200mm_peer_out* out, void* stream);
+int b200mm_gate_up_silu_w8_peer(const void* x, int64_t ldx, const int8_t* wg, const float* sg,
+                                const int8_t* wu, const float* su, int64_t ldw,
+                                int64_t M, int64_t N, int64_t K, int dtype,
+                                const b200mm_peer_out* out, void* stream);
+
+/*
  * b200mm_mla_decode_noalloc -- no counterpart in the reference.
  *
  * b200mm_mla_decode for callers that cannot allocate device memory at decode

@@ -38,6 +38,24 @@ class MlaShape(ctypes.Structure):
     ]
 
 
+class PeerOut(ctypes.Structure):
+    """Mirror of ``b200mm_peer_out``."""
+
+    _fields_ = [
+        ("dst", ctypes.c_void_p * 8),
+        ("ld_dst", ctypes.c_int64),
+        ("part_widths", ctypes.c_int64 * 3),
+        ("nparts", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("world", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+        ("flags", ctypes.c_void_p * 8),
+        ("ticket", ctypes.c_void_p),
+        ("seen", ctypes.c_void_p),
+        ("err", ctypes.c_void_p),
+    ]
+
+
 # name -> (restype, argtypes); kept in the order of include/b200mm.h
 SIGNATURES: dict[str, tuple] = {
     "b200mm_status_string": (ctypes.c_char_p, [ctypes.c_int]),
@@ -107,6 +125,19 @@ SIGNATURES: dict[str, tuple] = {
         [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_i64, _c_p,
          _c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, ctypes.c_float,
          ctypes.c_int, _c_p],
+    ),
+    "b200mm_linear_peer": (
+        ctypes.c_int,
+        [_c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int, ctypes.POINTER(PeerOut), _c_p],
+    ),
+    "b200mm_linear_w8_peer": (
+        ctypes.c_int,
+        [_c_p, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int, ctypes.POINTER(PeerOut), _c_p],
+    ),
+    "b200mm_gate_up_silu_w8_peer": (
+        ctypes.c_int,
+        [_c_p, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int,
+         ctypes.POINTER(PeerOut), _c_p],
     ),
     "b200mm_peer_gather": (
         ctypes.c_int,

@@ -52,6 +52,8 @@ int check_device() {
 }
 
 int dense_dispatch(const DenseArgs& a) {
+  // peer output: the decode-regime GEMV only (it carries the gather epilogue)
+  if (a.peer) return a.M <= (a.w8 ? 1 : 4) && gemv_supported(a) ? gemv_launch(a) : B200MM_ERR_SHAPE;
   if (g_force_generic.load(std::memory_order_relaxed)) return tiled_launch(a);
 #ifdef SWAP_TRACE
   // development builds only: force one family ("gemv", "mmv", "swap", "tc")
@@ -96,9 +98,30 @@ int validate_dense(const DenseArgs& a) {
 
 bool fits_i32(int64_t v) { return v >= 0 && v < (int64_t(1) << 31); }
 
+int validate_peer(const b200mm_peer_out& po, int64_t N) {
+  if (po.world < 1 || po.world > 8 || po.rank < 0 || po.rank >= po.world) return B200MM_ERR_ARG;
+  if (po.nparts < 1 || po.nparts > 3) return B200MM_ERR_SHAPE;
+  int64_t sum = 0;
+  for (int j = 0; j < po.nparts; ++j) {
+    if (po.part_widths[j] < 1) return B200MM_ERR_SHAPE;
+    sum += po.part_widths[j];
+  }
+  if (sum != N || po.ld_dst < sum * po.world) return B200MM_ERR_SHAPE;
+  for (int r = 0; r < po.world; ++r)
+    if (!po.dst[r] || !po.flags[r] || ((uintptr_t)po.flags[r] & 3u)) return B200MM_ERR_ARG;
+  if (!po.ticket || !po.seen || !po.err) return B200MM_ERR_ARG;
+  return B200MM_OK;
+}
+
 int run_dense(DenseArgs& a, int64_t M, int64_t N, int64_t K) {
   if (!fits_i32(M) || !fits_i32(N) || !fits_i32(K)) return B200MM_ERR_SHAPE;
   a.M = (int)M; a.N = (int)N; a.K = (int)K;
+  if (a.peer) {
+    const int st = validate_peer(*a.peer, N);
+    if (st != B200MM_OK) return st;
+    a.y = a.peer->dst[a.peer->rank];  // (unused: the epilogue stores through dst[])
+    a.ldy = a.peer->ld_dst;
+  }
   int st = validate_dense(a);
   if (st != B200MM_OK) return st;
   if (a.M == 0) return B200MM_OK;
@@ -183,6 +206,37 @@ int b200mm_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, void* 
 int b200mm_linear_w8(const void* x, int64_t ldx, const int8_t* w, const float* s, int64_t ldw,
                      void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int dtype, void* stream) {
   return b200mm_qkv_w8(x, ldx, w, s, ldw, y, ldy, M, N, K, dtype, stream);
+}
+
+int b200mm_linear_peer(const void* x, int64_t ldx, const void* w, int64_t ldw, int64_t M, int64_t N, int64_t K,
+                       int dtype, const b200mm_peer_out* out, void* stream) {
+  if (!out) return B200MM_ERR_ARG;
+  DenseArgs a{};
+  a.x = x; a.ldx = ldx; a.w0 = w; a.ldw0 = ldw;
+  a.dtype = dtype; a.w8 = false; a.gate = false; a.peer = out;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return run_dense(a, M, N, K);
+}
+
+int b200mm_linear_w8_peer(const void* x, int64_t ldx, const int8_t* w, const float* s, int64_t ldw, int64_t M,
+                          int64_t N, int64_t K, int dtype, const b200mm_peer_out* out, void* stream) {
+  if (!out) return B200MM_ERR_ARG;
+  DenseArgs a{};
+  a.x = x; a.ldx = ldx; a.w0 = w; a.ldw0 = ldw; a.s0 = s;
+  a.dtype = dtype; a.w8 = true; a.gate = false; a.peer = out;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return run_dense(a, M, N, K);
+}
+
+int b200mm_gate_up_silu_w8_peer(const void* x, int64_t ldx, const int8_t* wg, const float* sg, const int8_t* wu,
+                                const float* su, int64_t ldw, int64_t M, int64_t N, int64_t K, int dtype,
+                                const b200mm_peer_out* out, void* stream) {
+  if (!out) return B200MM_ERR_ARG;
+  DenseArgs a{};
+  a.x = x; a.ldx = ldx; a.w0 = wg; a.ldw0 = ldw; a.w1 = wu; a.ldw1 = ldw;
+  a.s0 = sg; a.s1 = su; a.dtype = dtype; a.w8 = true; a.gate = true; a.peer = out;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return run_dense(a, M, N, K);
 }
 
 int b200mm_rmsnorm(const void* x, int64_t ldx, const void* residual, int64_t ldr, void* h_out, int64_t ldh,

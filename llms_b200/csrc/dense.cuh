@@ -18,6 +18,7 @@ struct DenseArgs {
   int dtype;                        // B200MM_F32 / F16 / BF16 (x, y, dense w)
   bool w8;                          // weights are int8
   bool gate;                        // gate-up-SiLU epilogue
+  const b200mm_peer_out* peer;      // non-null: store into every rank's gathered buffer (GEMV only)
   cudaStream_t stream;
 };
 

@@ -37,6 +37,32 @@ class PeerSite:
     def __init__(self, ctx: "PeerGather", offset: int, max_rows: int, width: int, dtype: torch.dtype) -> None:
         self.ctx, self.offset, self.max_rows, self.width, self.dtype = ctx, offset, max_rows, width, dtype
 
+    def peer_out(self, parts: tuple[int, ...]) -> "_capi.PeerOut":
+        """The ``b200mm_peer_out`` of this site for a shard made of ``parts``
+        (cached per parts; the projection kernels write the gathered result
+        here themselves)."""
+        po = self._outs.get(parts) if hasattr(self, "_outs") else None
+        if po is None:
+            ctx = self.ctx
+            po = _capi.PeerOut()
+            for r in range(ctx.world):
+                po.dst[r] = ctx.peer_ptrs[r] + self.offset
+                po.flags[r] = ctx.fused_flag_ptrs[r]
+            po.ld_dst = self.width
+            for j, w in enumerate(parts):
+                po.part_widths[j] = w
+            po.nparts, po.rank, po.world = len(parts), ctx.rank, ctx.world
+            po.ticket, po.seen, po.err = ctx.ticket_ptr, ctx.fused_seen_ptr, ctx.err_ptr
+            self._outs = getattr(self, "_outs", {})
+            self._outs[parts] = po
+        return po
+
+    def result(self, lead: tuple[int, ...], rows: int) -> torch.Tensor:
+        """The gathered (..., width) view of this site's first ``rows`` rows."""
+        esz = torch.tensor([], dtype=self.dtype).element_size()
+        out = self.ctx.buf[self.offset:self.offset + rows * self.width * esz].view(self.dtype)
+        return out.view(rows, self.width).view(*lead, self.width)
+
     def fits(self, y: torch.Tensor) -> bool:
         rows = y.numel() // y.shape[-1] if y.dim() else 0
         return (y.is_cuda and y.dtype == self.dtype and rows <= self.max_rows
@@ -56,7 +82,6 @@ class PeerSite:
         if y2.stride(-1) != 1:
             y2 = y2.contiguous()
         rows = y2.shape[0]
-        esz = y.element_size()
         dst = (ctypes.c_void_p * ctx.world)(*[p + self.offset for p in ctx.peer_ptrs])
         widths = (ctypes.c_int64 * len(parts))(*parts)
         with _capi.on_device(y2):
@@ -65,8 +90,7 @@ class PeerSite:
                                               ctx.flag_ptrs, ctx.seen_ptr, ctx.err_ptr, NCTAS,
                                               _capi.stream_of(y2))
         _capi.check(st, "b200mm_peer_gather")
-        out = ctx.buf[self.offset:self.offset + rows * self.width * esz].view(y.dtype).view(rows, self.width)
-        return out.view(*lead, self.width)
+        return self.result(lead, rows)
 
 
 class PeerGather:
@@ -81,8 +105,11 @@ class PeerGather:
         if self.world > 8:
             raise ValueError(f"b200mm_peer_gather supports up to 8 ranks, not {self.world}")
         device = torch.device(device or torch.cuda.current_device())
+        # head: gather flags [world][NCTAS], seen [NCTAS], err, then the
+        # fused projections' counters [8], ticket and seen
         self.flags_bytes = self.world * NCTAS * 4
-        self.head = _align(self.flags_bytes + NCTAS * 4 + 4)
+        self.fused_off = self.flags_bytes + NCTAS * 4 + 4
+        self.head = _align(self.fused_off + 8 * 4 + 8)
         self.capacity = _align(capacity_bytes)
         name = getattr(self.group, "group_name", None)
         if hasattr(symm_mem, "enable_symm_mem_for_group") and name is not None:
@@ -96,7 +123,13 @@ class PeerGather:
         base = self.buf.data_ptr()
         self.seen_ptr = base + self.flags_bytes
         self.err_ptr = base + self.flags_bytes + NCTAS * 4
+        self.fused_flag_ptrs = [p + self.fused_off for p in self.peer_ptrs]
+        self.ticket_ptr = base + self.fused_off + 8 * 4
+        self.fused_seen_ptr = self.ticket_ptr + 4
         self._cursor = self.head
+        # the sharded modules fuse a gather into its projection where they can
+        # (b200mm_*_peer); False keeps projection and b200mm_peer_gather apart
+        self.fused = True
         dist.barrier(group=self.group)
 
     def site(self, max_rows: int, width: int, dtype: torch.dtype) -> PeerSite:

@@ -20,9 +20,12 @@ the local shard: ``int8_linear`` / ``int8_fused_gate_up_silu`` for the int8
 projections and ``b200_linear`` for ``o`` / ``down``.
 
 With a ``peer.PeerGather`` context (``shard_decode_model(..., peer=ctx)``)
-each of the four gathers per layer is one ``b200mm_peer_gather`` launch over
-NVLink into a region of its own instead of an NCCL all-gather plus a permute;
-batches above the context's row budget fall back to NCCL.
+the gathers run over NVLink into a region of their own per call site instead
+of an NCCL all-gather plus a permute: at decode batch 1 (int8) / up to 4
+(16-bit) the projection kernel itself stores its outputs into every rank's
+region (``b200mm_*_peer``: compute and gather in one kernel); at larger
+batches the projection is followed by one ``b200mm_peer_gather`` launch;
+beyond the context's row budget, NCCL.
 """
 
 from __future__ import annotations
@@ -31,6 +34,7 @@ import torch
 import torch.distributed as dist
 from torch import nn
 
+from . import _capi
 from .kernels.linear import b200_linear, int8_linear
 from .kernels.quant import Int8Attention, Int8FFN, int8_fused_gate_up_silu
 
@@ -85,6 +89,31 @@ def gather_qkv(y: torch.Tensor, cq: int, ck: int, world: int, group=None, site=N
     return tuple(p.permute(1, 0, 2).reshape(*lead, world * p.shape[-1]) for p in parts)
 
 
+def _fused_peer(site, x: torch.Tensor, n_out: int, parts, int8: bool, call):
+    """Run the projection with its all-gather fused in (the ``b200mm_*_peer``
+    entry points: the kernel stores into every rank's gathered buffer) when
+    the call is in the fused regime -- one token row for int8 weights, up to
+    four for 16-bit, at most the site's rows; returns the gathered tensor, or
+    None for the caller's unfused path."""
+    if site is None or site.ctx.world == 1 or not site.ctx.fused:
+        return None
+    K = x.shape[-1]
+    rows = x.numel() // K if K else 0
+    if (rows < 1 or rows > (1 if int8 else 4) or rows > site.max_rows or not x.is_cuda or x.dtype != site.dtype
+            or n_out * site.ctx.world != site.width):
+        return None
+    x2 = x.reshape(-1, K)
+    if x2.stride(-1) != 1 or (x2.stride(0) * x2.element_size()) % 16 or x2.data_ptr() % 16:
+        return None
+    po = site.peer_out(tuple(parts))
+    with _capi.on_device(x2):
+        st = call(x2, rows, po)
+    if st == 1:  # B200MM_ERR_SHAPE: outside the fused regime, nothing launched
+        return None
+    _capi.check(st, "b200mm_*_peer")
+    return site.result(tuple(x.shape[:-1]), rows)
+
+
 class ShardedLinear(nn.Module):
     """Bias-free projection holding this rank's block of output rows of the
     full weight; the output is gathered back to the full width."""
@@ -95,7 +124,15 @@ class ShardedLinear(nn.Module):
         self.world, self.group, self.site = world, group, None
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return gather_cols(b200_linear(x, self.weight), self.world, self.group, self.site)
+        w = self.weight
+        if w.dtype == x.dtype and w.stride(-1) == 1:
+            y = _fused_peer(self.site, x, w.shape[0], (w.shape[0],), False,
+                            lambda x2, rows, po: _capi.lib.b200mm_linear_peer(
+                                x2.data_ptr(), x2.stride(0), w.data_ptr(), w.stride(0), rows, w.shape[0], w.shape[1],
+                                _capi.dtype_code(x.dtype), po, _capi.stream_of(x2)))
+            if y is not None:
+                return y
+        return gather_cols(b200_linear(x, w), self.world, self.group, self.site)
 
 
 class ShardedInt8Attention(Int8Attention):
@@ -121,8 +158,15 @@ class ShardedInt8Attention(Int8Attention):
         return out
 
     def project_qkv(self, x: torch.Tensor):
-        y = int8_linear(x, self.q_qkv, self.s_qkv)
-        return gather_qkv(y, self.n_q // self.world, self.n_k // self.world, self.world, self.group, self.site)
+        cq, ck, q, s = self.n_q // self.world, self.n_k // self.world, self.q_qkv, self.s_qkv
+        y = _fused_peer(self.site, x, q.shape[0], (cq, ck, ck), True,
+                        lambda x2, rows, po: _capi.lib.b200mm_linear_w8_peer(
+                            x2.data_ptr(), x2.stride(0), q.data_ptr(), s.data_ptr(), q.stride(0), rows, q.shape[0],
+                            q.shape[1], _capi.dtype_code(x.dtype), po, _capi.stream_of(x2)))
+        if y is not None:
+            return y.split([self.world * cq, self.world * ck, self.world * ck], dim=-1)
+        y = int8_linear(x, q, s)
+        return gather_qkv(y, cq, ck, self.world, self.group, self.site)
 
 
 class ShardedInt8FFN(Int8FFN):
@@ -144,8 +188,15 @@ class ShardedInt8FFN(Int8FFN):
         return out
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        h = int8_fused_gate_up_silu(x, self.qg, self.sg, self.qu, self.su)
-        return self.down(gather_cols(h, self.world, self.group, self.site))
+        qg, sg, qu, su = self.qg, self.sg, self.qu, self.su
+        h = _fused_peer(self.site, x, qg.shape[0], (qg.shape[0],), True,
+                        lambda x2, rows, po: _capi.lib.b200mm_gate_up_silu_w8_peer(
+                            x2.data_ptr(), x2.stride(0), qg.data_ptr(), sg.data_ptr(), qu.data_ptr(), su.data_ptr(),
+                            qg.stride(0), rows, qg.shape[0], qg.shape[1], _capi.dtype_code(x.dtype), po,
+                            _capi.stream_of(x2)))
+        if h is None:
+            h = gather_cols(int8_fused_gate_up_silu(x, qg, sg, qu, su), self.world, self.group, self.site)
+        return self.down(h)
 
 
 def peer_bytes(model: nn.Module, max_rows: int) -> int:

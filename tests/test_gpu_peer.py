@@ -1,7 +1,9 @@
 """b200mm_peer_gather on two GPUs: the peer-memory all-gather of the
 column-sharded decode step against NCCL's all-gather on the same blocks, and
-the sharded Qwen3-8B-shaped step with peer gathers against the same step with
-NCCL gathers (the kernels are the same, so the logits must be identical).
+the sharded Qwen3-8B-shaped step with peer gathers -- at batch 1 fused into
+the projection kernels (b200mm_*_peer), at batch 4 partly -- against the same
+step with NCCL gathers (the arithmetic is the same, so the logits must be
+identical).
 One process per GPU; skipped with fewer than two GPUs."""
 
 import multiprocessing as mp
@@ -61,6 +63,8 @@ def _worker(rank, world, port, out):
             torch.cuda.synchronize()
             want = torch.cat([torch.full((16, 512), float(10 * r + call), device="cuda") for r in range(world)], 1)
             res[f"graph_{call}"] = bool(torch.equal(gy.float(), want))
+            # a peer's next gather writes this site again: read it first
+            dist.barrier()
         res["status"] = ctx.status()
 
         # the sharded 8B-shaped step (2 layers, small vocabulary): peer vs NCCL gathers
@@ -76,17 +80,22 @@ def _worker(rank, world, port, out):
             apply_decode_attn(model)
             peer = PeerGather(peer_bytes(model, 16)) if mode == "peer" else None
             shard_decode_model(model, rank, world, peer=peer, max_rows=16)
-            g = torch.Generator(device="cuda").manual_seed(5)
-            ids = torch.randint(0, shape.vocab_size, (4, 8), device="cuda", generator=g)
-            nxt = torch.randint(0, shape.vocab_size, (4, 1), device="cuda", generator=g)
-            with torch.inference_mode():
-                cache = model.alloc_cache(16, max_batch=4)
-                model(ids, cache, start_pos=0)  # prefill: 32 rows > 16, the NCCL fallback
-                logits[mode] = model(nxt, cache, start_pos=8)[:, -1].float().cpu()
+            for B in (1, 4):  # B = 1: every projection fused with its gather; B = 4: int8 + b200mm_peer_gather
+                g = torch.Generator(device="cuda").manual_seed(5)
+                ids = torch.randint(0, shape.vocab_size, (B, 8), device="cuda", generator=g)
+                nxt = torch.randint(0, shape.vocab_size, (B, 1), device="cuda", generator=g)
+                with torch.inference_mode():
+                    cache = model.alloc_cache(16, max_batch=B)
+                    model(ids, cache, start_pos=0)  # prefill: 8 B rows, the NCCL fallback above 16
+                    for step in range(2):
+                        logits[(mode, B, step)] = model(nxt, cache, start_pos=8 + step)[:, -1].float().cpu()
             if peer is not None:
                 res["model_status"] = peer.status()
             del model, peer
-        res["model_equal"] = bool(torch.equal(logits["nccl"], logits["peer"]))
+        for B in (1, 4):
+            for step in range(2):
+                res[f"model_equal_b{B}_{step}"] = bool(torch.equal(logits[("nccl", B, step)],
+                                                                   logits[("peer", B, step)]))
         out.put((rank, res))
     except Exception as e:  # noqa: BLE001 -- reported to the parent
         out.put((rank, {"error": f"{type(e).__name__}: {e}"}))
