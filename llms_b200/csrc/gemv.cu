@@ -101,9 +101,14 @@ constexpr int gemv_min_blocks() {
   return MR <= 4 ? 2 : 1;
 }
 
-template <typename TX, typename TW, int MR, bool GATE, int NCH>
+// GEN: the general form (K slices, peer output); the plain form compiles
+// both out (ks = 1, local y), since the general form's extra state cost the
+// whole-shape QKV launch ~5 % (7.0 -> 7.4 us).
+template <typename TX, typename TW, int MR, bool GATE, int NCH, bool GEN>
 __global__ void __launch_bounds__(kThreads, gemv_min_blocks<MR, GATE>())
-gemv_kernel(const GemvParams p, const int nsm, const int ks) {
+gemv_kernel(const GemvParams p, const int nsm, const int ks_arg) {
+  const int ks = GEN ? ks_arg : 1;
+  const int world = GEN ? p.world : 0;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   TX* xs = reinterpret_cast<TX*>(smem_raw);  // [MR][K] activation rows
   __shared__ float red[kThreads / 32][2][MR];  // K-slice partial sums (ks > 1)
@@ -294,12 +299,12 @@ gemv_kernel(const GemvParams p, const int nsm, const int ks) {
         if (m == lane) { a0 = acc[0][m]; a1 = acc[1][m]; }
       TX* y = static_cast<TX*>(p.y) + (int64_t)lane * p.ldy;
       auto put = [&](int n, float v) {
-        if (p.world == 0) {
+        if (world == 0) {
           y[n] = from_f<TX>(v);
         } else {
           const int64_t d = (int64_t)lane * p.ld_peer + peer_col(p, n);
           const TX o = from_f<TX>(v);
-          for (int r = 0; r < p.world; ++r) static_cast<TX*>(p.pdst[r])[d] = o;
+          for (int r = 0; r < world; ++r) static_cast<TX*>(p.pdst[r])[d] = o;
         }
       };
       if (GATE) {
@@ -316,30 +321,36 @@ gemv_kernel(const GemvParams p, const int nsm, const int ks) {
       }
     }
   }
-  if (p.world > 0) peer_finish(p);
+  if (world > 0) peer_finish(p);
 }
 
 template <typename TX, typename TW, int MR, bool GATE>
 int launch_one(const DenseArgs& a) {
   constexpr int NCH = (sizeof(TW) == 2) ? 10 : 8;
-  auto kern = gemv_kernel<TX, TW, MR, GATE, NCH>;
+  void (*const kerns[2])(const GemvParams, const int, const int) = {gemv_kernel<TX, TW, MR, GATE, NCH, false>,
+                                                                   gemv_kernel<TX, TW, MR, GATE, NCH, true>};
   const size_t smem = (size_t)MR * a.K * sizeof(TX);
-  static int configured_smem[64] = {0};  // per device: largest opt-in set so far
-  static int blocks_per_sm[64][8] = {{0}};
+  static int configured_smem[2][64] = {{0}};  // per form and device: largest opt-in set so far
+  static int blocks_per_sm[2][64][8] = {{{0}}};
   int dev = current_device();
   if (dev < 0 || dev >= 64) return B200MM_ERR_DEVICE;
-  if (smem > 48 * 1024 && (int)smem > configured_smem[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return B200MM_ERR_LAUNCH;
-    configured_smem[dev] = (int)smem;
-  }
-  // occupancy depends on smem; cache per (device, smem bucket of 32 KB)
+  // occupancy depends on smem; cache per (form, device, smem bucket of 32 KB)
   const int bucket = (int)(smem >> 15) < 8 ? (int)(smem >> 15) : 7;
-  int& bps = blocks_per_sm[dev][bucket];
-  if (bps == 0) {
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, kern, kThreads, smem) != cudaSuccess || bps < 1)
-      bps = 1;
-  }
+  auto prepare = [&](int g) -> int {
+    if (smem > 48 * 1024 && (int)smem > configured_smem[g][dev]) {
+      if (cudaFuncSetAttribute(kerns[g], cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return -1;
+      configured_smem[g][dev] = (int)smem;
+    }
+    int& b = blocks_per_sm[g][dev][bucket];
+    if (b == 0) {
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kerns[g], kThreads, smem) != cudaSuccess || b < 1)
+        b = 1;
+    }
+    return b;
+  };
+  int bps = prepare(0);
+  if (bps < 0) return B200MM_ERR_LAUNCH;
   const int nunits = a.gate ? a.N : (a.N + 1) / 2;
   const int warps_per_cta = kThreads / 32;
   const int slots = num_sms(dev) * bps * warps_per_cta;  // resident warps
@@ -352,6 +363,11 @@ int launch_one(const DenseArgs& a) {
   constexpr int WV = 16 / (int)sizeof(TW);
   int ks = 1;
   while (ks < 8 && (int64_t)nunits * 2 * ks <= slots && a.K / WV / (2 * ks) >= 32) ks *= 2;
+  const int gen = ks > 1 || a.peer ? 1 : 0;
+  if (gen) {
+    bps = prepare(1);
+    if (bps < 0) return B200MM_ERR_LAUNCH;
+  }
   const int upc = warps_per_cta / ks;
   int grid = num_sms(dev) * bps;
   const int need = (nunits + upc - 1) / upc;
@@ -379,7 +395,7 @@ int launch_one(const DenseArgs& a) {
     p.err = static_cast<int*>(po.err);
   }
   // plain projections: warps take units in SM-round-robin order (below)
-  cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, a.stream, p, GATE ? 0 : num_sms(dev), ks);
+  cudaError_t e = launch_pdl(kerns[gen], dim3(grid), dim3(kThreads), smem, a.stream, p, GATE ? 0 : num_sms(dev), ks);
   return e == cudaSuccess ? B200MM_OK : B200MM_ERR_LAUNCH;
 }
 
