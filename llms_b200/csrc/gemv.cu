@@ -53,18 +53,19 @@ __device__ __forceinline__ int64_t peer_col(const GemvParams& p, int n) {
   return p.pdoff[j] + (int64_t)p.rank * p.pw[j] + c;
 }
 
-// The launch's output has been stored on every rank: each CTA fences its
-// stores and takes a ticket; the launch's last CTA on this rank counts the
-// launch done on every peer (one remote add per peer, not one per CTA) and
-// then waits (bounded) until every peer's launch has counted itself done here.
+// The launch's output has been stored on every rank: each CTA takes a ticket
+// with a release (after a barrier, so it covers the CTA's stores); the
+// launch's last CTA, whose ticket acquires all of them, counts the launch done
+// on every peer with a system-scope release add (cumulative: it carries the
+// other CTAs' stores too; one remote add per peer, not one per CTA) and then
+// waits (bounded) until every peer's launch has counted itself done here.
 __device__ void peer_finish(const GemvParams& p) {
   __syncthreads();  // the CTA's stores are issued
   if (threadIdx.x != 0) return;
-  __threadfence_system();
-  const unsigned t = atomicAdd(p.ticket, 1u);
+  unsigned t;
+  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(t) : "l"(p.ticket) : "memory");
   if (t + 1 != gridDim.x) return;
   atomicExch(p.ticket, 0u);  // the next launch on this stream starts after this one ends
-  __threadfence_system();
   for (int r = 0; r < p.world; ++r)
     if (r != p.rank)
       asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(p.pflags[r] + p.rank) : "memory");
