@@ -368,11 +368,16 @@ class DecodeJob:
         return g, launches
 
 
-def gather(job, world):
+def gather(job, world, nccl=False):
+    """The step's outputs of every rank into job.gathered (rank-major blocks):
+    one b200mm_peer_gather launch over NVLink, or NCCL's all-gather."""
     if world > 1:
-        import torch.distributed as dist
+        if job.site is not None and not nccl:
+            job.site.gather(job.flat.view(1, -1))
+        else:
+            import torch.distributed as dist
 
-        dist.all_gather_into_tensor(job.gathered, job.flat)
+            dist.all_gather_into_tensor(job.gathered_nccl, job.flat)
 
 
 def time_graph(graph, steps, warmup, world, post=None):
@@ -733,16 +738,19 @@ def mla_sharded(rank, world, B=32, steps=10):
         ks, kz = mla.mla_sidebands(c, kr, wuk, kw, inv, B=b, L=L, num_kv_heads=KV, head_dim=D, eps=1e-6)
         del kr
         if ctx:
-            import torch.distributed as dist
+            from llms_b200.peer import PeerGather
+
             mine = torch.empty(mla.partial_numel(b, H, R), device="cuda")
-            parts = torch.empty(world, mine.numel(), device="cuda")
+            peer = PeerGather(world * mine.numel() * 4 + 4096)
+            site = peer.site(1, world * mine.numel(), torch.float32)
+            parts = site.result((1,), 1).view(world, mine.numel())
             ws = torch.empty(mla.workspace_bytes(b, H, KV, D, DR, R, len(toks), torch.bfloat16), dtype=torch.uint8,
                              device="cuda")
 
             def fn():
                 mla.mla_decode_partial(q, c, kz, ks, wuk, kw, inv, num_kv_heads=KV, L=L, tokens=toks,
                                        scale=D ** -0.5, eps=1e-6, out=mine, workspace=ws)
-                dist.all_gather_into_tensor(parts, mine)  # the one exchange of the step
+                site.gather(mine.view(1, -1))  # the one exchange of the step (into `parts`)
                 return mla.mla_combine_partials(parts, wuv, batch=b, num_heads=H, head_dim=D, d_rope=DR,
                                                  dtype=torch.bfloat16, eps=1e-6)
         else:
@@ -770,7 +778,7 @@ def mla_sharded(rank, world, B=32, steps=10):
         rank_bytes = 0
     per = sec / steps
     alg = 1024 * B * L + 32 * B * L + 917504 + 512 * B
-    split = ("context slices of every row, partial softmaxes all-gathered and merged" if ctx
+    split = ("context slices of every row, partial softmaxes all-gathered (b200mm_peer_gather) and merged" if ctx
              else "batch rows (no collective in the op)")
     return {"GB/s": alg / per / 1e9, "us_per_step": per * 1e6, "B": B, "L": L,
             "split": f"{split} over {world} GPUs", "rank0_cache_bytes": rank_bytes if rank == 0 else None,
@@ -1019,24 +1027,38 @@ def main():
     from llms_b200.kernels import triton_fused_gate_up_silu, triton_fused_qkv
 
     job = DecodeJob(rank, world)
+    job.site = None
+    if world > 1:
+        from llms_b200.peer import PeerGather
+
+        peer = PeerGather(job.out_numel * world * 2 + 4096)
+        job.site = peer.site(1, job.out_numel * world, torch.bfloat16)
+        job.gathered_nccl = job.gathered
+        job.gathered = job.site.result((1,), 1).view(-1)
 
     # ---- device-timed job: graph of 72 launches + pack, gather outside ----
     def step():
         job.step_kernels()
         job.pack()
+        gather(job, world)  # N > 1: one b200mm_peer_gather launch, captured with the step
 
     graph, launches_per_step = job.capture(step)
-    post = (lambda: gather(job, world)) if world > 1 else None
     with ClockSampler(local) as clk:
         time.sleep(0.5)  # let nvidia-smi start sampling before the timed region
-        sec = time_graph(graph, args.steps, max(3, args.warmup), world, post)
+        sec = time_graph(graph, args.steps, max(3, args.warmup), world)
     clocks = clk.summary()
     per_step = sec / args.steps
     limiter = None
     if world > 1:
         # the step's two parts timed apart (device time, max over ranks): this
         # rank's kernels (the graph alone) and the output all-gather alone
-        k_sec = time_graph(graph, args.steps, 3, world)
+        def kernels_only():
+            job.step_kernels()
+            job.pack()
+
+        k_graph, _ = job.capture(kernels_only)
+        k_sec = time_graph(k_graph, args.steps, 3, world)
+        del k_graph
         torch.cuda.synchronize()
         barrier(world)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -1046,7 +1068,16 @@ def main():
         e1.record()
         torch.cuda.synchronize()
         g_sec = max_over_ranks(e0.elapsed_time(e1) / 1e3, world)
+        barrier(world)
+        e0.record()
+        for _ in range(args.steps):
+            gather(job, world, nccl=True)
+        e1.record()
+        torch.cuda.synchronize()
+        n_sec = max_over_ranks(e0.elapsed_time(e1) / 1e3, world)
         limiter = {"kernels_ms_per_step": k_sec / args.steps * 1e3, "all_gather_ms_per_step": g_sec / args.steps * 1e3,
+                   "all_gather": "b200mm_peer_gather (one launch over NVLink)",
+                   "nccl_all_gather_ms_per_step": n_sec / args.steps * 1e3,
                    "kernel_GB/s_per_rank": job.bytes_step / (k_sec / args.steps) / 1e9,
                    "gather_bytes_per_rank": job.out_numel * 2 * world}
     total_bytes = job.bytes_step * world
@@ -1167,7 +1198,8 @@ def main():
             "data": "synthetic (seeded N(0,0.02) bf16 weights, N(0,1) activations)",
             "config": {"workload": WORKLOAD,
                        "model": "Qwen3-4B-shaped (random init)", "M": 1, "layers": LAYERS, "seq_len": 1,
-                       "parallelism": f"column-shard x{world} (head-aligned), NCCL all-gather of outputs",
+                       "parallelism": f"column-shard x{world} (head-aligned), outputs all-gathered over NVLink "
+                                      "(b200mm_peer_gather)",
                        "l2": "inputs larger than L2: 4.72 GB of distinct weights per step"},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,

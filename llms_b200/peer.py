@@ -82,8 +82,13 @@ class PeerSite:
         if y2.stride(-1) != 1:
             y2 = y2.contiguous()
         rows = y2.shape[0]
-        dst = (ctypes.c_void_p * ctx.world)(*[p + self.offset for p in ctx.peer_ptrs])
-        widths = (ctypes.c_int64 * len(parts))(*parts)
+        cached = getattr(self, "_args", {}).get(parts)
+        if cached is None:  # the call's pointer arrays, built once per parts
+            cached = ((ctypes.c_void_p * ctx.world)(*[p + self.offset for p in ctx.peer_ptrs]),
+                      (ctypes.c_int64 * len(parts))(*parts))
+            self._args = getattr(self, "_args", {})
+            self._args[parts] = cached
+        dst, widths = cached
         with _capi.on_device(y2):
             st = _capi.lib.b200mm_peer_gather(y2.data_ptr(), y2.stride(0), rows, widths, len(parts), dst,
                                               self.width, _capi.dtype_code(y.dtype), ctx.rank, ctx.world,
