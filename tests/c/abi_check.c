@@ -2,6 +2,7 @@
  * library, and exercises the calls that need no GPU (version, status strings,
  * workspace sizes, argument validation).  Exit status 0 when every check
  * holds; the failing check is printed otherwise. */
+#include <stddef.h>
 #include <stdint.h>
 #include <stdio.h>
 #include <string.h>
@@ -28,6 +29,24 @@ int main(void) {
   CHECK(b200mm_qkv(p, 64, p, 64, p, 96, 1, 96, 0, B200MM_BF16, NULL) == B200MM_ERR_SHAPE);
   CHECK(b200mm_linear(p, 64, p, 64, p, 32, 1, 32, 64, 42, NULL) == B200MM_ERR_DTYPE);
   CHECK(b200mm_linear(p, 64, p, 64, p, 32, 0, 32, 64, B200MM_BF16, NULL) == B200MM_OK); /* M == 0 */
+
+  /* peer output: layout (mirrored by llms_b200._capi.PeerOut) and validation */
+  CHECK(sizeof(b200mm_peer_out) == 200);
+  CHECK(offsetof(b200mm_peer_out, ld_dst) == 64 && offsetof(b200mm_peer_out, nparts) == 96);
+  CHECK(offsetof(b200mm_peer_out, flags) == 112 && offsetof(b200mm_peer_out, err) == 192);
+  CHECK(b200mm_linear_peer(p, 64, p, 64, 1, 32, 64, B200MM_BF16, NULL, NULL) == B200MM_ERR_ARG);
+  b200mm_peer_out po;
+  memset(&po, 0, sizeof(po));
+  CHECK(b200mm_linear_peer(p, 64, p, 64, 1, 32, 64, B200MM_BF16, &po, NULL) == B200MM_ERR_ARG); /* world 0 */
+  po.world = 2; po.rank = 0; po.nparts = 1; po.part_widths[0] = 16; po.ld_dst = 64;
+  po.dst[0] = po.dst[1] = p; po.flags[0] = po.flags[1] = p; po.ticket = po.seen = po.err = p;
+  CHECK(b200mm_linear_peer(p, 64, p, 64, 1, 32, 64, B200MM_BF16, &po, NULL) == B200MM_ERR_SHAPE); /* 16 != N */
+  CHECK(b200mm_gate_up_silu_w8_peer(p, 64, p, p, p, p, 64, 0, 16, 64, B200MM_BF16, &po, NULL) == B200MM_OK);
+  {
+    int64_t w = 16;
+    void* ptrs[2] = {p, p};
+    CHECK(b200mm_peer_gather(p, 16, 1, &w, 1, ptrs, 32, 42, 0, 2, ptrs, p, p, 16, NULL) == B200MM_ERR_DTYPE);
+  }
 
   b200mm_mla_shape s = {1, 32, 8, 128, 32, 256, B200MM_BF16, 1e-6f};
   CHECK(b200mm_mla_decode_workspace_size(&s, 32768) > 0);

@@ -160,3 +160,13 @@ def test_new_ops_check_arguments_on_the_host():
                          torch.zeros(2, 3, 10, 64, dtype=torch.bfloat16), scale=0.1)
     with pytest.raises(RuntimeError, match="no CPU path"):
         b200_decode_attn(q, k, k, scale=0.1)
+
+
+def test_peer_out_mirror_matches_header_layout():
+    """llms_b200._capi.PeerOut has b200mm_peer_out's layout (the C side checks
+    the same offsets in tests/c/abi_check.c)."""
+    import ctypes
+    from llms_b200._capi import PeerOut
+    assert ctypes.sizeof(PeerOut) == 200
+    assert PeerOut.ld_dst.offset == 64 and PeerOut.nparts.offset == 96
+    assert PeerOut.flags.offset == 112 and PeerOut.err.offset == 192
