@@ -411,9 +411,9 @@ typedef struct b200mm_peer_out {
  * column shard, fused with the all-gather that follows them in the
  * column-sharded decode step (the compute step and the collective in one
  * kernel: the output tiles cross NVLink as they are produced).  Only the
- * decode regime runs fused -- M <= 4 for 16-bit weights, M = 1 for int8 --
- * other calls return B200MM_ERR_SHAPE and launch nothing (run the projection
- * into a local buffer and b200mm_peer_gather instead).
+ * decode regime runs fused -- M <= 8 for 16-bit weights (gate-up 16), M <= 32
+ * for int8 -- other calls return B200MM_ERR_SHAPE and launch nothing (run
+ * the projection into a local buffer and b200mm_peer_gather instead).
  */
 int b200mm_linear_peer(const void* x, int64_t ldx, const void* w, int64_t ldw,
                        int64_t M, int64_t N, int64_t K, int dtype,

@@ -52,8 +52,13 @@ int check_device() {
 }
 
 int dense_dispatch(const DenseArgs& a) {
-  // peer output: the decode-regime GEMV only (it carries the gather epilogue)
-  if (a.peer) return a.M <= (a.w8 ? 1 : 4) && gemv_supported(a) ? gemv_launch(a) : B200MM_ERR_SHAPE;
+  // peer output: the decode-regime families that carry the gather epilogue,
+  // chosen exactly as below
+  if (a.peer) {
+    if (a.M <= (a.w8 ? 1 : 4) && gemv_supported(a)) return gemv_launch(a);
+    if (a.M <= (a.w8 ? 32 : a.gate ? 16 : 8) && mmv_supported(a)) return mmv_launch(a);
+    return B200MM_ERR_SHAPE;
+  }
   if (g_force_generic.load(std::memory_order_relaxed)) return tiled_launch(a);
 #ifdef SWAP_TRACE
   // development builds only: force one family ("gemv", "mmv", "swap", "tc")

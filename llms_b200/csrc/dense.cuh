@@ -24,6 +24,98 @@ struct DenseArgs {
 
 int dense_dispatch(const DenseArgs& a);
 
+// ---------------------------------------------------------------------------
+// Peer output (the b200mm_*_peer entry points): a projection's epilogue
+// stores column n of this rank's shard into every rank's gathered buffer, at
+// the column an all-gather would give it, and the launch ends with one
+// completion count per peer and a bounded wait for the peers' counts.
+// ---------------------------------------------------------------------------
+struct PeerEpi {
+  int world, rank, nparts;  // world == 0: no peer output
+  int64_t ld;               // gathered row stride (elements)
+  int64_t pw[3], pdoff[3];  // part widths; part j's rank-0 column in the gathered row
+  void* pdst[8];
+  unsigned* pflags[8];
+  unsigned* ticket;
+  unsigned* seen;
+  int* err;
+};
+
+inline void peer_epi_from(const b200mm_peer_out& po, PeerEpi& e) {
+  e.world = po.world;
+  e.rank = po.rank;
+  e.nparts = po.nparts;
+  e.ld = po.ld_dst;
+  int64_t off = 0;
+  for (int j = 0; j < po.nparts; ++j) {
+    e.pw[j] = po.part_widths[j];
+    e.pdoff[j] = off;
+    off += po.part_widths[j] * po.world;
+  }
+  for (int r = 0; r < po.world; ++r) {
+    e.pdst[r] = po.dst[r];
+    e.pflags[r] = static_cast<unsigned*>(po.flags[r]);
+  }
+  e.ticket = static_cast<unsigned*>(po.ticket);
+  e.seen = static_cast<unsigned*>(po.seen);
+  e.err = static_cast<int*>(po.err);
+}
+
+constexpr unsigned long long kPeerWaitNs = 5ull * 1000 * 1000 * 1000;  // 5 s
+
+__device__ __forceinline__ int64_t peer_col(const PeerEpi& e, int n) {
+  int64_t c = n;
+  int j = 0;
+  while (j + 1 < e.nparts && c >= e.pw[j]) c -= e.pw[j++];
+  return e.pdoff[j] + (int64_t)e.rank * e.pw[j] + c;
+}
+
+// Row `row`, shard column n, value v -> every rank's gathered buffer.
+template <typename TX>
+__device__ __forceinline__ void peer_store(const PeerEpi& e, int64_t row, int n, TX v) {
+  const int64_t d = row * e.ld + peer_col(e, n);
+  for (int r = 0; r < e.world; ++r) static_cast<TX*>(e.pdst[r])[d] = v;
+}
+
+// End of a peer-output launch (every thread of every CTA calls it): each CTA
+// takes a ticket with a release (after a barrier, so it covers the CTA's
+// stores); the launch's last CTA, whose ticket acquires all of them, counts
+// the launch done on every peer with a system-scope release add (cumulative:
+// it carries the other CTAs' stores too; one remote add per peer, not one per
+// CTA) and then waits (bounded) until every peer's launch has counted itself
+// done here.  A full system fence per CTA instead cost ~8 us per launch.
+__device__ __forceinline__ void peer_finish(const PeerEpi& e) {
+  __syncthreads();  // the CTA's stores are issued
+  if (threadIdx.x != 0) return;
+  const unsigned ncta = gridDim.x * gridDim.y * gridDim.z;
+  unsigned t;
+  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(t) : "l"(e.ticket) : "memory");
+  if (t + 1 != ncta) return;
+  atomicExch(e.ticket, 0u);  // the next launch on this stream starts after this one ends
+  for (int r = 0; r < e.world; ++r)
+    if (r != e.rank)
+      asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(e.pflags[r] + e.rank) : "memory");
+  const unsigned expect = *e.seen + 1u;
+  unsigned long long t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (int r = 0; r < e.world; ++r) {
+    if (r == e.rank) continue;
+    for (;;) {
+      unsigned v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(e.pflags[e.rank] + r) : "memory");
+      if ((int)(v - expect) >= 0) break;
+      unsigned long long now;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+      if (now - t0 > kPeerWaitNs) {
+        atomicExch(e.err, 1);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  *e.seen = expect;
+}
+
 // Kernel families (each returns B200MM_OK, or a status if it declines / fails).
 // `*_supported` answers whether the family can serve the call, with no launch.
 bool gemv_supported(const DenseArgs& a);

@@ -32,66 +32,8 @@ struct GemvParams {
   const float* s0; const float* s1;
   void* y; int64_t ldy;
   int M, N, K;
-  // peer output (world > 0): column n of this rank's shard goes to column
-  // map(n) of every rank's gathered buffer instead of y
-  int world, rank, nparts;
-  int64_t ld_peer;
-  int64_t pw[3], pdoff[3];  // part widths; part j's rank-0 column in the gathered row
-  void* pdst[8];
-  unsigned* pflags[8];
-  unsigned* ticket;
-  unsigned* seen;
-  int* err;
+  PeerEpi pe;  // peer output (pe.world > 0): every rank's gathered buffer instead of y
 };
-
-constexpr unsigned long long kPeerWaitNs = 5ull * 1000 * 1000 * 1000;  // 5 s
-
-__device__ __forceinline__ int64_t peer_col(const GemvParams& p, int n) {
-  int64_t c = n;
-  int j = 0;
-  while (j + 1 < p.nparts && c >= p.pw[j]) c -= p.pw[j++];
-  return p.pdoff[j] + (int64_t)p.rank * p.pw[j] + c;
-}
-
-// The launch's output has been stored on every rank: each CTA takes a ticket
-// with a release (after a barrier, so it covers the CTA's stores); the
-// launch's last CTA, whose ticket acquires all of them, counts the launch done
-// on every peer with a system-scope release add (cumulative: it carries the
-// other CTAs' stores too; one remote add per peer, not one per CTA) and then
-// waits (bounded) until every peer's launch has counted itself done here.
-__device__ void peer_finish(const GemvParams& p) {
-  __syncthreads();  // the CTA's stores are issued
-  if (threadIdx.x != 0) return;
-  unsigned t;
-  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(t) : "l"(p.ticket) : "memory");
-  if (t + 1 != gridDim.x) return;
-  atomicExch(p.ticket, 0u);  // the next launch on this stream starts after this one ends
-  for (int r = 0; r < p.world; ++r)
-    if (r != p.rank)
-      asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(p.pflags[r] + p.rank) : "memory");
-  const unsigned expect = *p.seen + 1u;
-  const unsigned long long t0 = [] {
-    unsigned long long v;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(v));
-    return v;
-  }();
-  for (int r = 0; r < p.world; ++r) {
-    if (r == p.rank) continue;
-    for (;;) {
-      unsigned v;
-      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p.pflags[p.rank] + r) : "memory");
-      if ((int)(v - expect) >= 0) break;
-      unsigned long long now;
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
-      if (now - t0 > kPeerWaitNs) {
-        atomicExch(p.err, 1);
-        break;
-      }
-      __nanosleep(64);
-    }
-  }
-  *p.seen = expect;
-}
 
 // Two CTAs per SM for M <= 4 (at most 128 registers).  Three per SM with
 // fewer loads in flight made a lone QKV launch faster, but in the decode step
@@ -109,7 +51,7 @@ template <typename TX, typename TW, int MR, bool GATE, int NCH, bool GEN>
 __global__ void __launch_bounds__(kThreads, gemv_min_blocks<MR, GATE>())
 gemv_kernel(const GemvParams p, const int nsm, const int ks_arg) {
   const int ks = GEN ? ks_arg : 1;
-  const int world = GEN ? p.world : 0;
+  const int world = GEN ? p.pe.world : 0;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   TX* xs = reinterpret_cast<TX*>(smem_raw);  // [MR][K] activation rows
   __shared__ float red[kThreads / 32][2][MR];  // K-slice partial sums (ks > 1)
@@ -303,9 +245,7 @@ gemv_kernel(const GemvParams p, const int nsm, const int ks_arg) {
         if (world == 0) {
           y[n] = from_f<TX>(v);
         } else {
-          const int64_t d = (int64_t)lane * p.ld_peer + peer_col(p, n);
-          const TX o = from_f<TX>(v);
-          for (int r = 0; r < world; ++r) static_cast<TX*>(p.pdst[r])[d] = o;
+          peer_store(p.pe, lane, n, from_f<TX>(v));
         }
       };
       if (GATE) {
@@ -322,7 +262,7 @@ gemv_kernel(const GemvParams p, const int nsm, const int ks_arg) {
       }
     }
   }
-  if (world > 0) peer_finish(p);
+  if (world > 0) peer_finish(p.pe);
 }
 
 template <typename TX, typename TW, int MR, bool GATE>
@@ -375,26 +315,7 @@ int launch_one(const DenseArgs& a) {
   if (grid > need) grid = need;
   if (grid < 1) grid = 1;
   GemvParams p{a.x, a.ldx, a.w0, a.ldw0, a.w1, a.ldw1, a.s0, a.s1, a.y, a.ldy, a.M, a.N, a.K};
-  if (a.peer) {
-    const b200mm_peer_out& po = *a.peer;
-    p.world = po.world;
-    p.rank = po.rank;
-    p.nparts = po.nparts;
-    p.ld_peer = po.ld_dst;
-    int64_t off = 0;
-    for (int j = 0; j < po.nparts; ++j) {
-      p.pw[j] = po.part_widths[j];
-      p.pdoff[j] = off;
-      off += po.part_widths[j] * po.world;
-    }
-    for (int r = 0; r < po.world; ++r) {
-      p.pdst[r] = po.dst[r];
-      p.pflags[r] = static_cast<unsigned*>(po.flags[r]);
-    }
-    p.ticket = static_cast<unsigned*>(po.ticket);
-    p.seen = static_cast<unsigned*>(po.seen);
-    p.err = static_cast<int*>(po.err);
-  }
+  if (a.peer) peer_epi_from(*a.peer, p.pe);
   // plain projections: warps take units in SM-round-robin order (below)
   cudaError_t e = launch_pdl(kerns[gen], dim3(grid), dim3(kThreads), smem, a.stream, p, GATE ? 0 : num_sms(dev), ks);
   return e == cudaSuccess ? B200MM_OK : B200MM_ERR_LAUNCH;

@@ -45,6 +45,7 @@ struct MmvParams {
   void* y; int64_t ldy;
   int M, N, K;
   int kslice;  // K columns per cluster rank (multiple of 64)
+  PeerEpi pe;  // peer output (pe.world > 0): every rank's gathered buffer instead of y
 };
 
 template <typename T> struct MmaOp;
@@ -248,9 +249,13 @@ __global__ void __launch_bounds__(kThreads) mmv_kernel(const MmvParams p) {
         out = v[0];
         if (p.s0) out *= p.s0[n];
       }
-      y[(int64_t)m * p.ldy + n] = from_f<TX>(out);
+      if (p.pe.world == 0)
+        y[(int64_t)m * p.ldy + n] = from_f<TX>(out);
+      else
+        peer_store(p.pe, m, n, from_f<TX>(out));
     }
   }
+  if (p.pe.world > 0) peer_finish(p.pe);
 }
 
 size_t smem_bytes(int MT, bool gate, bool w8, int kslice) {
@@ -272,6 +277,7 @@ int launch_mmv(const DenseArgs& a, int kslice) {
     configured[dev] = (int)smem;
   }
   MmvParams p{a.x, a.ldx, a.w0, a.ldw0, a.w1, a.ldw1, a.s0, a.s1, a.y, a.ldy, a.M, a.N, a.K, kslice};
+  if (a.peer) peer_epi_from(*a.peer, p.pe);
   const int groups = (a.N + kRows - 1) / kRows;
   return launch_pdl_cluster(kern, dim3(groups * CS), dim3(kThreads), smem, a.stream, CS, p) == cudaSuccess
              ? B200MM_OK

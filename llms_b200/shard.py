@@ -92,14 +92,14 @@ def gather_qkv(y: torch.Tensor, cq: int, ck: int, world: int, group=None, site=N
 def _fused_peer(site, x: torch.Tensor, n_out: int, parts, int8: bool, call):
     """Run the projection with its all-gather fused in (the ``b200mm_*_peer``
     entry points: the kernel stores into every rank's gathered buffer) when
-    the call is in the fused regime -- one token row for int8 weights, up to
-    four for 16-bit, at most the site's rows; returns the gathered tensor, or
+    the call is in the fused regime -- up to 32 token rows for int8 weights,
+    8 for 16-bit, at most the site's rows; returns the gathered tensor, or
     None for the caller's unfused path."""
     if site is None or site.ctx.world == 1 or not site.ctx.fused:
         return None
     K = x.shape[-1]
     rows = x.numel() // K if K else 0
-    if (rows < 1 or rows > (1 if int8 else 4) or rows > site.max_rows or not x.is_cuda or x.dtype != site.dtype
+    if (rows < 1 or rows > (32 if int8 else 8) or rows > site.max_rows or not x.is_cuda or x.dtype != site.dtype
             or n_out * site.ctx.world != site.width):
         return None
     x2 = x.reshape(-1, K)

@@ -1,7 +1,7 @@
 """b200mm_peer_gather on two GPUs: the peer-memory all-gather of the
 column-sharded decode step against NCCL's all-gather on the same blocks, and
-the sharded Qwen3-8B-shaped step with peer gathers -- at batch 1 fused into
-the projection kernels (b200mm_*_peer), at batch 4 partly -- against the same
+the sharded Qwen3-8B-shaped step with peer gathers -- at batch 1 and 4 fused
+into the projection kernels (b200mm_*_peer), at batch 16 partly -- against the same
 step with NCCL gathers (the arithmetic is the same, so the logits must be
 identical).
 One process per GPU; skipped with fewer than two GPUs."""
@@ -80,7 +80,7 @@ def _worker(rank, world, port, out):
             apply_decode_attn(model)
             peer = PeerGather(peer_bytes(model, 16)) if mode == "peer" else None
             shard_decode_model(model, rank, world, peer=peer, max_rows=16)
-            for B in (1, 4):  # B = 1: every projection fused with its gather; B = 4: int8 + b200mm_peer_gather
+            for B in (1, 4, 16):  # 1, 4: every projection fused with its gather; 16: int8 fused, bf16 + b200mm_peer_gather
                 g = torch.Generator(device="cuda").manual_seed(5)
                 ids = torch.randint(0, shape.vocab_size, (B, 8), device="cuda", generator=g)
                 nxt = torch.randint(0, shape.vocab_size, (B, 1), device="cuda", generator=g)
@@ -92,7 +92,7 @@ def _worker(rank, world, port, out):
             if peer is not None:
                 res["model_status"] = peer.status()
             del model, peer
-        for B in (1, 4):
+        for B in (1, 4, 16):
             for step in range(2):
                 res[f"model_equal_b{B}_{step}"] = bool(torch.equal(logits[("nccl", B, step)],
                                                                    logits[("peer", B, step)]))
