@@ -32,8 +32,13 @@ struct GemvParams {
   const float* s0; const float* s1;
   void* y; int64_t ldy;
   int M, N, K;
-  PeerEpi pe;  // peer output (pe.world > 0): every rank's gathered buffer instead of y
 };
+
+// The peer-output block is a kernel parameter of the general form only: in
+// the plain form it is an empty struct, so the plain launches carry the
+// original ~100-byte parameter block.
+template <bool GEN> struct PeerArg { int world; };  // plain: never peer output (world = 0)
+template <> struct PeerArg<true> : PeerEpi {};
 
 // Two CTAs per SM for M <= 4 (at most 128 registers).  Three per SM with
 // fewer loads in flight made a lone QKV launch faster, but in the decode step
@@ -49,9 +54,9 @@ constexpr int gemv_min_blocks() {
 // whole-shape QKV launch ~5 % (7.0 -> 7.4 us).
 template <typename TX, typename TW, int MR, bool GATE, int NCH, bool GEN>
 __global__ void __launch_bounds__(kThreads, gemv_min_blocks<MR, GATE>())
-gemv_kernel(const GemvParams p, const int nsm, const int ks_arg) {
+gemv_kernel(const GemvParams p, const int nsm, const int ks_arg, const PeerArg<GEN> pe) {
   const int ks = GEN ? ks_arg : 1;
-  const int world = GEN ? p.pe.world : 0;
+  const int world = GEN ? pe.world : 0;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   TX* xs = reinterpret_cast<TX*>(smem_raw);  // [MR][K] activation rows
   __shared__ float red[kThreads / 32][2][MR];  // K-slice partial sums (ks > 1)
@@ -245,7 +250,7 @@ gemv_kernel(const GemvParams p, const int nsm, const int ks_arg) {
         if (world == 0) {
           y[n] = from_f<TX>(v);
         } else {
-          peer_store(p.pe, lane, n, from_f<TX>(v));
+          if constexpr (GEN) peer_store(pe, lane, n, from_f<TX>(v));
         }
       };
       if (GATE) {
@@ -262,14 +267,16 @@ gemv_kernel(const GemvParams p, const int nsm, const int ks_arg) {
       }
     }
   }
-  if (world > 0) peer_finish(p.pe);
+  if constexpr (GEN) {
+    if (world > 0) peer_finish(pe);
+  }
 }
 
 template <typename TX, typename TW, int MR, bool GATE>
 int launch_one(const DenseArgs& a) {
   constexpr int NCH = (sizeof(TW) == 2) ? 10 : 8;
-  void (*const kerns[2])(const GemvParams, const int, const int) = {gemv_kernel<TX, TW, MR, GATE, NCH, false>,
-                                                                   gemv_kernel<TX, TW, MR, GATE, NCH, true>};
+  auto kplain = gemv_kernel<TX, TW, MR, GATE, NCH, false>;
+  auto kgen = gemv_kernel<TX, TW, MR, GATE, NCH, true>;
   const size_t smem = (size_t)MR * a.K * sizeof(TX);
   static int configured_smem[2][64] = {{0}};  // per form and device: largest opt-in set so far
   static int blocks_per_sm[2][64][8] = {{{0}}};
@@ -277,20 +284,20 @@ int launch_one(const DenseArgs& a) {
   if (dev < 0 || dev >= 64) return B200MM_ERR_DEVICE;
   // occupancy depends on smem; cache per (form, device, smem bucket of 32 KB)
   const int bucket = (int)(smem >> 15) < 8 ? (int)(smem >> 15) : 7;
-  auto prepare = [&](int g) -> int {
+  auto prepare = [&](int g, auto kern) -> int {
     if (smem > 48 * 1024 && (int)smem > configured_smem[g][dev]) {
-      if (cudaFuncSetAttribute(kerns[g], cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return -1;
       configured_smem[g][dev] = (int)smem;
     }
     int& b = blocks_per_sm[g][dev][bucket];
     if (b == 0) {
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kerns[g], kThreads, smem) != cudaSuccess || b < 1)
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kern, kThreads, smem) != cudaSuccess || b < 1)
         b = 1;
     }
     return b;
   };
-  int bps = prepare(0);
+  int bps = prepare(0, kplain);
   if (bps < 0) return B200MM_ERR_LAUNCH;
   const int nunits = a.gate ? a.N : (a.N + 1) / 2;
   const int warps_per_cta = kThreads / 32;
@@ -306,7 +313,7 @@ int launch_one(const DenseArgs& a) {
   while (ks < 8 && (int64_t)nunits * 2 * ks <= slots && a.K / WV / (2 * ks) >= 32) ks *= 2;
   const int gen = ks > 1 || a.peer ? 1 : 0;
   if (gen) {
-    bps = prepare(1);
+    bps = prepare(1, kgen);
     if (bps < 0) return B200MM_ERR_LAUNCH;
   }
   const int upc = warps_per_cta / ks;
@@ -315,9 +322,12 @@ int launch_one(const DenseArgs& a) {
   if (grid > need) grid = need;
   if (grid < 1) grid = 1;
   GemvParams p{a.x, a.ldx, a.w0, a.ldw0, a.w1, a.ldw1, a.s0, a.s1, a.y, a.ldy, a.M, a.N, a.K};
-  if (a.peer) peer_epi_from(*a.peer, p.pe);
+  PeerArg<true> pe{};
+  if (a.peer) peer_epi_from(*a.peer, pe);
   // plain projections: warps take units in SM-round-robin order (below)
-  cudaError_t e = launch_pdl(kerns[gen], dim3(grid), dim3(kThreads), smem, a.stream, p, GATE ? 0 : num_sms(dev), ks);
+  const int order = GATE ? 0 : num_sms(dev);
+  cudaError_t e = gen ? launch_pdl(kgen, dim3(grid), dim3(kThreads), smem, a.stream, p, order, ks, pe)
+                      : launch_pdl(kplain, dim3(grid), dim3(kThreads), smem, a.stream, p, order, ks, PeerArg<false>{0});
   return e == cudaSuccess ? B200MM_OK : B200MM_ERR_LAUNCH;
 }
 

@@ -45,8 +45,13 @@ struct MmvParams {
   void* y; int64_t ldy;
   int M, N, K;
   int kslice;  // K columns per cluster rank (multiple of 64)
-  PeerEpi pe;  // peer output (pe.world > 0): every rank's gathered buffer instead of y
 };
+
+// The peer-output block is a kernel parameter of the peer form only (an
+// empty struct otherwise): the larger parameter block slowed the plain
+// launches (8B int8 QKV at M = 4: 9.8 -> 11.0 us).
+template <bool PEER> struct MmvPeer { int world; };
+template <> struct MmvPeer<true> : PeerEpi {};
 
 template <typename T> struct MmaOp;
 template <> struct MmaOp<__nv_bfloat16> {
@@ -72,8 +77,8 @@ template <> struct MmaOp<__half> {
 
 // TX: activation dtype in memory; TM: MMA input dtype (== TX, or fp16 for int8
 // weights); TW: weight dtype; MT: n-tiles of 8 activation rows.
-template <typename TX, typename TM, typename TW, int MT, bool GATE, int CS>
-__global__ void __launch_bounds__(kThreads) mmv_kernel(const MmvParams p) {
+template <typename TX, typename TM, typename TW, int MT, bool GATE, int CS, bool PEER>
+__global__ void __launch_bounds__(kThreads) mmv_kernel(const MmvParams p, const MmvPeer<PEER> pe) {
   constexpr bool W8 = sizeof(TW) == 1;
   constexpr int KC = W8 ? 64 : 32;       // K columns per warp-chunk (4 lanes x 16 bytes)
   constexpr int NM = GATE ? 2 : 1;
@@ -249,13 +254,13 @@ __global__ void __launch_bounds__(kThreads) mmv_kernel(const MmvParams p) {
         out = v[0];
         if (p.s0) out *= p.s0[n];
       }
-      if (p.pe.world == 0)
-        y[(int64_t)m * p.ldy + n] = from_f<TX>(out);
+      if constexpr (PEER)
+        peer_store(pe, m, n, from_f<TX>(out));
       else
-        peer_store(p.pe, m, n, from_f<TX>(out));
+        y[(int64_t)m * p.ldy + n] = from_f<TX>(out);
     }
   }
-  if (p.pe.world > 0) peer_finish(p.pe);
+  if constexpr (PEER) peer_finish(pe);
 }
 
 size_t smem_bytes(int MT, bool gate, bool w8, int kslice) {
@@ -265,23 +270,34 @@ size_t smem_bytes(int MT, bool gate, bool w8, int kslice) {
 
 template <typename TX, typename TM, typename TW, int MT, bool GATE, int CS>
 int launch_mmv(const DenseArgs& a, int kslice) {
-  auto kern = mmv_kernel<TX, TM, TW, MT, GATE, CS>;
+  auto kern = mmv_kernel<TX, TM, TW, MT, GATE, CS, false>;
+  auto kpeer = mmv_kernel<TX, TM, TW, MT, GATE, CS, true>;
   const size_t smem = smem_bytes(MT, GATE, sizeof(TW) == 1, kslice);
   if (smem > 220 * 1024) return B200MM_ERR_SHAPE;
-  static int configured[64] = {0};
+  static int configured[2][64] = {{0}};
   const int dev = current_device();
   if (dev < 0 || dev >= 64) return B200MM_ERR_DEVICE;
-  if ((int)smem > configured[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return B200MM_ERR_LAUNCH;
-    configured[dev] = (int)smem;
-  }
+  auto prepare = [&](int g, auto k) -> bool {
+    if ((int)smem > configured[g][dev]) {
+      if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return false;
+      configured[g][dev] = (int)smem;
+    }
+    return true;
+  };
   MmvParams p{a.x, a.ldx, a.w0, a.ldw0, a.w1, a.ldw1, a.s0, a.s1, a.y, a.ldy, a.M, a.N, a.K, kslice};
-  if (a.peer) peer_epi_from(*a.peer, p.pe);
   const int groups = (a.N + kRows - 1) / kRows;
-  return launch_pdl_cluster(kern, dim3(groups * CS), dim3(kThreads), smem, a.stream, CS, p) == cudaSuccess
-             ? B200MM_OK
-             : B200MM_ERR_LAUNCH;
+  cudaError_t e;
+  if (a.peer) {
+    if (!prepare(1, kpeer)) return B200MM_ERR_LAUNCH;
+    MmvPeer<true> pe{};
+    peer_epi_from(*a.peer, pe);
+    e = launch_pdl_cluster(kpeer, dim3(groups * CS), dim3(kThreads), smem, a.stream, CS, p, pe);
+  } else {
+    if (!prepare(0, kern)) return B200MM_ERR_LAUNCH;
+    e = launch_pdl_cluster(kern, dim3(groups * CS), dim3(kThreads), smem, a.stream, CS, p, MmvPeer<false>{0});
+  }
+  return e == cudaSuccess ? B200MM_OK : B200MM_ERR_LAUNCH;
 }
 
 template <typename TX, typename TM, typename TW, bool GATE, int CS>
