@@ -75,3 +75,38 @@ def test_sharded_projections_gather_to_full_gloo(world):
     assert sorted(res) == list(range(world))
     for r, ok in res.items():
         assert all(ok), (r, ok)
+
+
+def test_peer_sites_fit_peer_bytes():
+    """shard_decode_model with a peer context reserves one region per call
+    site (QKV, o, gate-up, down per layer, then the LM head), each as wide as
+    the gathered output, and peer_bytes covers them all (CPU: a recording
+    stand-in for the symmetric buffer)."""
+    import dataclasses
+
+    from llms_b200.qwen3 import QWEN3_8B, synthetic_int8_model
+    from llms_b200.shard import peer_bytes, shard_decode_model
+
+    shape = dataclasses.replace(QWEN3_8B, hidden_size=256, num_attention_heads=4, num_key_value_heads=2,
+                                head_dim=64, intermediate_size=512, vocab_size=1024, num_hidden_layers=2)
+    model = synthetic_int8_model(shape, device="cpu")
+    need = peer_bytes(model, 8)
+
+    class Ctx:
+        world = 2
+
+        def __init__(self):
+            self.sites = []
+
+        def site(self, rows, width, dtype):
+            self.sites.append((rows, width, dtype))
+            return ("site", len(self.sites))
+
+    ctx = Ctx()
+    shard_decode_model(model, 0, 2, peer=ctx, max_rows=8)
+    widths = [w for _, w, _ in ctx.sites]
+    qkv = 4 * 64 + 2 * 2 * 64
+    assert widths == [qkv, 256, 512, 256] * 2 + [1024]
+    assert all(r == 8 and d == torch.bfloat16 for r, _, d in ctx.sites)
+    assert sum((8 * w * 2 + 255) // 256 * 256 for w in widths) <= need
+    assert model.lm_head.weight.shape == (512, 256)  # vocabulary rows of rank 0
